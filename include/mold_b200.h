@@ -1,0 +1,202 @@
+/*
+ * mold_b200.h — C ABI of the B200 (sm_100a) quantized-DiT denoising hot path.
+ *
+ * This is the drop-in boundary for mold's GGUF-quantized FLUX / Qwen-Image
+ * transformer. Every entry point below names the reference interface it stands
+ * in for (paths are inside utensils/mold; third-party candle items carry the
+ * crate version pinned in the reference's Cargo.lock).
+ *
+ * Conventions
+ *  - All functions return an mb_status (0 = MB_OK). On failure a message for the
+ *    calling thread is available from mb_last_error(). No C++ exception crosses
+ *    this boundary. (Reference: candle_core::Result / anyhow::Result with bail!
+ *    on shape errors, e.g. qwen_image/quantized_transformer.rs:223-225.)
+ *  - Activations are caller-owned device buffers (plain pointers + sizes); the
+ *    library never frees them. Weights are copied into library-owned device
+ *    memory by mb_weight_create and freed by mb_weight_destroy.
+ *  - Every compute call takes an explicit cudaStream_t (passed as void*; NULL =
+ *    the legacy default stream) and is asynchronous with respect to the host.
+ *  - One thread per device, as in mold's per-GPU worker threads
+ *    (crates/mold-server/src/gpu_worker.rs:18-39); calls for different devices
+ *    may run concurrently from different threads.
+ *  - GGML type ids are GGUF's: F32=0, F16=1, Q8_0=8, Q4_K=12, BF16=30.
+ *  - Element types of activations: MB_DT_F32 or MB_DT_BF16.
+ */
+#ifndef MOLD_B200_H
+#define MOLD_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define MB_API __attribute__((visibility("default")))
+#else
+#define MB_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+  MB_OK = 0,
+  MB_ERR_INVALID = 1,     /* bad argument, shape or alignment */
+  MB_ERR_UNSUPPORTED = 2, /* ggml type / feature not supported */
+  MB_ERR_CUDA = 3,        /* a CUDA runtime/driver call failed */
+  MB_ERR_TIMEOUT = 4,     /* a kernel gave up on a bounded wait (see mb_device_status) */
+  MB_ERR_NOMEM = 5,       /* device allocation failed */
+  MB_ERR_NOT_READY = 6    /* model missing tensors / not initialised */
+} mb_status;
+
+enum { MB_GGML_F32 = 0, MB_GGML_F16 = 1, MB_GGML_Q8_0 = 8, MB_GGML_Q4_K = 12, MB_GGML_BF16 = 30 };
+enum { MB_DT_F32 = 0, MB_DT_BF16 = 1 };
+
+/* Epilogues fused into the quantized linear. */
+enum {
+  MB_EPI_NONE = 0,          /* y = x W^T + b                                         */
+  MB_EPI_GELU_TANH = 1,     /* y = gelu_tanh(x W^T + b) for columns >= gelu_from      */
+  MB_EPI_GATE_RESIDUAL = 2  /* y = residual + gate[n] * (x W^T + b)  (f32 out; y may alias residual) */
+};
+
+typedef struct mb_weight mb_weight;
+typedef struct mb_flux mb_flux;
+
+/* ------------------------------------------------------------------ runtime */
+
+/* Message for the last failing call on this thread ("" if none). */
+MB_API const char* mb_last_error(void);
+
+/* ABI version (major*10000 + minor*100 + patch). */
+MB_API int mb_version(void);
+
+/* Select and initialise a device for the calling thread (driver entry points,
+ * SM count). Replaces candle's `Device::new_cuda(ordinal)` as called from
+ * crates/mold-inference/src/device.rs:147-180. */
+MB_API mb_status mb_init(int device);
+
+/* Read and clear the device status word that kernels raise when a bounded wait
+ * expires (0 = no event). */
+MB_API mb_status mb_device_status(int* status_out);
+
+/* ------------------------------------------------------------------ weights */
+
+/* Upload one GGUF tensor [n_rows, n_cols] (rows = output features, ggml blocks
+ * run along n_cols) in its raw GGML block layout. `data` is host memory unless
+ * data_on_device != 0. Replaces `QMatMul::from_weights(Arc<QTensor>)`
+ * (candle-core-mold 0.9.10; pattern at crates/mold-inference/src/encoders/qwen3_gguf.rs:273-305)
+ * and the per-tensor part of `quantized_var_builder::VarBuilder::from_gguf`
+ * (flux/pipeline.rs:976). */
+MB_API mb_status mb_weight_create(int ggml_type, int64_t n_rows, int64_t n_cols, const void* data, size_t nbytes,
+                           int data_on_device, mb_weight** out);
+MB_API mb_status mb_weight_destroy(mb_weight* w);
+/* Raw device pointer of the weight bytes and their GGML type. */
+MB_API mb_status mb_weight_info(const mb_weight* w, int* ggml_type, int64_t* n_rows, int64_t* n_cols, const void** dev_ptr);
+
+/* ------------------------------------------------------------------ kernels */
+
+/* K1. Dequantize a whole weight to f32 or bf16 [n_rows, n_cols] (bit-exact GGML
+ * decode; bf16 = round-to-nearest-even of that f32). Replaces
+ * `QTensor::dequantize` (qwen_image/quantized_transformer.rs:60-67). */
+MB_API mb_status mb_dequant(const mb_weight* w, void* out, int out_dtype, void* stream);
+
+/* K2. Quantized linear y[M,N] = epilogue(x[M,K] W^T + bias). x is bf16 (row
+ * stride ldx elements) or f32 (converted to bf16 on the way in). y is bf16 or
+ * f32 with row stride ldy. bias: f32 [N] or NULL. For MB_EPI_GATE_RESIDUAL y
+ * must be f32, gate is f32 [N] and residual f32 [M, ldr] (may equal y).
+ * Replaces `QMatMul::forward` (candle, called through quantized_nn::Linear inside
+ * flux::quantized_model; flux/transformer.rs:64-72) and `QwenLinear::forward`
+ * (qwen_image/quantized_transformer.rs:54-77). */
+MB_API mb_status mb_qlinear(const mb_weight* w, const void* x, int x_dtype, int64_t M, int64_t ldx, void* y, int y_dtype,
+                     int64_t ldy, const float* bias, int epilogue, int64_t gelu_from, const float* gate,
+                     const float* residual, int64_t ldr, void* stream);
+
+/* K3. Quantized GEMV for the modulation vectors: y[N] = W silu?(x)[K] + bias.
+ * Replaces Modulation1/2::forward's silu(vec)->Linear (flux/offload.rs:117-156). */
+MB_API mb_status mb_qgemv(const mb_weight* w, const float* x, int apply_silu, const float* bias, float* y, void* stream);
+
+/* K5. LayerNorm (no affine, eps 1e-6) + AdaLN modulate: y = LN(x) * (1 + scale) + shift.
+ * x f32 [M, C] (row stride ldx), y bf16 [M, C] (row stride ldy); shift, scale f32 [C].
+ * Replaces LayerNorm + broadcast_mul/add (flux/offload.rs:286-295,379-382,424-427). */
+MB_API mb_status mb_ln_modulate(const float* x, int64_t M, int64_t C, int64_t ldx, const float* shift, const float* scale,
+                         void* y, int64_t ldy, void* stream);
+
+/* RoPE table pe f32 [L, D/2, 2, 2] from position ids f32 [L, n_axes] (EmbedNd:
+ * flux2/transformer.rs:99-118,170-184; FLUX.1 axes (16,56,56), theta 10000). */
+MB_API mb_status mb_rope_table(const float* ids, int64_t L, int n_axes, const int* axes_dim, int theta, float* pe,
+                        void* stream);
+
+/* K6. Split a fused qkv row block, RMSNorm q and k (learned scale [D], eps 1e-6),
+ * apply RoPE (pe rows row_offset.. row_offset+M) and write q, k, v in attention
+ * layout bf16 [H, L_total, D] at rows row_offset..row_offset+M.
+ * qkv: bf16 [M, 3*H*D] with row stride ld_qkv. D must be 128.
+ * Replaces SelfAttention::qkv + apply_rope (flux/offload.rs:56-72,191-201). */
+MB_API mb_status mb_qk_norm_rope(const void* qkv, int64_t M, int64_t ld_qkv, int H, const float* q_scale,
+                          const float* k_scale, const float* pe, int64_t row_offset, int64_t L_total, void* q, void* k,
+                          void* v, void* stream);
+
+/* K4. Attention softmax(q k^T / sqrt(D)) v, non-causal, D = 128.
+ * q: bf16 [H, Lq, D]; k, v: bf16 [H, Lk, D]; out: bf16 [Lq, ldo] with head h in
+ * columns h*D..h*D+D (the (B,H,L,D)->(B,L,H*D) transpose of the reference is
+ * fused). n_valid_keys < Lk masks keys >= n_valid_keys (key padding, Qwen).
+ * Replaces scaled_dot_product_attention (flux/offload.rs:40-54) and Qwen's
+ * masked attention (qwen_image/quantized_transformer.rs:799-816). */
+MB_API mb_status mb_attention(const void* q, const void* k, const void* v, int H, int64_t Lq, int64_t Lk,
+                       int64_t n_valid_keys, void* out, int64_t ldo, void* stream);
+
+/* K9. Euler step of the flow-matching loop: img += pred * (t_prev - t_curr), f32 [n].
+ * Replaces flux/transformer.rs:84 and qwen_image/sampling.rs:117-129. */
+MB_API mb_status mb_euler_step(float* img, const float* pred, int64_t n, float dt, void* stream);
+
+/* ------------------------------------------------------------------ FLUX model */
+
+/* FLUX.1 configuration (candle flux::model::Config as used by mold). */
+typedef struct {
+  int in_channels;        /* 64 */
+  int vec_in_dim;         /* 768 */
+  int context_in_dim;     /* 4096 */
+  int hidden_size;        /* 3072 */
+  int mlp_hidden;         /* 12288 */
+  int num_heads;          /* 24 (head_dim must be 128) */
+  int depth;              /* 19 double-stream blocks */
+  int depth_single;       /* 38 single-stream blocks */
+  int axes_dim[3];        /* 16, 56, 56 */
+  int theta;              /* 10000 */
+  int guidance_embed;     /* 1 for dev */
+} mb_flux_config;
+
+/* Create a FLUX transformer on the current device for sequences up to
+ * max_txt + max_img tokens. Replaces the `FluxTransformer::Quantized` arm
+ * (flux/transformer.rs:17-23) built at flux/pipeline.rs:976-977. */
+MB_API mb_status mb_flux_create(const mb_flux_config* cfg, int64_t max_txt, int64_t max_img, mb_flux** out);
+MB_API mb_status mb_flux_destroy(mb_flux* m);
+
+/* Hand one GGUF tensor to the model by its GGUF name (e.g.
+ * "double_blocks.0.img_attn.qkv.weight"); 1-D tensors (biases, norm scales)
+ * have n_rows = 1. Names as read by flux/pipeline.rs:255-276. */
+MB_API mb_status mb_flux_set_tensor(mb_flux* m, const char* name, int ggml_type, int64_t n_rows, int64_t n_cols,
+                             const void* data, size_t nbytes, int data_on_device);
+
+/* Names of tensors the model still lacks (newline separated) — 0 bytes when complete. */
+MB_API mb_status mb_flux_missing(const mb_flux* m, char* buf, size_t buflen);
+
+/* One transformer forward (batch 1). Device pointers:
+ *   img f32 [L_img, in_channels], img_ids f32 [L_img, 3], txt f32 [L_txt, context_in_dim],
+ *   txt_ids f32 [L_txt, 3], y f32 [vec_in_dim]; pred f32 [L_img, in_channels].
+ * Replaces `flux::quantized_model::Flux::forward` (WithForward; called at
+ * flux/transformer.rs:64-72; math of flux/offload.rs:525-580). */
+MB_API mb_status mb_flux_forward(mb_flux* m, const float* img, const float* img_ids, int64_t L_img, const float* txt,
+                          const float* txt_ids, int64_t L_txt, float t, const float* y, float guidance, float* pred,
+                          void* stream);
+
+/* The whole denoising loop in place on img (f32 [L_img, in_channels], device):
+ * for each (t_curr, t_prev) in timesteps: img += forward(img, t_curr) * (t_prev - t_curr).
+ * One CUDA graph per step shape is captured on first use and replayed.
+ * Replaces `FluxTransformer::denoise` (flux/transformer.rs:30-98; no inpaint context). */
+MB_API mb_status mb_flux_denoise(mb_flux* m, float* img, const float* img_ids, int64_t L_img, const float* txt,
+                          const float* txt_ids, int64_t L_txt, const float* y, const double* timesteps,
+                          int n_timesteps, float guidance, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* MOLD_B200_H */

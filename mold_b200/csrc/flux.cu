@@ -1,0 +1,585 @@
+// FLUX.1 quantized transformer: weights by GGUF name, device workspace, the
+// forward pass as a sequence of this library's kernels, and the denoising loop
+// replayed from one captured CUDA graph per step shape.
+//
+// Math order follows mold's in-repo restatement of candle's FLUX model:
+//   forward            flux/offload.rs:525-580
+//   DoubleBlock        flux/offload.rs:275-323
+//   SingleBlock        flux/offload.rs:377-396
+//   FinalLayer         flux/offload.rs:421-429
+//   denoise loop       flux/transformer.rs:50-95 (img += pred * (t_prev - t_curr))
+//
+// HBM layout of the activations (L = L_txt + L_img, h = hidden, m = mlp hidden):
+//   x   f32  [L, h]         residual stream; txt rows 0..L_txt-1, then img rows, so the
+//                           single-stream input cat[txt, img] is x itself (no concat copy)
+//   xm  bf16 [L, h]         LayerNorm+modulate output = A operand of the next linear
+//   Y   bf16 [L, 3h + m]    cols [0,3h): fused qkv / linear1 qkv part; the attention output
+//                           is written over the consumed v columns [2h,3h); cols [3h, 3h+m):
+//                           GELU(mlp) -> so [2h, 3h+m) is exactly cat[attn, gelu(mlp)], the
+//                           input of single-block linear2 (and [3h, 3h+m) of double-block mlp.2)
+//   q,k,v bf16 [H, L, 128]  attention layout written by the fused QK-norm/RoPE kernel
+//   pe  f32  [L, 64, 2, 2]  RoPE table (computed once per denoise call)
+#include <map>
+#include <string>
+#include <vector>
+
+#include "common.cuh"
+#include "internal.h"
+
+namespace mb {
+cudaError_t launch_gemv_single(const mb_weight* w, const float* x, int apply_silu, const float* bias, float* y,
+                               cudaStream_t st);
+}
+
+using namespace mb;
+
+namespace {
+
+struct Vec1 {
+  float* dev = nullptr;
+  int64_t n = 0;
+};
+
+__global__ void k_set_scalars(float* dst, float a, float b) {
+  dst[0] = a;
+  dst[1] = b;
+}
+
+// t_cur = sched[i], dt = sched[i+1] - sched[i] (f64), then ++i. Runs at the start of each
+// replayed step so one captured graph serves every step of the schedule.
+__global__ void k_step_prologue(const double* sched, int* counter, float* scal) {
+  const int i = *counter;
+  scal[0] = (float)sched[i];
+  scal[2] = (float)(sched[i + 1] - sched[i]);
+  *counter = i + 1;
+}
+
+struct Seg {  // a row range of the joint sequence
+  int64_t row0, rows;
+};
+
+}  // namespace
+
+struct mb_flux {
+  mb_flux_config cfg;
+  int device = 0;
+  int64_t max_txt = 0, max_img = 0;
+  std::map<std::string, mb_weight*> mats;
+  std::map<std::string, Vec1> vecs;
+  bool finalized = false;
+
+  // workspace
+  float* x = nullptr;
+  __nv_bfloat16* xm = nullptr;
+  __nv_bfloat16* Y = nullptr;
+  __nv_bfloat16 *q = nullptr, *k = nullptr, *v = nullptr;
+  float* pe = nullptr;
+  float* ids = nullptr;
+  __nv_bfloat16* txt_bf = nullptr;
+  __nv_bfloat16* img_bf = nullptr;
+  float* pred = nullptr;
+  float* scal = nullptr;   // [0] t, [1] guidance, [2] dt
+  int* counter = nullptr;
+  double* sched = nullptr;
+  int sched_cap = 0;
+  float* temb = nullptr;   // [2][256]
+  float* hid = nullptr;    // [3][h]
+  float* parts = nullptr;  // [3][h]
+  float* mods = nullptr;   // all modulation vectors
+  std::vector<int64_t> mod_off_double, mod_off_single;
+  int64_t mod_off_final = 0, mod_total = 0;
+  GemvJob* jobs_dev = nullptr;
+  int* blocks_dev = nullptr;
+  int n_jobs[3] = {0, 0, 0}, n_blocks[3] = {0, 0, 0}, job0[3] = {0, 0, 0}, block0[3] = {0, 0, 0};
+
+  // graph cache
+  cudaGraphExec_t graph = nullptr;
+  int64_t graph_lt = -1, graph_li = -1;
+  const void* graph_key[6] = {nullptr, nullptr, nullptr, nullptr, nullptr, nullptr};
+
+  int64_t H() const { return cfg.num_heads; }
+  int64_t h() const { return cfg.hidden_size; }
+  int64_t mh() const { return cfg.mlp_hidden; }
+  int64_t ldY() const { return 3 * h() + mh(); }
+};
+
+namespace {
+
+std::vector<std::pair<std::string, std::vector<int64_t>>> expected_tensors(const mb_flux_config& c) {
+  std::vector<std::pair<std::string, std::vector<int64_t>>> out;
+  const int64_t h = c.hidden_size, m = c.mlp_hidden, hd = h / c.num_heads;
+  auto lin = [&](const std::string& n, int64_t o, int64_t i) {
+    out.push_back({n + ".weight", {o, i}});
+    out.push_back({n + ".bias", {o}});
+  };
+  lin("img_in", h, c.in_channels);
+  lin("txt_in", h, c.context_in_dim);
+  lin("time_in.in_layer", h, 256);
+  lin("time_in.out_layer", h, h);
+  lin("vector_in.in_layer", h, c.vec_in_dim);
+  lin("vector_in.out_layer", h, h);
+  if (c.guidance_embed) {
+    lin("guidance_in.in_layer", h, 256);
+    lin("guidance_in.out_layer", h, h);
+  }
+  for (int i = 0; i < c.depth; i++) {
+    const std::string p = "double_blocks." + std::to_string(i) + ".";
+    for (const char* s : {"img", "txt"}) {
+      const std::string S(s);
+      lin(p + S + "_mod.lin", 6 * h, h);
+      lin(p + S + "_attn.qkv", 3 * h, h);
+      out.push_back({p + S + "_attn.norm.query_norm.scale", {hd}});
+      out.push_back({p + S + "_attn.norm.key_norm.scale", {hd}});
+      lin(p + S + "_attn.proj", h, h);
+      lin(p + S + "_mlp.0", m, h);
+      lin(p + S + "_mlp.2", h, m);
+    }
+  }
+  for (int i = 0; i < c.depth_single; i++) {
+    const std::string p = "single_blocks." + std::to_string(i) + ".";
+    lin(p + "linear1", 3 * h + m, h);
+    lin(p + "linear2", h, h + m);
+    out.push_back({p + "norm.query_norm.scale", {hd}});
+    out.push_back({p + "norm.key_norm.scale", {hd}});
+    lin(p + "modulation.lin", 3 * h, h);
+  }
+  lin("final_layer.linear", c.in_channels, h);
+  lin("final_layer.adaLN_modulation.1", 2 * h, h);
+  return out;
+}
+
+template <typename T>
+mb_status dalloc(T** p, size_t n) {
+  if (cudaMalloc((void**)p, n * sizeof(T)) != cudaSuccess)
+    return set_error(MB_ERR_NOMEM, "cudaMalloc of " + std::to_string(n * sizeof(T)) + " bytes failed");
+  return MB_OK;
+}
+
+mb_status check_launch(cudaError_t e, const char* what) {
+  if (e != cudaSuccess) return cuda_error(e, what);
+  return MB_OK;
+}
+#define MB_TRY(expr)                 \
+  do {                               \
+    mb_status s__ = (expr);          \
+    if (s__ != MB_OK) return s__;    \
+  } while (0)
+
+const mb_weight* W(const mb_flux* m, const std::string& n) { return m->mats.at(n); }
+const float* B(const mb_flux* m, const std::string& n) { return m->vecs.at(n).dev; }
+
+mb_status linear(const mb_flux* m, const std::string& name, const void* x, int64_t M, int64_t ldx, void* y,
+                 int64_t ldy, bool out_bf16, int epi, int64_t gelu_from, const float* gate, cudaStream_t st) {
+  GemmEpilogue e;
+  e.kind = epi;
+  e.out_bf16 = out_bf16;
+  e.gelu_from = epi == MB_EPI_GELU_TANH ? gelu_from : (int64_t)1 << 40;
+  e.y = y;
+  e.ldy = ldy;
+  e.bias = B(m, name + ".bias");
+  e.gate = gate;
+  e.res = (const float*)y;
+  e.ldr = ldy;
+  return check_launch(launch_qgemm(W(m, name + ".weight"), x, M, ldx, e, st), name.c_str());
+}
+
+// Builds the three GEMV job tables: [0] stem in_layers, [1] stem out_layers, [2] all modulations.
+mb_status finalize(mb_flux* m) {
+  const int64_t h = m->h();
+  std::vector<GemvJob> jobs;
+  std::vector<int> blocks;  // pairs (job, row0)
+  auto add = [&](int table, const std::string& name, float* y, int slot) {
+    const mb_weight* w = W(m, name + ".weight");
+    GemvJob j = {};
+    j.w = w->dev;
+    j.type = w->type;
+    j.n_rows = (int)w->n_rows;
+    j.n_cols = (int)w->n_cols;
+    j.row_bytes = w->row_bytes;
+    j.bias = B(m, name + ".bias");
+    j.y = y;
+    j.x_slot = slot;
+    const int id = (int)jobs.size();
+    jobs.push_back(j);
+    for (int r = 0; r < j.n_rows; r += 8) {
+      blocks.push_back(id);
+      blocks.push_back(r);
+    }
+    m->n_jobs[table]++;
+    (void)table;
+  };
+  const bool g = m->cfg.guidance_embed;
+  m->job0[0] = 0;
+  m->block0[0] = 0;
+  add(0, "time_in.in_layer", m->hid, 0);
+  if (g) add(0, "guidance_in.in_layer", m->hid + h, 1);
+  add(0, "vector_in.in_layer", m->hid + 2 * h, 2);
+  m->n_blocks[0] = (int)blocks.size() / 2;
+  m->block0[1] = m->n_blocks[0];
+  add(1, "time_in.out_layer", m->parts, 0);
+  if (g) add(1, "guidance_in.out_layer", m->parts + h, 1);
+  add(1, "vector_in.out_layer", m->parts + 2 * h, 2);
+  m->n_blocks[1] = (int)blocks.size() / 2 - m->block0[1];
+  m->block0[2] = m->block0[1] + m->n_blocks[1];
+  m->mod_off_double.clear();
+  m->mod_off_single.clear();
+  int64_t off = 0;
+  for (int i = 0; i < m->cfg.depth; i++) {
+    m->mod_off_double.push_back(off);
+    off += 12 * h;
+  }
+  for (int i = 0; i < m->cfg.depth_single; i++) {
+    m->mod_off_single.push_back(off);
+    off += 3 * h;
+  }
+  m->mod_off_final = off;
+  off += 2 * h;
+  m->mod_total = off;
+  MB_TRY(dalloc(&m->mods, (size_t)off));
+  for (int i = 0; i < m->cfg.depth; i++) {
+    const std::string p = "double_blocks." + std::to_string(i) + ".";
+    add(2, p + "img_mod.lin", m->mods + m->mod_off_double[i], 0);
+    add(2, p + "txt_mod.lin", m->mods + m->mod_off_double[i] + 6 * h, 0);
+  }
+  for (int i = 0; i < m->cfg.depth_single; i++)
+    add(2, "single_blocks." + std::to_string(i) + ".modulation.lin", m->mods + m->mod_off_single[i], 0);
+  add(2, "final_layer.adaLN_modulation.1", m->mods + m->mod_off_final, 0);
+  m->n_blocks[2] = (int)blocks.size() / 2 - m->block0[2];
+  MB_TRY(dalloc(&m->jobs_dev, jobs.size()));
+  MB_TRY(dalloc(&m->blocks_dev, blocks.size()));
+  if (cudaMemcpy(m->jobs_dev, jobs.data(), jobs.size() * sizeof(GemvJob), cudaMemcpyHostToDevice) != cudaSuccess ||
+      cudaMemcpy(m->blocks_dev, blocks.data(), blocks.size() * sizeof(int), cudaMemcpyHostToDevice) != cudaSuccess)
+    return set_error(MB_ERR_CUDA, "job table upload failed");
+  m->finalized = true;
+  return MB_OK;
+}
+
+mb_status gemv_table(const mb_flux* m, int table, const GemvInput* ins, int n_in, int max_len, cudaStream_t st) {
+  return check_launch(launch_gemv_batch(m->jobs_dev, 0, m->blocks_dev + 2 * m->block0[table], m->n_blocks[table], ins,
+                                        n_in, max_len, st),
+                      "gemv batch");
+}
+
+// The forward pass on device pointers; t / guidance are read from m->scal.
+mb_status run_forward(mb_flux* m, const float* img, int64_t Li, const float* txt, int64_t Lt, const float* y,
+                      cudaStream_t st) {
+  const int64_t h = m->h(), H = m->H(), mh = m->mh(), L = Lt + Li, ldY = m->ldY();
+  const mb_flux_config& c = m->cfg;
+  // ---- conditioning vector: temb(t), temb(g), y -> stem MLPs -> all modulations
+  MB_TRY(check_launch(launch_timestep_embedding(m->scal, 1000.f, m->temb, 256, st), "temb t"));
+  if (c.guidance_embed)
+    MB_TRY(check_launch(launch_timestep_embedding(m->scal + 1, 1000.f, m->temb + 256, 256, st), "temb g"));
+  {
+    GemvInput in[3] = {};
+    in[0].parts[0] = m->temb;
+    in[0].n_parts = 1;
+    in[1].parts[0] = m->temb + 256;
+    in[1].n_parts = 1;
+    in[2].parts[0] = y;
+    in[2].n_parts = 1;
+    MB_TRY(gemv_table(m, 0, in, 3, 4096, st));
+    for (int i = 0; i < 3; i++) {
+      in[i].parts[0] = m->hid + i * h;
+      in[i].apply_silu = 1;
+    }
+    MB_TRY(gemv_table(m, 1, in, 3, 4096, st));
+    GemvInput v = {};
+    v.parts[0] = m->parts;
+    v.parts[1] = m->parts + 2 * h;
+    v.n_parts = 2;
+    if (c.guidance_embed) {
+      v.parts[2] = m->parts + h;
+      v.n_parts = 3;
+    }
+    v.apply_silu = 1;
+    MB_TRY(gemv_table(m, 2, &v, 1, 4096, st));
+  }
+  // ---- stems: txt_in, img_in into the residual stream
+  MB_TRY(check_launch(launch_cast_f32_bf16(txt, Lt, c.context_in_dim, c.context_in_dim, m->txt_bf, c.context_in_dim, st),
+                      "cast txt"));
+  MB_TRY(linear(m, "txt_in", m->txt_bf, Lt, c.context_in_dim, m->x, h, false, MB_EPI_NONE, 0, nullptr, st));
+  MB_TRY(check_launch(launch_cast_f32_bf16(img, Li, c.in_channels, c.in_channels, m->img_bf, c.in_channels, st),
+                      "cast img"));
+  MB_TRY(linear(m, "img_in", m->img_bf, Li, c.in_channels, m->x + Lt * h, h, false, MB_EPI_NONE, 0, nullptr, st));
+
+  const Seg segs[2] = {{0, Lt}, {Lt, Li}};  // txt, img
+  // ---- double-stream blocks
+  for (int i = 0; i < c.depth; i++) {
+    const std::string p = "double_blocks." + std::to_string(i) + ".";
+    const float* md = m->mods + m->mod_off_double[i];
+    for (int s = 0; s < 2; s++) {
+      const Seg g = segs[s];
+      const std::string S = s == 0 ? "txt" : "img";
+      const float* mo = md + (s == 0 ? 6 * h : 0);  // img_mod first, then txt_mod
+      MB_TRY(check_launch(launch_ln_modulate(m->x + g.row0 * h, g.rows, h, h, mo, mo + h, m->xm + g.row0 * h, h, st),
+                          "ln_mod1"));
+      MB_TRY(linear(m, p + S + "_attn.qkv", m->xm + g.row0 * h, g.rows, h, m->Y + g.row0 * ldY, ldY, true,
+                    MB_EPI_NONE, 0, nullptr, st));
+      MB_TRY(check_launch(launch_qk_norm_rope(m->Y + g.row0 * ldY, g.rows, ldY, (int)H,
+                                              B(m, p + S + "_attn.norm.query_norm.scale"),
+                                              B(m, p + S + "_attn.norm.key_norm.scale"), m->pe, g.row0, L, m->q, m->k,
+                                              m->v, st),
+                          "qk_norm_rope"));
+    }
+    MB_TRY(check_launch(launch_attention(m->q, m->k, m->v, (int)H, L, L, L, m->Y + 2 * h, ldY, st), "attention"));
+    for (int s = 0; s < 2; s++) {
+      const Seg g = segs[s];
+      const std::string S = s == 0 ? "txt" : "img";
+      const float* mo = md + (s == 0 ? 6 * h : 0);
+      float* xr = m->x + g.row0 * h;
+      MB_TRY(linear(m, p + S + "_attn.proj", m->Y + g.row0 * ldY + 2 * h, g.rows, ldY, xr, h, false,
+                    MB_EPI_GATE_RESIDUAL, 0, mo + 2 * h, st));
+      MB_TRY(check_launch(launch_ln_modulate(xr, g.rows, h, h, mo + 3 * h, mo + 4 * h, m->xm + g.row0 * h, h, st),
+                          "ln_mod2"));
+      MB_TRY(linear(m, p + S + "_mlp.0", m->xm + g.row0 * h, g.rows, h, m->Y + g.row0 * ldY + 3 * h, ldY, true,
+                    MB_EPI_GELU_TANH, 0, nullptr, st));
+      MB_TRY(linear(m, p + S + "_mlp.2", m->Y + g.row0 * ldY + 3 * h, g.rows, ldY, xr, h, false, MB_EPI_GATE_RESIDUAL,
+                    0, mo + 5 * h, st));
+    }
+  }
+  // ---- single-stream blocks over cat[txt, img] == x
+  for (int i = 0; i < c.depth_single; i++) {
+    const std::string p = "single_blocks." + std::to_string(i) + ".";
+    const float* mo = m->mods + m->mod_off_single[i];
+    MB_TRY(check_launch(launch_ln_modulate(m->x, L, h, h, mo, mo + h, m->xm, h, st), "ln_mod"));
+    MB_TRY(linear(m, p + "linear1", m->xm, L, h, m->Y, ldY, true, MB_EPI_GELU_TANH, 3 * h, nullptr, st));
+    MB_TRY(check_launch(launch_qk_norm_rope(m->Y, L, ldY, (int)H, B(m, p + "norm.query_norm.scale"),
+                                            B(m, p + "norm.key_norm.scale"), m->pe, 0, L, m->q, m->k, m->v, st),
+                        "qk_norm_rope"));
+    MB_TRY(check_launch(launch_attention(m->q, m->k, m->v, (int)H, L, L, L, m->Y + 2 * h, ldY, st), "attention"));
+    MB_TRY(linear(m, p + "linear2", m->Y + 2 * h, L, ldY, m->x, h, false, MB_EPI_GATE_RESIDUAL, 0, mo + 2 * h, st));
+  }
+  // ---- final layer on the img rows
+  {
+    const float* mo = m->mods + m->mod_off_final;
+    MB_TRY(check_launch(launch_ln_modulate(m->x + Lt * h, Li, h, h, mo, mo + h, m->xm + Lt * h, h, st), "ln_final"));
+    MB_TRY(linear(m, "final_layer.linear", m->xm + Lt * h, Li, h, m->pred, c.in_channels, false, MB_EPI_NONE, 0,
+                  nullptr, st));
+  }
+  (void)mh;
+  return MB_OK;
+}
+
+mb_status prepare(mb_flux* m, const float* img_ids, int64_t Li, const float* txt_ids, int64_t Lt, cudaStream_t st) {
+  MB_CHECK(m->finalized || finalize(m) == MB_OK, MB_ERR_NOT_READY, mb_last_error());
+  MB_CHECK(Lt >= 1 && Li >= 1 && Lt <= m->max_txt && Li <= m->max_img, MB_ERR_INVALID,
+           "sequence lengths exceed the model's workspace (max_txt/max_img)");
+  const int64_t L = Lt + Li;
+  MB_CUDA(cudaMemcpyAsync(m->ids, txt_ids, Lt * 3 * sizeof(float), cudaMemcpyDeviceToDevice, st));
+  MB_CUDA(cudaMemcpyAsync(m->ids + Lt * 3, img_ids, Li * 3 * sizeof(float), cudaMemcpyDeviceToDevice, st));
+  MB_CUDA(launch_rope_table(m->ids, L, 3, m->cfg.axes_dim, m->cfg.theta, m->pe, st));
+  return MB_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+mb_status mb_flux_create(const mb_flux_config* cfg, int64_t max_txt, int64_t max_img, mb_flux** out) {
+  MB_CHECK(cfg && out, MB_ERR_INVALID, "NULL argument");
+  *out = nullptr;
+  MB_CHECK(cfg->num_heads > 0 && cfg->hidden_size == cfg->num_heads * 128, MB_ERR_UNSUPPORTED,
+           "head_dim must be 128 (hidden_size == 128 * num_heads)");
+  MB_CHECK(cfg->axes_dim[0] + cfg->axes_dim[1] + cfg->axes_dim[2] == 128, MB_ERR_INVALID, "sum(axes_dim) must be 128");
+  MB_CHECK(cfg->hidden_size % 256 == 0 && cfg->mlp_hidden % 256 == 0, MB_ERR_INVALID,
+           "hidden and mlp sizes must be multiples of 256");
+  MB_CHECK(cfg->context_in_dim % 64 == 0 && cfg->in_channels % 64 == 0 && cfg->vec_in_dim <= 4096 &&
+               cfg->hidden_size <= 4096,
+           MB_ERR_INVALID, "unsupported stem sizes");
+  MB_CHECK(max_txt > 0 && max_img > 0, MB_ERR_INVALID, "max_txt and max_img must be positive");
+  mb_flux* m = new mb_flux();
+  m->cfg = *cfg;
+  cudaGetDevice(&m->device);
+  m->max_txt = max_txt;
+  m->max_img = max_img;
+  const int64_t L = max_txt + max_img, h = m->h(), H = m->H();
+  mb_status s = MB_OK;
+  if ((s = dalloc(&m->x, L * h)) || (s = dalloc(&m->xm, L * h)) || (s = dalloc(&m->Y, L * m->ldY())) ||
+      (s = dalloc(&m->q, H * L * 128)) || (s = dalloc(&m->k, H * L * 128)) || (s = dalloc(&m->v, H * L * 128)) ||
+      (s = dalloc(&m->pe, L * 256)) || (s = dalloc(&m->ids, L * 3)) ||
+      (s = dalloc(&m->txt_bf, max_txt * cfg->context_in_dim)) || (s = dalloc(&m->img_bf, max_img * cfg->in_channels)) ||
+      (s = dalloc(&m->pred, max_img * cfg->in_channels)) || (s = dalloc(&m->scal, 4)) ||
+      (s = dalloc(&m->counter, 1)) || (s = dalloc(&m->temb, 512)) || (s = dalloc(&m->hid, 3 * h)) ||
+      (s = dalloc(&m->parts, 3 * h))) {
+    mb_flux_destroy(m);
+    return s;
+  }
+  cudaMemset(m->hid, 0, 3 * h * sizeof(float));
+  cudaMemset(m->parts, 0, 3 * h * sizeof(float));
+  *out = m;
+  return MB_OK;
+}
+
+mb_status mb_flux_destroy(mb_flux* m) {
+  if (!m) return MB_OK;
+  if (m->graph) cudaGraphExecDestroy(m->graph);
+  for (auto& kv : m->mats) mb_weight_destroy(kv.second);
+  for (auto& kv : m->vecs) cudaFree(kv.second.dev);
+  void* bufs[] = {m->x, m->xm, m->Y, m->q, m->k, m->v, m->pe, m->ids, m->txt_bf, m->img_bf, m->pred, m->scal,
+                  m->counter, m->sched, m->temb, m->hid, m->parts, m->mods, m->jobs_dev, m->blocks_dev};
+  for (void* b : bufs)
+    if (b) cudaFree(b);
+  delete m;
+  return MB_OK;
+}
+
+mb_status mb_flux_set_tensor(mb_flux* m, const char* name, int ggml_type, int64_t n_rows, int64_t n_cols,
+                             const void* data, size_t nbytes, int data_on_device) {
+  MB_CHECK(m && name && data, MB_ERR_INVALID, "NULL argument");
+  MB_CHECK(!m->finalized, MB_ERR_INVALID, "tensors cannot be replaced after the first forward");
+  const std::string n(name);
+  const auto exp = expected_tensors(m->cfg);
+  const std::vector<int64_t>* shape = nullptr;
+  for (const auto& e : exp)
+    if (e.first == n) shape = &e.second;
+  MB_CHECK(shape, MB_ERR_INVALID, "unknown FLUX tensor name '" + n + "'");
+  if (shape->size() == 1) {
+    MB_CHECK(n_rows * n_cols == (*shape)[0], MB_ERR_INVALID, "tensor '" + n + "' has the wrong length");
+    MB_CHECK(ggml_type == MB_GGML_F32 || ggml_type == MB_GGML_F16 || ggml_type == MB_GGML_BF16, MB_ERR_UNSUPPORTED,
+             "1-D tensor '" + n + "' must be F32, F16 or BF16");
+    const int64_t len = (*shape)[0];
+    MB_CHECK((int64_t)nbytes == len * (ggml_type == MB_GGML_F32 ? 4 : 2), MB_ERR_INVALID, "nbytes mismatch for " + n);
+    Vec1 v;
+    v.n = len;
+    MB_TRY(dalloc(&v.dev, (size_t)len));
+    void* tmp = nullptr;
+    if (cudaMalloc(&tmp, nbytes) != cudaSuccess) {
+      cudaFree(v.dev);
+      return set_error(MB_ERR_NOMEM, "staging alloc failed");
+    }
+    cudaMemcpy(tmp, data, nbytes, data_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice);
+    cudaError_t e = launch_dequant(ggml_type, tmp, 1, len, len * (ggml_type == MB_GGML_F32 ? 4 : 2), v.dev, 0, 0);
+    cudaDeviceSynchronize();
+    cudaFree(tmp);
+    if (e != cudaSuccess) {
+      cudaFree(v.dev);
+      return cuda_error(e, "vector upload");
+    }
+    auto it = m->vecs.find(n);
+    if (it != m->vecs.end()) cudaFree(it->second.dev);
+    m->vecs[n] = v;
+    return MB_OK;
+  }
+  MB_CHECK(n_rows == (*shape)[0] && n_cols == (*shape)[1], MB_ERR_INVALID,
+           "tensor '" + n + "' has shape [" + std::to_string(n_rows) + ", " + std::to_string(n_cols) + "], expected [" +
+               std::to_string((*shape)[0]) + ", " + std::to_string((*shape)[1]) + "]");
+  mb_weight* w = nullptr;
+  MB_TRY(mb_weight_create(ggml_type, n_rows, n_cols, data, nbytes, data_on_device, &w));
+  const bool gemm_ready = (w->type == MB_GGML_Q4_K || w->type == MB_GGML_Q8_0) ? n_cols % 256 == 0
+                                                                                 : w->type == MB_GGML_BF16;
+  const bool gemv_only = n.find("_mod.lin") != std::string::npos || n.find("modulation") != std::string::npos ||
+                         n.rfind("time_in", 0) == 0 || n.rfind("vector_in", 0) == 0 || n.rfind("guidance_in", 0) == 0;
+  if (!gemm_ready && !gemv_only) {
+    // Rows whose length is not a multiple of the quant block (or F32/F16 storage): keep a BF16 copy
+    // for the tensor-core path (e.g. img_in [3072, 64]).
+    mb_weight* wb = new mb_weight(*w);
+    wb->type = MB_GGML_BF16;
+    wb->row_bytes = n_cols * 2;
+    if (cudaMalloc(&wb->dev, (size_t)n_rows * n_cols * 2) != cudaSuccess) {
+      delete wb;
+      mb_weight_destroy(w);
+      return set_error(MB_ERR_NOMEM, "bf16 copy alloc failed");
+    }
+    cudaError_t e = launch_dequant(w->type, w->dev, n_rows, n_cols, w->row_bytes, wb->dev, 1, 0);
+    cudaDeviceSynchronize();
+    mb_weight_destroy(w);
+    if (e != cudaSuccess) {
+      mb_weight_destroy(wb);
+      return cuda_error(e, "bf16 conversion");
+    }
+    w = wb;
+  }
+  auto it = m->mats.find(n);
+  if (it != m->mats.end()) mb_weight_destroy(it->second);
+  m->mats[n] = w;
+  return MB_OK;
+}
+
+mb_status mb_flux_missing(const mb_flux* m, char* buf, size_t buflen) {
+  MB_CHECK(m && buf && buflen > 0, MB_ERR_INVALID, "NULL argument");
+  std::string s;
+  for (const auto& e : expected_tensors(m->cfg)) {
+    const bool have = e.second.size() == 1 ? m->vecs.count(e.first) > 0 : m->mats.count(e.first) > 0;
+    if (!have) s += e.first + "\n";
+  }
+  const size_t n = s.size() < buflen - 1 ? s.size() : buflen - 1;
+  memcpy(buf, s.data(), n);
+  buf[n] = 0;
+  return MB_OK;
+}
+
+static mb_status check_complete(const mb_flux* m) {
+  char buf[256];
+  mb_flux_missing(m, buf, sizeof(buf));
+  MB_CHECK(buf[0] == 0, MB_ERR_NOT_READY, std::string("FLUX model is missing tensors, first: ") + buf);
+  return MB_OK;
+}
+
+mb_status mb_flux_forward(mb_flux* m, const float* img, const float* img_ids, int64_t L_img, const float* txt,
+                          const float* txt_ids, int64_t L_txt, float t, const float* y, float guidance, float* pred,
+                          void* stream) {
+  MB_CHECK(m && img && img_ids && txt && txt_ids && y && pred, MB_ERR_INVALID, "NULL argument");
+  MB_TRY(check_complete(m));
+  cudaStream_t st = (cudaStream_t)stream;
+  MB_TRY(prepare(m, img_ids, L_img, txt_ids, L_txt, st));
+  k_set_scalars<<<1, 1, 0, st>>>(m->scal, t, guidance);
+  MB_TRY(run_forward(m, img, L_img, txt, L_txt, y, st));
+  MB_CUDA(cudaMemcpyAsync(pred, m->pred, L_img * m->cfg.in_channels * sizeof(float), cudaMemcpyDeviceToDevice, st));
+  return MB_OK;
+}
+
+mb_status mb_flux_denoise(mb_flux* m, float* img, const float* img_ids, int64_t L_img, const float* txt,
+                          const float* txt_ids, int64_t L_txt, const float* y, const double* timesteps,
+                          int n_timesteps, float guidance, void* stream) {
+  MB_CHECK(m && img && img_ids && txt && txt_ids && y && timesteps, MB_ERR_INVALID, "NULL argument");
+  MB_CHECK(n_timesteps >= 2, MB_ERR_INVALID, "need at least two timesteps");
+  MB_TRY(check_complete(m));
+  cudaStream_t st = (cudaStream_t)stream;
+  MB_TRY(prepare(m, img_ids, L_img, txt_ids, L_txt, st));
+  if (m->sched_cap < n_timesteps) {
+    if (m->sched) cudaFree(m->sched);
+    m->sched = nullptr;
+    MB_TRY(dalloc(&m->sched, (size_t)n_timesteps));
+    m->sched_cap = n_timesteps;
+  }
+  MB_CUDA(cudaMemcpyAsync(m->sched, timesteps, n_timesteps * sizeof(double), cudaMemcpyHostToDevice, st));
+  MB_CUDA(cudaMemsetAsync(m->counter, 0, sizeof(int), st));
+  k_set_scalars<<<1, 1, 0, st>>>(m->scal, (float)timesteps[0], guidance);
+  const int64_t n_img = L_img * m->cfg.in_channels;
+  const void* key[6] = {img, txt, y, m->sched, nullptr, nullptr};
+  const bool reuse = m->graph && m->graph_lt == L_txt && m->graph_li == L_img &&
+                     memcmp(key, m->graph_key, sizeof(key)) == 0;
+  if (!reuse) {
+    if (m->graph) {
+      cudaGraphExecDestroy(m->graph);
+      m->graph = nullptr;
+    }
+    // Eager warm-up of the step so every kernel attribute is set before capture.
+    k_step_prologue<<<1, 1, 0, st>>>(m->sched, m->counter, m->scal);
+    MB_TRY(run_forward(m, img, L_img, txt, L_txt, y, st));
+    MB_CUDA(cudaMemsetAsync(m->counter, 0, sizeof(int), st));
+    MB_CUDA(cudaStreamSynchronize(st));
+    cudaStream_t cs;
+    MB_CUDA(cudaStreamCreateWithFlags(&cs, cudaStreamNonBlocking));
+    cudaGraph_t g;
+    MB_CUDA(cudaStreamBeginCapture(cs, cudaStreamCaptureModeThreadLocal));
+    k_step_prologue<<<1, 1, 0, cs>>>(m->sched, m->counter, m->scal);
+    mb_status s = run_forward(m, img, L_img, txt, L_txt, y, cs);
+    cudaError_t le = launch_euler_dev(img, m->pred, n_img, m->scal + 2, cs);
+    cudaError_t ce = cudaStreamEndCapture(cs, &g);
+    cudaStreamDestroy(cs);
+    if (s != MB_OK) return s;
+    MB_CUDA(le);
+    MB_CUDA(ce);
+    cudaError_t ie = cudaGraphInstantiate(&m->graph, g, 0);
+    cudaGraphDestroy(g);
+    MB_CUDA(ie);
+    m->graph_lt = L_txt;
+    m->graph_li = L_img;
+    memcpy(m->graph_key, key, sizeof(key));
+  }
+  for (int i = 0; i + 1 < n_timesteps; i++) MB_CUDA(cudaGraphLaunch(m->graph, st));
+  return MB_OK;
+}
+
+}  // extern "C"

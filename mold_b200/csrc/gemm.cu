@@ -1,0 +1,432 @@
+// K2: GGUF-quantized linear y = epilogue(x W^T + b) on tcgen05 / TMEM (sm_100a).
+//
+// Replaces candle's QMatMul::forward (quantized FLUX, flux/transformer.rs:64-72)
+// and QwenLinear::forward (qwen_image/quantized_transformer.rs:54-77).
+//
+// Design (one persistent CTA per SM, warp-specialised):
+//   * The product is computed transposed: D[n, m] = W[n, :] . X[m, :], so the
+//     weight tile is the MMA's A operand and lives in TENSOR MEMORY: dequant
+//     warps decode raw GGML blocks to bf16 in registers and tcgen05.st them
+//     straight into TMEM (one TMEM lane = one weight row). Dequantized weights
+//     never touch shared memory, which keeps shared-memory traffic at the X tile
+//     (TMA write + MMA read) plus the raw blocks.
+//   * X (activations, bf16, K-major) is TMA-loaded with the 128-byte swizzle into
+//     an 8-stage ring and read by tcgen05.mma as the B operand.
+//   * Raw weight bytes are TMA-loaded per 64-wide K stage (Q4_K: the 16-byte
+//     header + the 32 bytes of nibbles of that stage; Q8_0: the 80-byte window
+//     holding the stage's two 34-byte blocks; BF16: 128 bytes).
+//   * Accumulators: two 128x128 f32 tiles in TMEM (double buffered), so the
+//     epilogue warps drain tile i while the MMA warp runs tile i+1.
+// Warp roles (448 threads): 0 TMA producer, 1 MMA issuer + TMEM owner,
+// 2..9 dequant (two threads per weight row, one per K half of a stage),
+// 10..13 epilogue (thread = output feature n; stores are coalesced along n).
+//
+// Bit-exactness: the dequantized value of every weight equals the GGML decode
+// (Q4_K: (d*sc)*q - dmin*m with one rounding per operation; Q8_0: d*q) rounded
+// to bf16 RNE. d1*q is formed as fma(d1, 2^23+q, -d1*2^23), which is the same
+// single rounding of the exact product.
+#include "common.cuh"
+#include "internal.h"
+
+namespace mb {
+
+namespace gemm {
+
+constexpr int TN = 128;  // weight rows per tile (MMA M, TMEM lanes)
+constexpr int TM = 128;  // activation rows per tile (MMA N)
+constexpr int BK = 64;   // K per stage
+constexpr int SX = 8;    // X ring depth
+constexpr int SAT = 8;   // TMEM A-stage ring depth (32 columns each)
+constexpr int kThreads = 448;
+constexpr uint32_t kXStageBytes = TM * BK * 2;  // 16 KB
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kTmemA = 256;  // first A-stage column
+
+template <int WT>
+struct Cfg;
+template <>
+struct Cfg<MB_GGML_Q4_K> {
+  static constexpr int kRawRow = 48, kSR = 8;
+};
+template <>
+struct Cfg<MB_GGML_Q8_0> {
+  static constexpr int kRawRow = 80, kSR = 8;
+};
+template <>
+struct Cfg<MB_GGML_BF16> {
+  static constexpr int kRawRow = 128, kSR = 4;
+};
+
+template <int WT>
+constexpr size_t smem_bytes() {
+  return 1024 + (size_t)SX * kXStageBytes + (size_t)Cfg<WT>::kSR * TN * Cfg<WT>::kRawRow + 512;
+}
+
+struct Params {
+  int M, N, K;
+  int tiles_m, tiles_n;
+  GemmEpilogue epi;
+  int* status;
+};
+
+// ---- Q4_K helpers ----
+MB_DEV uint32_t sbyte(uint32_t sy, uint32_t sz, uint32_t sw, int k) {
+  uint32_t w = k < 4 ? sy : (k < 8 ? sz : sw);
+  return (w >> ((k & 3) * 8)) & 0xFFu;
+}
+MB_DEV void q4k_scale_min(int j, uint32_t sy, uint32_t sz, uint32_t sw, int& sc, int& m) {
+  if (j < 4) {
+    sc = sbyte(sy, sz, sw, j) & 63;
+    m = sbyte(sy, sz, sw, j + 4) & 63;
+  } else {
+    sc = (sbyte(sy, sz, sw, j + 4) & 0xF) | ((sbyte(sy, sz, sw, j - 4) >> 6) << 4);
+    m = (sbyte(sy, sz, sw, j + 4) >> 4) | ((sbyte(sy, sz, sw, j) >> 6) << 4);
+  }
+}
+MB_DEV float h16(uint32_t v) { return __half2float(__ushort_as_half((unsigned short)(v & 0xFFFFu))); }
+
+// 4 nibbles/bytes (one per byte of `b`, values 0..255) -> 2 packed bf16x2 of d1*b - m1.
+MB_DEV void dq4(uint32_t b, float d1, float c1, float m1, uint32_t& o0, uint32_t& o1) {
+  float f0 = __int_as_float(__byte_perm(b, 0x4B000000u, 0x7440));
+  float f1 = __int_as_float(__byte_perm(b, 0x4B000000u, 0x7441));
+  float f2 = __int_as_float(__byte_perm(b, 0x4B000000u, 0x7442));
+  float f3 = __int_as_float(__byte_perm(b, 0x4B000000u, 0x7443));
+  float v0 = __fsub_rn(__fmaf_rn(d1, f0, c1), m1);
+  float v1 = __fsub_rn(__fmaf_rn(d1, f1, c1), m1);
+  float v2 = __fsub_rn(__fmaf_rn(d1, f2, c1), m1);
+  float v3 = __fsub_rn(__fmaf_rn(d1, f3, c1), m1);
+  o0 = pack_bf16x2(v0, v1);
+  o1 = pack_bf16x2(v2, v3);
+}
+
+// 4 int8 (bytes of q) -> 2 packed bf16x2 of d*q (exact product, one rounding to bf16).
+MB_DEV void dq8(uint32_t q, float d, uint32_t& o0, uint32_t& o1) {
+  uint32_t b = q ^ 0x80808080u;  // bias to 0..255
+  const float kBias = 8388736.f;  // 2^23 + 128
+  float f0 = __fsub_rn(__int_as_float(__byte_perm(b, 0x4B000000u, 0x7440)), kBias);
+  float f1 = __fsub_rn(__int_as_float(__byte_perm(b, 0x4B000000u, 0x7441)), kBias);
+  float f2 = __fsub_rn(__int_as_float(__byte_perm(b, 0x4B000000u, 0x7442)), kBias);
+  float f3 = __fsub_rn(__int_as_float(__byte_perm(b, 0x4B000000u, 0x7443)), kBias);
+  o0 = pack_bf16x2(__fmul_rn(f0, d), __fmul_rn(f1, d));
+  o1 = pack_bf16x2(__fmul_rn(f2, d), __fmul_rn(f3, d));
+}
+
+// Q8_0 block at byte offset P (compile-time) of a 48-byte window W[12].
+template <int P>
+MB_DEV void q8_block(const uint32_t (&W)[12], uint32_t (&o)[16]) {
+  constexpr int wi = P >> 2;
+  float d = (P & 3) == 0 ? h16(W[wi]) : h16(W[wi] >> 16);
+  constexpr int qb = P + 2;  // first quant byte
+  constexpr int qw = qb >> 2;
+#pragma unroll
+  for (int i = 0; i < 8; i++) {
+    uint32_t q = (qb & 3) == 0 ? W[qw + i] : __byte_perm(W[qw + i], W[qw + i + 1], 0x5432);
+    dq8(q, d, o[2 * i], o[2 * i + 1]);
+  }
+}
+
+MB_DEV void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
+          taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
+
+// D(tmem) (+)= A(tmem) * B(smem desc)^T
+MB_DEV void umma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(
+          d_tmem),
+      "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+template <int WT>
+__global__ void __launch_bounds__(kThreads, 1)
+    k_qgemm(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_r0,
+            const __grid_constant__ CUtensorMap tm_r1, const Params p) {
+  constexpr int kSR = Cfg<WT>::kSR;
+  constexpr uint32_t kRawStage = TN * Cfg<WT>::kRawRow;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  uint8_t* xs = smem;                                    // SX x 16 KB, 1024-aligned
+  uint8_t* rs = smem + SX * kXStageBytes;                // kSR raw stages
+  uint64_t* bars = (uint64_t*)(rs + kSR * kRawStage);
+  uint64_t* x_full = bars;
+  uint64_t* x_empty = x_full + SX;
+  uint64_t* r_full = x_empty + SX;
+  uint64_t* r_empty = r_full + kSR;
+  uint64_t* a_full = r_empty + kSR;
+  uint64_t* a_empty = a_full + SAT;
+  uint64_t* acc_full = a_empty + SAT;
+  uint64_t* acc_empty = acc_full + 2;
+  uint32_t* tmem_slot = (uint32_t*)(acc_empty + 2);
+  volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nks = p.K / BK;
+  const int n_tiles = p.tiles_m * p.tiles_n;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < SX; i++) { mbar_init(&x_full[i], 1); mbar_init(&x_empty[i], 1); }
+    for (int i = 0; i < kSR; i++) { mbar_init(&r_full[i], 1); mbar_init(&r_empty[i], 8); }
+    for (int i = 0; i < SAT; i++) { mbar_init(&a_full[i], 8); mbar_init(&a_empty[i], 1); }
+    for (int i = 0; i < 2; i++) { mbar_init(&acc_full[i], 1); mbar_init(&acc_empty[i], 4); }
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, kTmemCols);
+    tmem_relinquish();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tm_x);
+    tma_prefetch_desc(&tm_r0);
+    if (WT == MB_GGML_Q4_K) tma_prefetch_desc(&tm_r1);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------ TMA producer
+    if (lane == 0) {
+      uint32_t it = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x) {
+        const int m0 = (tile % p.tiles_m) * TM, n0 = (tile / p.tiles_m) * TN;
+        for (int ks = 0; ks < nks && ok; ks++, it++) {
+          const uint32_t sx = it % SX, px = (it / SX) & 1;
+          if (!(ok = mbar_wait(&x_empty[sx], px ^ 1, abort_flag, p.status, kDevTimeoutGemm))) break;
+          mbar_expect_tx(&x_full[sx], kXStageBytes);
+          tma_load_2d(xs + sx * kXStageBytes, &tm_x, &x_full[sx], ks * BK, m0);
+          const uint32_t sr = it % kSR, pr = (it / kSR) & 1;
+          if (!(ok = mbar_wait(&r_empty[sr], pr ^ 1, abort_flag, p.status, kDevTimeoutGemm))) break;
+          mbar_expect_tx(&r_full[sr], kRawStage);
+          uint8_t* rdst = rs + sr * kRawStage;
+          if (WT == MB_GGML_Q4_K) {
+            const int kb = ks >> 2, g = ks & 3;
+            tma_load_2d(rdst, &tm_r0, &r_full[sr], kb * 144, n0);
+            tma_load_2d(rdst + TN * 16, &tm_r1, &r_full[sr], kb * 144 + 16 + 32 * g, n0);
+          } else if (WT == MB_GGML_Q8_0) {
+            tma_load_2d(rdst, &tm_r0, &r_full[sr], (68 * ks) & ~15, n0);
+          } else {
+            tma_load_2d(rdst, &tm_r0, &r_full[sr], ks * 128, n0);
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------ MMA issuer
+    constexpr uint32_t idesc = idesc_bf16(TN, TM);
+    uint32_t it = 0, tcount = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x, tcount++) {
+      const uint32_t buf = tcount & 1, pb = (tcount >> 1) & 1;
+      if (!(ok = mbar_wait(&acc_empty[buf], pb ^ 1, abort_flag, p.status, kDevTimeoutGemm))) break;
+      tc_fence_after();
+      const uint32_t d_tmem = tmem + buf * TM;
+      for (int ks = 0; ks < nks; ks++, it++) {
+        const uint32_t sx = it % SX, px = (it / SX) & 1;
+        const uint32_t sa = it % SAT, pa = (it / SAT) & 1;
+        if (!(ok = mbar_wait(&x_full[sx], px, abort_flag, p.status, kDevTimeoutGemm))) break;
+        if (!(ok = mbar_wait(&a_full[sa], pa, abort_flag, p.status, kDevTimeoutGemm))) break;
+        tc_fence_after();
+        if (lane == 0) {
+          const uint32_t xaddr = smem_u32(xs + sx * kXStageBytes);
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; kk++) {
+            const uint64_t bdesc = sw128_desc(xaddr + kk * 32, 16, 1024);
+            umma_ts(d_tmem, tmem + kTmemA + sa * 32 + kk * 8, bdesc, idesc, (ks | kk) != 0);
+          }
+          umma_commit(&x_empty[sx]);
+          umma_commit(&a_empty[sa]);
+        }
+        __syncwarp();
+      }
+      if (!ok) break;
+      if (lane == 0) umma_commit(&acc_full[buf]);
+      __syncwarp();
+    }
+  } else if (warp < 10) {
+    // ------------------------------------------------ dequant: raw GGML -> bf16 -> TMEM
+    const int q = warp & 3;               // TMEM lane quarter
+    const int hh = (warp - 2) >> 2;       // K half of the stage (32 values)
+    const int r = q * 32 + lane;          // weight row within the tile == TMEM lane
+    const uint32_t lane_addr = (uint32_t)(q * 32) << 16;
+    uint32_t it = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x) {
+      for (int ks = 0; ks < nks; ks++, it++) {
+        const uint32_t sr = it % kSR, pr = (it / kSR) & 1;
+        const uint32_t sa = it % SAT, pa = (it / SAT) & 1;
+        if (!(ok = mbar_wait(&r_full[sr], pr, abort_flag, p.status, kDevTimeoutGemm))) break;
+        const uint8_t* R = rs + sr * kRawStage;
+        uint32_t o[16];
+        if (WT == MB_GGML_Q4_K) {
+          const uint4 h = *(const uint4*)(R + r * 16);
+          const uint4* qp = (const uint4*)(R + TN * 16 + r * 32);
+          const uint4 qa = qp[0], qb = qp[1];
+          const float d = h16(h.x), dmin = h16(h.x >> 16);
+          int sc, mm;
+          q4k_scale_min(2 * (ks & 3) + hh, h.y, h.z, h.w, sc, mm);
+          const float d1 = d * (float)sc, m1 = dmin * (float)mm;
+          const float c1 = -(d1 * 8388608.f);
+          const uint32_t w[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+#pragma unroll
+          for (int i = 0; i < 8; i++) {
+            const uint32_t nib = hh ? ((w[i] >> 4) & 0x0F0F0F0Fu) : (w[i] & 0x0F0F0F0Fu);
+            dq4(nib, d1, c1, m1, o[2 * i], o[2 * i + 1]);
+          }
+        } else if (WT == MB_GGML_Q8_0) {
+          const int off = (68 * ks) & 15;  // window offset of block 0 (0,4,8,12)
+          const int base16 = hh ? 32 : 0;  // 16-aligned start of the 48-byte window
+          const uint4* src = (const uint4*)(R + r * 80 + base16);
+          const uint4 a0 = src[0], a1 = src[1], a2 = src[2];
+          const uint32_t W[12] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w, a2.x, a2.y, a2.z, a2.w};
+          // block start within the window: hh=0 -> off ; hh=1 -> off + 34 - 32
+          const int P = hh ? off + 2 : off;
+          switch (P) {
+            case 0: q8_block<0>(W, o); break;
+            case 4: q8_block<4>(W, o); break;
+            case 8: q8_block<8>(W, o); break;
+            case 12: q8_block<12>(W, o); break;
+            case 2: q8_block<2>(W, o); break;
+            case 6: q8_block<6>(W, o); break;
+            case 10: q8_block<10>(W, o); break;
+            default: q8_block<14>(W, o); break;
+          }
+        } else {
+          const uint4* src = (const uint4*)(R + r * 128 + hh * 64);
+#pragma unroll
+          for (int i = 0; i < 4; i++) {
+            const uint4 v = src[i];
+            o[4 * i] = v.x; o[4 * i + 1] = v.y; o[4 * i + 2] = v.z; o[4 * i + 3] = v.w;
+          }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&r_empty[sr]);
+        if (!(ok = mbar_wait(&a_empty[sa], pa ^ 1, abort_flag, p.status, kDevTimeoutGemm))) break;
+        tc_fence_after();
+        tmem_st16(tmem + lane_addr + kTmemA + sa * 32 + hh * 16, o);
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&a_full[sa]);
+      }
+    }
+  } else {
+    // ------------------------------------------------ epilogue
+    const int q = warp & 3;
+    const uint32_t lane_addr = (uint32_t)(q * 32) << 16;
+    const GemmEpilogue& e = p.epi;
+    uint32_t tcount = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x, tcount++) {
+      const uint32_t buf = tcount & 1, pb = (tcount >> 1) & 1;
+      const int m0 = (tile % p.tiles_m) * TM, n0 = (tile / p.tiles_m) * TN;
+      const int n = n0 + q * 32 + lane;
+      if (!(ok = mbar_wait(&acc_full[buf], pb, abort_flag, p.status, kDevTimeoutGemm))) break;
+      tc_fence_after();
+      const bool nvalid = n < p.N;
+      const float bias = (nvalid && e.bias) ? e.bias[n] : 0.f;
+      const float gate = (nvalid && e.kind == MB_EPI_GATE_RESIDUAL) ? e.gate[n] : 0.f;
+      const bool do_gelu = e.kind == MB_EPI_GELU_TANH && n >= e.gelu_from;
+#pragma unroll 1
+      for (int c = 0; c < TM / 32; c++) {
+        uint32_t v[32];
+        tmem_ld32(tmem + lane_addr + buf * TM + c * 32, v);
+        tmem_wait_ld();
+        const int mb = m0 + c * 32;
+        if (nvalid) {
+#pragma unroll
+          for (int i = 0; i < 32; i++) {
+            const int m = mb + i;
+            if (m < p.M) {
+              float a = __uint_as_float(v[i]) + bias;
+              if (e.kind == MB_EPI_GATE_RESIDUAL) {
+                const float rv = e.res[(int64_t)m * e.ldr + n];
+                ((float*)e.y)[(int64_t)m * e.ldy + n] = rv + gate * a;
+              } else {
+                if (do_gelu) a = gelu_tanh(a);
+                if (e.out_bf16)
+                  ((__nv_bfloat16*)e.y)[(int64_t)m * e.ldy + n] = __float2bfloat16_rn(a);
+                else
+                  ((float*)e.y)[(int64_t)m * e.ldy + n] = a;
+              }
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[buf]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+template <int WT>
+cudaError_t launch_t(const mb_weight* w, const void* x, int64_t M, int64_t ldx, const GemmEpilogue& epi,
+                     cudaStream_t st) {
+  CUtensorMap tx, tr0, tr1;
+  if (!make_tmap_2d(&tx, x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)w->n_cols, (uint64_t)M, (uint64_t)ldx * 2,
+                    BK, TM, CU_TENSOR_MAP_SWIZZLE_128B))
+    return cudaErrorInvalidValue;
+  const uint64_t rb = (uint64_t)w->row_bytes, nr = (uint64_t)w->n_rows;
+  if (WT == MB_GGML_Q4_K) {
+    if (!make_tmap_2d(&tr0, w->dev, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, rb, nr, rb, 16, TN, CU_TENSOR_MAP_SWIZZLE_NONE) ||
+        !make_tmap_2d(&tr1, w->dev, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, rb, nr, rb, 32, TN, CU_TENSOR_MAP_SWIZZLE_NONE))
+      return cudaErrorInvalidValue;
+  } else {
+    const uint32_t box = WT == MB_GGML_Q8_0 ? 80 : 128;
+    if (!make_tmap_2d(&tr0, w->dev, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, rb, nr, rb, box, TN, CU_TENSOR_MAP_SWIZZLE_NONE))
+      return cudaErrorInvalidValue;
+    tr1 = tr0;
+  }
+  Params p;
+  p.M = (int)M;
+  p.N = (int)w->n_rows;
+  p.K = (int)w->n_cols;
+  p.tiles_m = (int)((M + TM - 1) / TM);
+  p.tiles_n = (int)((w->n_rows + TN - 1) / TN);
+  p.epi = epi;
+  p.status = device_status_ptr();
+  const int tiles = p.tiles_m * p.tiles_n;
+  const int grid = tiles < num_sms() ? tiles : num_sms();
+  constexpr size_t smem = smem_bytes<WT>();
+  static int attr_done[64];  // per template instance and device
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!attr_done[dev & 63]) {
+    cudaError_t e = cudaFuncSetAttribute(k_qgemm<WT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    attr_done[dev & 63] = 1;
+  }
+  k_qgemm<WT><<<grid, kThreads, smem, st>>>(tx, tr0, tr1, p);
+  return cudaGetLastError();
+}
+
+}  // namespace gemm
+
+cudaError_t launch_qgemm(const mb_weight* w, const void* x_bf16, int64_t M, int64_t ldx, const GemmEpilogue& epi,
+                         cudaStream_t st) {
+  if (M <= 0) return cudaSuccess;
+  switch (w->type) {
+    case MB_GGML_Q4_K: return gemm::launch_t<MB_GGML_Q4_K>(w, x_bf16, M, ldx, epi, st);
+    case MB_GGML_Q8_0: return gemm::launch_t<MB_GGML_Q8_0>(w, x_bf16, M, ldx, epi, st);
+    case MB_GGML_BF16: return gemm::launch_t<MB_GGML_BF16>(w, x_bf16, M, ldx, epi, st);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+}  // namespace mb

@@ -1,0 +1,103 @@
+// Host-side internals shared by the .cu files of libmold_b200 (not part of the C ABI).
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <string>
+
+#include "../../include/mold_b200.h"
+
+struct mb_weight {
+  int type;        // GGML type id
+  int64_t n_rows;  // output features
+  int64_t n_cols;  // input features (blocks run along this axis)
+  int64_t row_bytes;
+  void* dev;       // device copy of the raw GGML bytes
+  int device;
+};
+
+namespace mb {
+
+// ---- error plumbing (thread-local last error) ----
+mb_status set_error(mb_status s, const std::string& msg);
+mb_status cuda_error(cudaError_t e, const char* what);
+#define MB_CUDA(call)                                   \
+  do {                                                  \
+    cudaError_t e__ = (call);                           \
+    if (e__ != cudaSuccess) return ::mb::cuda_error(e__, #call); \
+  } while (0)
+#define MB_CHECK(cond, status, msg)                     \
+  do {                                                  \
+    if (!(cond)) return ::mb::set_error(status, msg);   \
+  } while (0)
+
+int num_sms();
+int* device_status_ptr();  // per-device status word (allocated on first use)
+int64_t row_bytes_of(int ggml_type, int64_t n_cols);  // -1 if unsupported / not divisible
+bool ggml_type_supported(int ggml_type);
+
+// ---- TMA descriptors ----
+bool make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, int elem_bytes, uint64_t inner,
+                  uint64_t outer, uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer,
+                  CUtensorMapSwizzle swz);
+bool make_tmap_3d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, int elem_bytes, uint64_t d0,
+                  uint64_t d1, uint64_t d2, uint64_t stride1_bytes, uint64_t stride2_bytes, uint32_t b0, uint32_t b1,
+                  uint32_t b2, CUtensorMapSwizzle swz);
+
+// ---- per-device scratch (grown on demand; used by the f32-input path of mb_qlinear) ----
+void* device_scratch(size_t bytes);
+
+// ---- launchers (return cudaError_t of the launch) ----
+struct GemmEpilogue {
+  int kind;          // MB_EPI_*
+  int out_bf16;      // 1: bf16 output, 0: f32
+  int64_t gelu_from;
+  void* y;
+  int64_t ldy;
+  const float* bias;
+  const float* gate;
+  const float* res;
+  int64_t ldr;
+};
+cudaError_t launch_qgemm(const mb_weight* w, const void* x_bf16, int64_t M, int64_t ldx, const GemmEpilogue& epi,
+                         cudaStream_t st);
+cudaError_t launch_dequant(int type, const void* raw, int64_t n_rows, int64_t n_cols, int64_t row_bytes, void* out,
+                           int out_bf16, cudaStream_t st);
+cudaError_t launch_cast_f32_bf16(const float* x, int64_t M, int64_t K, int64_t ldx, void* y, int64_t ldy,
+                                 cudaStream_t st);
+
+struct GemvJob {
+  const void* w;       // raw GGML rows
+  int type;
+  int n_rows, n_cols;
+  int64_t row_bytes;
+  const float* bias;   // [n_rows] or null
+  float* y;            // [n_rows]
+  int x_slot;          // which staged input vector (0..3)
+  int row_begin;       // first global row of this job (prefix sum)
+};
+struct GemvInput {
+  const float* parts[3];  // x = silu?(sum of non-null parts)
+  int n_parts;
+  int apply_silu;
+  int len;
+};
+// Runs a batch of GEMV jobs in one launch. jobs_dev / block_job_dev live in device memory.
+cudaError_t launch_gemv_batch(const GemvJob* jobs_dev, int n_jobs, const int* block_job_dev, int n_blocks,
+                              const GemvInput* inputs, int n_inputs, int max_len, cudaStream_t st);
+
+cudaError_t launch_ln_modulate(const float* x, int64_t M, int64_t C, int64_t ldx, const float* shift,
+                               const float* scale, void* y, int64_t ldy, cudaStream_t st);
+cudaError_t launch_rope_table(const float* ids, int64_t L, int n_axes, const int* axes_dim, int theta, float* pe,
+                              cudaStream_t st);
+cudaError_t launch_qk_norm_rope(const void* qkv, int64_t M, int64_t ld_qkv, int H, const float* q_scale,
+                                const float* k_scale, const float* pe, int64_t row_offset, int64_t L_total, void* q,
+                                void* k, void* v, cudaStream_t st);
+cudaError_t launch_attention(const void* q, const void* k, const void* v, int H, int64_t Lq, int64_t Lk,
+                             int64_t n_valid, void* out, int64_t ldo, cudaStream_t st);
+cudaError_t launch_euler(float* img, const float* pred, int64_t n, float dt, cudaStream_t st);
+cudaError_t launch_euler_dev(float* img, const float* pred, int64_t n, const float* dt_dev, cudaStream_t st);
+cudaError_t launch_timestep_embedding(const float* t_dev, float scale, float* out, int dim, cudaStream_t st);
+
+}  // namespace mb

@@ -1,0 +1,104 @@
+"""FluxTransformer — the FLUX.1 GGUF transformer behind the C ABI.
+
+Mirrors the reference's `FluxTransformer` enum arm (crates/mold-inference/src/flux/transformer.rs:17-98):
+`forward(img, img_ids, txt, txt_ids, timesteps, y, guidance)` is candle's
+`WithForward::forward` for the quantized model, and `denoise(...)` is the Euler
+loop of `FluxTransformer::denoise`. Weights are handed over by GGUF tensor name
+(as `quantized_var_builder::VarBuilder::from_gguf` reads them, flux/pipeline.rs:976).
+"""
+import ctypes
+from dataclasses import dataclass
+
+import torch
+
+from ._lib import FluxConfigC, check, lib
+from .ops import QTensor, _ptr, _stream, init
+
+
+@dataclass
+class FluxConfig:
+    """candle flux::model::Config (FLUX.1-dev values by default)."""
+    in_channels: int = 64
+    vec_in_dim: int = 768
+    context_in_dim: int = 4096
+    hidden_size: int = 3072
+    mlp_ratio: float = 4.0
+    num_heads: int = 24
+    depth: int = 19
+    depth_single_blocks: int = 38
+    axes_dim: tuple = (16, 56, 56)
+    theta: int = 10000
+    qkv_bias: bool = True
+    guidance_embed: bool = True
+
+    @property
+    def mlp_hidden(self):
+        return int(self.hidden_size * self.mlp_ratio)
+
+    def to_c(self):
+        c = FluxConfigC()
+        c.in_channels, c.vec_in_dim, c.context_in_dim = self.in_channels, self.vec_in_dim, self.context_in_dim
+        c.hidden_size, c.mlp_hidden, c.num_heads = self.hidden_size, self.mlp_hidden, self.num_heads
+        c.depth, c.depth_single = self.depth, self.depth_single_blocks
+        c.axes_dim[0], c.axes_dim[1], c.axes_dim[2] = self.axes_dim
+        c.theta, c.guidance_embed = self.theta, int(self.guidance_embed)
+        return c
+
+
+class FluxTransformer:
+    def __init__(self, cfg: FluxConfig, max_txt=512, max_img=4096, device=0):
+        init(device)
+        self.cfg, self.device = cfg, device
+        self._cc = cfg.to_c()
+        h = ctypes.c_void_p()
+        check(lib().mb_flux_create(ctypes.byref(self._cc), max_txt, max_img, ctypes.byref(h)))
+        self._h = h
+
+    def __del__(self):
+        h = getattr(self, "_h", None)
+        if h is not None and h.value:
+            try:
+                lib().mb_flux_destroy(h)
+            except Exception:
+                pass
+            self._h = None
+
+    def set_tensor(self, name, qt):
+        """qt: QTensor (host bytes) or a CUDA uint8 tensor with (ggml_type, shape) attributes."""
+        if isinstance(qt, QTensor):
+            n_rows = qt.n_rows if len(qt.shape) > 1 else 1
+            check(lib().mb_flux_set_tensor(self._h, name.encode(), qt.ggml_type, n_rows, qt.n_cols,
+                                           qt.raw.ctypes.data_as(ctypes.c_void_p), qt.raw.size, 0))
+        else:
+            raw, ggml_type, shape = qt
+            n_rows = shape[0] if len(shape) > 1 else 1
+            check(lib().mb_flux_set_tensor(self._h, name.encode(), ggml_type, n_rows, shape[-1], _ptr(raw),
+                                           raw.numel(), 1))
+
+    def load(self, tensors):
+        for name, qt in tensors.items():
+            self.set_tensor(name, qt)
+        return self
+
+    def missing(self):
+        buf = ctypes.create_string_buffer(1 << 16)
+        check(lib().mb_flux_missing(self._h, buf, len(buf)))
+        return [s for s in buf.value.decode().split("\n") if s]
+
+    def forward(self, img, img_ids, txt, txt_ids, t, y, guidance):
+        """img [L_img, C], ids [L, 3], txt [L_txt, ctx], y [vec_in] (f32 CUDA) -> pred [L_img, C]."""
+        img, img_ids, txt, txt_ids, y = (a.contiguous().float() for a in (img, img_ids, txt, txt_ids, y))
+        pred = torch.empty_like(img)
+        check(lib().mb_flux_forward(self._h, _ptr(img), _ptr(img_ids), img.shape[0], _ptr(txt), _ptr(txt_ids),
+                                    txt.shape[0], float(t), _ptr(y), float(guidance), _ptr(pred), _stream()))
+        return pred
+
+    def denoise(self, img, img_ids, txt, txt_ids, y, timesteps, guidance):
+        """In-place Euler loop over `timesteps` (list of floats); returns img."""
+        assert img.dtype == torch.float32 and img.is_contiguous()
+        ts = (ctypes.c_double * len(timesteps))(*[float(t) for t in timesteps])
+        txt, txt_ids, img_ids, y = (a.contiguous().float() for a in (txt, txt_ids, img_ids, y))
+        self._keep = (txt, txt_ids, img_ids, y)
+        check(lib().mb_flux_denoise(self._h, _ptr(img), _ptr(img_ids), img.shape[0], _ptr(txt), _ptr(txt_ids),
+                                    txt.shape[0], _ptr(y), ts, len(timesteps), float(guidance), _stream()))
+        return img

@@ -1,0 +1,188 @@
+"""Torch-tensor front of the single-kernel C-ABI entry points.
+
+Each function takes CUDA tensors, checks dtypes/contiguity, and passes raw
+pointers plus the current torch stream to libmold_b200.so.
+"""
+import ctypes
+
+import numpy as np
+import torch
+
+from ._lib import (DT_BF16, DT_F32, EPI_GATE_RESIDUAL, EPI_GELU_TANH, EPI_NONE, GGML_BF16, GGML_F16, GGML_F32,
+                   GGML_Q4_K, GGML_Q8_0, check, lib)
+
+_BLOCK = {GGML_F32: (1, 4), GGML_F16: (1, 2), GGML_BF16: (1, 2), GGML_Q8_0: (32, 34), GGML_Q4_K: (256, 144)}
+_inited = set()
+
+
+def init(device=0):
+    """mb_init for `device` (idempotent); also makes it torch's current device."""
+    torch.cuda.set_device(device)
+    if device not in _inited:
+        check(lib().mb_init(device))
+        _inited.add(device)
+
+
+def _stream():
+    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+def _ptr(t):
+    return ctypes.c_void_p(t.data_ptr()) if t is not None else None
+
+
+def _dt(t):
+    if t.dtype == torch.float32:
+        return DT_F32
+    if t.dtype == torch.bfloat16:
+        return DT_BF16
+    raise TypeError(f"unsupported dtype {t.dtype}")
+
+
+def row_bytes(ggml_type, n_cols):
+    be, bb = _BLOCK[ggml_type]
+    if n_cols % be:
+        raise ValueError(f"n_cols {n_cols} not a multiple of block {be}")
+    return n_cols // be * bb
+
+
+class QTensor:
+    """A GGUF tensor held as raw GGML bytes: rows = output features, blocks along cols
+    (candle's QTensor)."""
+
+    def __init__(self, ggml_type, shape, raw):
+        self.ggml_type = int(ggml_type)
+        self.shape = tuple(int(s) for s in shape)
+        raw = np.ascontiguousarray(raw, dtype=np.uint8).reshape(-1)
+        n_rows = int(np.prod(self.shape[:-1])) if len(self.shape) > 1 else 1
+        if raw.size != n_rows * row_bytes(self.ggml_type, self.shape[-1]):
+            raise ValueError("raw byte count does not match shape/type")
+        self.raw = raw
+
+    @property
+    def n_rows(self):
+        return int(np.prod(self.shape[:-1])) if len(self.shape) > 1 else 1
+
+    @property
+    def n_cols(self):
+        return self.shape[-1]
+
+
+class QMatMul:
+    """Device copy of a quantized weight; forward(x) = x W^T (candle QMatMul)."""
+
+    def __init__(self, handle, n_rows, n_cols, ggml_type, device):
+        self._h = handle
+        self.n_rows, self.n_cols, self.ggml_type, self.device = n_rows, n_cols, ggml_type, device
+
+    @classmethod
+    def from_weights(cls, qt: QTensor, device=0):
+        init(device)
+        h = ctypes.c_void_p()
+        check(lib().mb_weight_create(qt.ggml_type, qt.n_rows, qt.n_cols, qt.raw.ctypes.data_as(ctypes.c_void_p),
+                                     qt.raw.size, 0, ctypes.byref(h)))
+        return cls(h, qt.n_rows, qt.n_cols, qt.ggml_type, device)
+
+    def __del__(self):
+        h = getattr(self, "_h", None)
+        if h is not None and h.value and lib is not None:
+            try:
+                lib().mb_weight_destroy(h)
+            except Exception:
+                pass
+            self._h = None
+
+    @property
+    def handle(self):
+        return self._h
+
+    def forward(self, x, bias=None, epilogue=EPI_NONE, gelu_from=0, gate=None, residual=None, out=None,
+                out_dtype=None):
+        """x [..., K] (bf16 or f32, CUDA) -> [..., N]. Epilogues as mb_qlinear."""
+        return qlinear(self, x, bias=bias, epilogue=epilogue, gelu_from=gelu_from, gate=gate, residual=residual,
+                       out=out, out_dtype=out_dtype)
+
+    __call__ = forward
+
+
+def qlinear(w: QMatMul, x, bias=None, epilogue=EPI_NONE, gelu_from=0, gate=None, residual=None, out=None,
+            out_dtype=None):
+    K, N = w.n_cols, w.n_rows
+    if x.shape[-1] != K:
+        raise ValueError(f"x has K={x.shape[-1]}, weight expects {K}")
+    x2 = x.reshape(-1, K)
+    if x2.stride(-1) != 1:
+        x2 = x2.contiguous()
+    M = x2.shape[0]
+    if epilogue == EPI_GATE_RESIDUAL:
+        out_dtype = torch.float32
+    if out is None:
+        out_dtype = out_dtype or x.dtype
+        out = torch.empty((M, N), dtype=out_dtype, device=x.device)
+    y2 = out.reshape(-1, out.shape[-1])
+    res = residual.reshape(-1, residual.shape[-1]) if residual is not None else None
+    check(lib().mb_qlinear(w.handle, _ptr(x2), _dt(x2), M, x2.stride(0), _ptr(y2), _dt(y2), y2.stride(0),
+                           _ptr(bias), epilogue, gelu_from, _ptr(gate), _ptr(res), res.stride(0) if res is not None else 0,
+                           _stream()))
+    return out.reshape(*x.shape[:-1], N) if out.dim() == 2 and x.dim() != 2 else out
+
+
+def dequantize(w: QMatMul, dtype=torch.float32):
+    out = torch.empty((w.n_rows, w.n_cols), dtype=dtype, device=f"cuda:{w.device}")
+    check(lib().mb_dequant(w.handle, _ptr(out), _dt(out), _stream()))
+    return out
+
+
+def qgemv(w: QMatMul, x, apply_silu=False, bias=None):
+    y = torch.empty(w.n_rows, dtype=torch.float32, device=x.device)
+    check(lib().mb_qgemv(w.handle, _ptr(x.contiguous()), int(apply_silu), _ptr(bias), _ptr(y), _stream()))
+    return y
+
+
+def ln_modulate(x, shift, scale):
+    M, C = x.shape
+    y = torch.empty((M, C), dtype=torch.bfloat16, device=x.device)
+    check(lib().mb_ln_modulate(_ptr(x), M, C, x.stride(0), _ptr(shift), _ptr(scale), _ptr(y), y.stride(0), _stream()))
+    return y
+
+
+def rope_table(ids, axes_dim=(16, 56, 56), theta=10000):
+    L, n_axes = ids.shape
+    pe = torch.empty((L, sum(axes_dim) // 2, 2, 2), dtype=torch.float32, device=ids.device)
+    ax = (ctypes.c_int * len(axes_dim))(*axes_dim)
+    check(lib().mb_rope_table(_ptr(ids.contiguous()), L, n_axes, ax, theta, _ptr(pe), _stream()))
+    return pe
+
+
+def qk_norm_rope(qkv, H, q_scale, k_scale, pe, row_offset=0, L_total=None, q=None, k=None, v=None):
+    M = qkv.shape[0]
+    L_total = L_total or M
+    if q is None:
+        q = torch.empty((H, L_total, 128), dtype=torch.bfloat16, device=qkv.device)
+        k = torch.empty_like(q)
+        v = torch.empty_like(q)
+    check(lib().mb_qk_norm_rope(_ptr(qkv), M, qkv.stride(0), H, _ptr(q_scale), _ptr(k_scale), _ptr(pe), row_offset,
+                                L_total, _ptr(q), _ptr(k), _ptr(v), _stream()))
+    return q, k, v
+
+
+def attention(q, k, v, n_valid_keys=None, out=None):
+    """q [H, Lq, 128], k/v [H, Lk, 128] bf16 -> out [Lq, H*128] bf16."""
+    H, Lq, D = q.shape
+    Lk = k.shape[1]
+    if out is None:
+        out = torch.empty((Lq, H * D), dtype=torch.bfloat16, device=q.device)
+    check(lib().mb_attention(_ptr(q), _ptr(k), _ptr(v), H, Lq, Lk, n_valid_keys or Lk, _ptr(out), out.stride(0),
+                             _stream()))
+    return out
+
+
+def euler_step(img, pred, dt):
+    check(lib().mb_euler_step(_ptr(img), _ptr(pred), img.numel(), float(dt), _stream()))
+    return img
+
+
+def device_status():
+    s = ctypes.c_int(0)
+    check(lib().mb_device_status(ctypes.byref(s)))
+    return s.value

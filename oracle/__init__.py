@@ -1,0 +1,21 @@
+"""CPU oracle for the mold quantized-DiT hot path — TEST INFRASTRUCTURE ONLY.
+
+Only ``tests/``, ``__graft_entry__.smoke()`` and the ``cpu_baseline`` /
+``--impl reference`` legs of ``bench.py`` may import this package, and only as
+the checker or the timed CPU baseline. The product (``mold_b200``, the CUDA
+library behind ``include/mold_b200.h``) never imports, links or calls it.
+
+Pinning status:
+  * GGML codecs (``codec.c``): bit-exact against the ``gguf`` 0.19.0 package
+    (fixtures in ``tests/golden/``).
+  * Schedules (``flux_ref.get_schedule``, ``qwen_ref``): pinned against the
+    reference's own known-answer tests (qwen_image/sampling.rs:136-140).
+  * FLUX / Qwen block math: restated from the reference's in-repo copy of the
+    block math (flux/offload.rs, flux2/transformer.rs:99-178); the reference
+    cannot be built here (no Rust toolchain, candle not vendored), so the block
+    math is **parity unpinned** beyond that restatement.
+"""
+from .codec import (  # noqa: F401
+    GGML_F32, GGML_F16, GGML_Q8_0, GGML_Q4_K, GGML_BF16,
+    block_bytes, block_elems, dequantize, quantize, randn, round_bf16, lib_path,
+)

@@ -1,0 +1,55 @@
+"""Generates the GGML codec golden vectors in this directory.
+
+Run from the repository root, in a container where the `gguf` 0.19.0 package
+is importable (it is the third-party codec the fixtures come from; it is not
+needed to *read* the fixtures):
+
+    python tests/golden/make_golden.py
+
+Fixtures (codec_golden.npz):
+  q8_in        f32 [64, 256]  seeded N(0, 0.02) (+ a zero row, a row of ±max)
+  q8_blocks    gguf-py Q8_0.quantize_blocks of q8_in
+  q8_deq       gguf-py Q8_0.dequantize_blocks of q8_blocks
+  q4k_blocks   uint8 [96, 144]: 64 blocks of random bytes (finite f16 d/dmin,
+               so every 6-bit scale/min packing pattern occurs) + 32 blocks from
+               the oracle's own quantizer
+  q4k_deq      gguf-py Q4_K.dequantize_blocks of q4k_blocks
+"""
+import os
+import sys
+
+import numpy as np
+
+sys.path.insert(0, os.path.join(os.path.dirname(os.path.abspath(__file__)), "..", ".."))
+
+import gguf  # noqa: E402
+from gguf import quants  # noqa: E402
+
+import oracle  # noqa: E402
+
+
+def main():
+    rng = np.random.default_rng(1234)
+    q8_in = oracle.randn(7, (64, 256), 0.02)
+    q8_in[0] = 0.0
+    q8_in[1, ::2] = 3.0
+    q8_in[1, 1::2] = -3.0
+    q8_blocks = quants.quantize(q8_in, gguf.GGMLQuantizationType.Q8_0)
+    q8_deq = quants.dequantize(q8_blocks, gguf.GGMLQuantizationType.Q8_0).reshape(q8_in.shape)
+
+    rand_blocks = rng.integers(0, 256, size=(64, 144), dtype=np.uint8)
+    # finite, moderate f16 d / dmin
+    d = rng.uniform(-0.01, 0.01, size=(64, 2)).astype(np.float16)
+    rand_blocks[:, 0:4] = d.view(np.uint8).reshape(64, 4)
+    own = oracle.quantize(oracle.randn(8, (32, 256), 0.02), oracle.GGML_Q4_K).reshape(32, 144)
+    q4k_blocks = np.concatenate([rand_blocks, own], axis=0)
+    q4k_deq = quants.dequantize(q4k_blocks.reshape(-1), gguf.GGMLQuantizationType.Q4_K).reshape(96, 256)
+
+    out = os.path.join(os.path.dirname(os.path.abspath(__file__)), "codec_golden.npz")
+    np.savez_compressed(out, q8_in=q8_in, q8_blocks=q8_blocks, q8_deq=q8_deq,
+                        q4k_blocks=q4k_blocks, q4k_deq=q4k_deq)
+    print("wrote", out)
+
+
+if __name__ == "__main__":
+    main()
