@@ -539,8 +539,9 @@ mb_status mb_flux_denoise(mb_flux* m, float* img, const float* img_ids, int64_t 
   if (m->sched_cap < n_timesteps) {
     if (m->sched) cudaFree(m->sched);
     m->sched = nullptr;
-    MB_TRY(dalloc(&m->sched, (size_t)n_timesteps));
-    m->sched_cap = n_timesteps;
+    const int cap = n_timesteps > 1024 ? n_timesteps : 1024;  // keeps the pointer (and the graph) stable
+    MB_TRY(dalloc(&m->sched, (size_t)cap));
+    m->sched_cap = cap;
   }
   MB_CUDA(cudaMemcpyAsync(m->sched, timesteps, n_timesteps * sizeof(double), cudaMemcpyHostToDevice, st));
   MB_CUDA(cudaMemsetAsync(m->counter, 0, sizeof(int), st));

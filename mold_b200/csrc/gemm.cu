@@ -15,11 +15,15 @@
 //   * Raw weight bytes are TMA-loaded per 64-wide K stage (Q4_K: the 16-byte
 //     header + the 32 bytes of nibbles of that stage; Q8_0: the 80-byte window
 //     holding the stage's two 34-byte blocks; BF16: 128 bytes).
-//   * Accumulators: two 128x128 f32 tiles in TMEM (double buffered), so the
-//     epilogue warps drain tile i while the MMA warp runs tile i+1.
-// Warp roles (448 threads): 0 TMA producer, 1 MMA issuer + TMEM owner,
+//   * Tile = 128 weight rows x 256 activation rows, so each decoded weight feeds
+//     256 MACs (the dequant rate needed is 16 values per SM clock at full MMA
+//     rate). TMEM: the 128x256 f32 accumulator in columns [0, 256) and an
+//     8-deep ring of 64-wide bf16 A stages in [256, 512). The epilogue releases
+//     the accumulator as soon as its last columns are in registers.
+// Warp roles (576 threads): 0 TMA producer, 1 MMA issuer + TMEM owner,
 // 2..9 dequant (two threads per weight row, one per K half of a stage),
-// 10..13 epilogue (thread = output feature n; stores are coalesced along n).
+// 10..17 epilogue (thread = output feature n; stores are coalesced along n).
+// Decoding uses sm_100's packed f32x2 FMA/SUB (two exact IEEE ops per instruction).
 //
 // Bit-exactness: the dequantized value of every weight equals the GGML decode
 // (Q4_K: (d*sc)*q - dmin*m with one rounding per operation; Q8_0: d*q) rounded
@@ -33,33 +37,34 @@ namespace mb {
 namespace gemm {
 
 constexpr int TN = 128;  // weight rows per tile (MMA M, TMEM lanes)
-constexpr int TM = 128;  // activation rows per tile (MMA N)
+constexpr int TM = 256;  // activation rows per tile (MMA N): every decoded weight feeds 256 rows
 constexpr int BK = 64;   // K per stage
-constexpr int SX = 8;    // X ring depth
 constexpr int SAT = 8;   // TMEM A-stage ring depth (32 columns each)
-constexpr int kThreads = 448;
-constexpr uint32_t kXStageBytes = TM * BK * 2;  // 16 KB
+constexpr int kDW = 8;   // dequant warps (2..9)
+constexpr int kEW = 8;   // epilogue warps (10..17)
+constexpr int kThreads = (2 + kDW + kEW) * 32;
+constexpr uint32_t kXStageBytes = TM * BK * 2;  // 32 KB
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kTmemA = 256;  // first A-stage column
+constexpr uint32_t kTmemA = 256;  // first A-stage column (D uses [0, 256))
 
 template <int WT>
 struct Cfg;
 template <>
 struct Cfg<MB_GGML_Q4_K> {
-  static constexpr int kRawRow = 48, kSR = 8;
+  static constexpr int kRawRow = 48, kSR = 8, kSX = 5;
 };
 template <>
 struct Cfg<MB_GGML_Q8_0> {
-  static constexpr int kRawRow = 80, kSR = 8;
+  static constexpr int kRawRow = 80, kSR = 6, kSX = 5;
 };
 template <>
 struct Cfg<MB_GGML_BF16> {
-  static constexpr int kRawRow = 128, kSR = 4;
+  static constexpr int kRawRow = 128, kSR = 4, kSX = 5;
 };
 
 template <int WT>
 constexpr size_t smem_bytes() {
-  return 1024 + (size_t)SX * kXStageBytes + (size_t)Cfg<WT>::kSR * TN * Cfg<WT>::kRawRow + 512;
+  return 1024 + (size_t)Cfg<WT>::kSX * kXStageBytes + (size_t)Cfg<WT>::kSR * TN * Cfg<WT>::kRawRow + 512;
 }
 
 struct Params {
@@ -68,6 +73,33 @@ struct Params {
   GemmEpilogue epi;
   int* status;
 };
+
+// ---- packed f32x2 arithmetic (sm_100): two IEEE single-precision ops per instruction ----
+MB_DEV uint64_t f2(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1,%2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+MB_DEV uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+MB_DEV uint64_t fsub2(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+MB_DEV uint64_t fmul2(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+MB_DEV uint32_t bf16x2_of(uint64_t v) {  // low float -> low half
+  uint32_t r;
+  asm("{\n .reg .f32 lo, hi;\n mov.b64 {lo, hi}, %1;\n cvt.rn.bf16x2.f32 %0, hi, lo;\n}\n" : "=r"(r) : "l"(v));
+  return r;
+}
 
 // ---- Q4_K helpers ----
 MB_DEV uint32_t sbyte(uint32_t sy, uint32_t sz, uint32_t sw, int k) {
@@ -85,43 +117,41 @@ MB_DEV void q4k_scale_min(int j, uint32_t sy, uint32_t sz, uint32_t sw, int& sc,
 }
 MB_DEV float h16(uint32_t v) { return __half2float(__ushort_as_half((unsigned short)(v & 0xFFFFu))); }
 
-// 4 nibbles/bytes (one per byte of `b`, values 0..255) -> 2 packed bf16x2 of d1*b - m1.
-MB_DEV void dq4(uint32_t b, float d1, float c1, float m1, uint32_t& o0, uint32_t& o1) {
-  float f0 = __int_as_float(__byte_perm(b, 0x4B000000u, 0x7440));
-  float f1 = __int_as_float(__byte_perm(b, 0x4B000000u, 0x7441));
-  float f2 = __int_as_float(__byte_perm(b, 0x4B000000u, 0x7442));
-  float f3 = __int_as_float(__byte_perm(b, 0x4B000000u, 0x7443));
-  float v0 = __fsub_rn(__fmaf_rn(d1, f0, c1), m1);
-  float v1 = __fsub_rn(__fmaf_rn(d1, f1, c1), m1);
-  float v2 = __fsub_rn(__fmaf_rn(d1, f2, c1), m1);
-  float v3 = __fsub_rn(__fmaf_rn(d1, f3, c1), m1);
-  o0 = pack_bf16x2(v0, v1);
-  o1 = pack_bf16x2(v2, v3);
+// 4 values (one per byte of `b`, 0..255) -> 2 packed bf16x2 of (d1*b) - m1, each op rounded
+// once: d1*b = fma(d1, 2^23 + b, -d1*2^23) is the correctly rounded product.
+MB_DEV void dq4(uint32_t b, uint64_t d1, uint64_t c1, uint64_t m1, uint32_t& o0, uint32_t& o1) {
+  const float f0 = __int_as_float(__byte_perm(b, 0x4B000000u, 0x7440));
+  const float f1 = __int_as_float(__byte_perm(b, 0x4B000000u, 0x7441));
+  const float f2v = __int_as_float(__byte_perm(b, 0x4B000000u, 0x7442));
+  const float f3 = __int_as_float(__byte_perm(b, 0x4B000000u, 0x7443));
+  o0 = bf16x2_of(fsub2(ffma2(d1, f2(f0, f1), c1), m1));
+  o1 = bf16x2_of(fsub2(ffma2(d1, f2(f2v, f3), c1), m1));
 }
 
 // 4 int8 (bytes of q) -> 2 packed bf16x2 of d*q (exact product, one rounding to bf16).
-MB_DEV void dq8(uint32_t q, float d, uint32_t& o0, uint32_t& o1) {
-  uint32_t b = q ^ 0x80808080u;  // bias to 0..255
-  const float kBias = 8388736.f;  // 2^23 + 128
-  float f0 = __fsub_rn(__int_as_float(__byte_perm(b, 0x4B000000u, 0x7440)), kBias);
-  float f1 = __fsub_rn(__int_as_float(__byte_perm(b, 0x4B000000u, 0x7441)), kBias);
-  float f2 = __fsub_rn(__int_as_float(__byte_perm(b, 0x4B000000u, 0x7442)), kBias);
-  float f3 = __fsub_rn(__int_as_float(__byte_perm(b, 0x4B000000u, 0x7443)), kBias);
-  o0 = pack_bf16x2(__fmul_rn(f0, d), __fmul_rn(f1, d));
-  o1 = pack_bf16x2(__fmul_rn(f2, d), __fmul_rn(f3, d));
+MB_DEV void dq8(uint32_t q, uint64_t d, uint32_t& o0, uint32_t& o1) {
+  const uint32_t b = q ^ 0x80808080u;  // bias to 0..255
+  const uint64_t kBias = f2(8388736.f, 8388736.f);  // 2^23 + 128
+  const float f0 = __int_as_float(__byte_perm(b, 0x4B000000u, 0x7440));
+  const float f1 = __int_as_float(__byte_perm(b, 0x4B000000u, 0x7441));
+  const float f2v = __int_as_float(__byte_perm(b, 0x4B000000u, 0x7442));
+  const float f3 = __int_as_float(__byte_perm(b, 0x4B000000u, 0x7443));
+  o0 = bf16x2_of(fmul2(fsub2(f2(f0, f1), kBias), d));
+  o1 = bf16x2_of(fmul2(fsub2(f2(f2v, f3), kBias), d));
 }
 
 // Q8_0 block at byte offset P (compile-time) of a 48-byte window W[12].
 template <int P>
 MB_DEV void q8_block(const uint32_t (&W)[12], uint32_t (&o)[16]) {
   constexpr int wi = P >> 2;
-  float d = (P & 3) == 0 ? h16(W[wi]) : h16(W[wi] >> 16);
+  const float d = (P & 3) == 0 ? h16(W[wi]) : h16(W[wi] >> 16);
+  const uint64_t dd = f2(d, d);
   constexpr int qb = P + 2;  // first quant byte
   constexpr int qw = qb >> 2;
 #pragma unroll
   for (int i = 0; i < 8; i++) {
-    uint32_t q = (qb & 3) == 0 ? W[qw + i] : __byte_perm(W[qw + i], W[qw + i + 1], 0x5432);
-    dq8(q, d, o[2 * i], o[2 * i + 1]);
+    const uint32_t q = (qb & 3) == 0 ? W[qw + i] : __byte_perm(W[qw + i], W[qw + i + 1], 0x5432);
+    dq8(q, dd, o[2 * i], o[2 * i + 1]);
   }
 }
 
@@ -147,11 +177,11 @@ template <int WT>
 __global__ void __launch_bounds__(kThreads, 1)
     k_qgemm(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_r0,
             const __grid_constant__ CUtensorMap tm_r1, const Params p) {
-  constexpr int kSR = Cfg<WT>::kSR;
+  constexpr int kSR = Cfg<WT>::kSR, SX = Cfg<WT>::kSX;
   constexpr uint32_t kRawStage = TN * Cfg<WT>::kRawRow;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-  uint8_t* xs = smem;                                    // SX x 16 KB, 1024-aligned
+  uint8_t* xs = smem;                                    // SX x 32 KB, 1024-aligned
   uint8_t* rs = smem + SX * kXStageBytes;                // kSR raw stages
   uint64_t* bars = (uint64_t*)(rs + kSR * kRawStage);
   uint64_t* x_full = bars;
@@ -161,8 +191,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* a_full = r_empty + kSR;
   uint64_t* a_empty = a_full + SAT;
   uint64_t* acc_full = a_empty + SAT;
-  uint64_t* acc_empty = acc_full + 2;
-  uint32_t* tmem_slot = (uint32_t*)(acc_empty + 2);
+  uint64_t* acc_empty = acc_full + 1;
+  uint32_t* tmem_slot = (uint32_t*)(acc_empty + 1);
   volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -171,9 +201,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < SX; i++) { mbar_init(&x_full[i], 1); mbar_init(&x_empty[i], 1); }
-    for (int i = 0; i < kSR; i++) { mbar_init(&r_full[i], 1); mbar_init(&r_empty[i], 8); }
-    for (int i = 0; i < SAT; i++) { mbar_init(&a_full[i], 8); mbar_init(&a_empty[i], 1); }
-    for (int i = 0; i < 2; i++) { mbar_init(&acc_full[i], 1); mbar_init(&acc_empty[i], 4); }
+    for (int i = 0; i < kSR; i++) { mbar_init(&r_full[i], 1); mbar_init(&r_empty[i], kDW); }
+    for (int i = 0; i < SAT; i++) { mbar_init(&a_full[i], kDW); mbar_init(&a_empty[i], 1); }
+    mbar_init(acc_full, 1);
+    mbar_init(acc_empty, kEW);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -225,10 +256,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t it = 0, tcount = 0;
     bool ok = true;
     for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x, tcount++) {
-      const uint32_t buf = tcount & 1, pb = (tcount >> 1) & 1;
-      if (!(ok = mbar_wait(&acc_empty[buf], pb ^ 1, abort_flag, p.status, kDevTimeoutGemm))) break;
+      if (!(ok = mbar_wait(acc_empty, (tcount & 1) ^ 1, abort_flag, p.status, kDevTimeoutGemm))) break;
       tc_fence_after();
-      const uint32_t d_tmem = tmem + buf * TM;
       for (int ks = 0; ks < nks; ks++, it++) {
         const uint32_t sx = it % SX, px = (it / SX) & 1;
         const uint32_t sa = it % SAT, pa = (it / SAT) & 1;
@@ -240,7 +269,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int kk = 0; kk < BK / 16; kk++) {
             const uint64_t bdesc = sw128_desc(xaddr + kk * 32, 16, 1024);
-            umma_ts(d_tmem, tmem + kTmemA + sa * 32 + kk * 8, bdesc, idesc, (ks | kk) != 0);
+            umma_ts(tmem, tmem + kTmemA + sa * 32 + kk * 8, bdesc, idesc, (ks | kk) != 0);
           }
           umma_commit(&x_empty[sx]);
           umma_commit(&a_empty[sa]);
@@ -248,10 +277,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         __syncwarp();
       }
       if (!ok) break;
-      if (lane == 0) umma_commit(&acc_full[buf]);
+      if (lane == 0) umma_commit(acc_full);
       __syncwarp();
     }
-  } else if (warp < 10) {
+  } else if (warp < 2 + kDW) {
     // ------------------------------------------------ dequant: raw GGML -> bf16 -> TMEM
     const int q = warp & 3;               // TMEM lane quarter
     const int hh = (warp - 2) >> 2;       // K half of the stage (32 values)
@@ -275,11 +304,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           q4k_scale_min(2 * (ks & 3) + hh, h.y, h.z, h.w, sc, mm);
           const float d1 = d * (float)sc, m1 = dmin * (float)mm;
           const float c1 = -(d1 * 8388608.f);
+          const uint64_t D1 = f2(d1, d1), C1 = f2(c1, c1), M1 = f2(m1, m1);
           const uint32_t w[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
 #pragma unroll
           for (int i = 0; i < 8; i++) {
             const uint32_t nib = hh ? ((w[i] >> 4) & 0x0F0F0F0Fu) : (w[i] & 0x0F0F0F0Fu);
-            dq4(nib, d1, c1, m1, o[2 * i], o[2 * i + 1]);
+            dq4(nib, D1, C1, M1, o[2 * i], o[2 * i + 1]);
           }
         } else if (WT == MB_GGML_Q8_0) {
           const int off = (68 * ks) & 15;  // window offset of block 0 (0,4,8,12)
@@ -307,6 +337,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             o[4 * i] = v.x; o[4 * i + 1] = v.y; o[4 * i + 2] = v.z; o[4 * i + 3] = v.w;
           }
         }
+        // generic-proxy reads of this raw stage are ordered before the TMA that will refill it
+        fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) mbar_arrive(&r_empty[sr]);
         if (!(ok = mbar_wait(&a_empty[sa], pa ^ 1, abort_flag, p.status, kDevTimeoutGemm))) break;
@@ -319,27 +351,32 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else {
-    // ------------------------------------------------ epilogue
+    // ------------------------------------------------ epilogue (thread = output feature n)
     const int q = warp & 3;
+    const int ch = (warp - 2 - kDW) >> 2;  // which 128 of the tile's 256 activation rows
     const uint32_t lane_addr = (uint32_t)(q * 32) << 16;
     const GemmEpilogue& e = p.epi;
     uint32_t tcount = 0;
     bool ok = true;
     for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x, tcount++) {
-      const uint32_t buf = tcount & 1, pb = (tcount >> 1) & 1;
-      const int m0 = (tile % p.tiles_m) * TM, n0 = (tile / p.tiles_m) * TN;
+      const int m0 = (tile % p.tiles_m) * TM + ch * 128, n0 = (tile / p.tiles_m) * TN;
       const int n = n0 + q * 32 + lane;
-      if (!(ok = mbar_wait(&acc_full[buf], pb, abort_flag, p.status, kDevTimeoutGemm))) break;
+      if (!(ok = mbar_wait(acc_full, tcount & 1, abort_flag, p.status, kDevTimeoutGemm))) break;
       tc_fence_after();
       const bool nvalid = n < p.N;
       const float bias = (nvalid && e.bias) ? e.bias[n] : 0.f;
       const float gate = (nvalid && e.kind == MB_EPI_GATE_RESIDUAL) ? e.gate[n] : 0.f;
       const bool do_gelu = e.kind == MB_EPI_GELU_TANH && n >= e.gelu_from;
 #pragma unroll 1
-      for (int c = 0; c < TM / 32; c++) {
+      for (int c = 0; c < 4; c++) {
         uint32_t v[32];
-        tmem_ld32(tmem + lane_addr + buf * TM + c * 32, v);
+        tmem_ld32(tmem + lane_addr + ch * 128 + c * 32, v);
         tmem_wait_ld();
+        if (c == 3) {  // the accumulator is free as soon as the last columns are in registers
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(acc_empty);
+        }
         const int mb = m0 + c * 32;
         if (nvalid) {
 #pragma unroll
@@ -361,9 +398,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&acc_empty[buf]);
     }
   }
 

@@ -45,6 +45,56 @@ class FluxConfig:
         return c
 
 
+def tensor_specs(cfg: FluxConfig):
+    """(GGUF name, shape) of every tensor the model reads (flux/pipeline.rs:255-276 naming;
+    matrices are [out, in])."""
+    h, m, hd = cfg.hidden_size, cfg.mlp_hidden, cfg.hidden_size // cfg.num_heads
+    out = []
+
+    def lin(n, o, i):
+        out.append((n + ".weight", (o, i)))
+        out.append((n + ".bias", (o,)))
+    lin("img_in", h, cfg.in_channels)
+    lin("txt_in", h, cfg.context_in_dim)
+    lin("time_in.in_layer", h, 256)
+    lin("time_in.out_layer", h, h)
+    lin("vector_in.in_layer", h, cfg.vec_in_dim)
+    lin("vector_in.out_layer", h, h)
+    if cfg.guidance_embed:
+        lin("guidance_in.in_layer", h, 256)
+        lin("guidance_in.out_layer", h, h)
+    for i in range(cfg.depth):
+        p = f"double_blocks.{i}."
+        for s in ("img", "txt"):
+            lin(p + f"{s}_mod.lin", 6 * h, h)
+            lin(p + f"{s}_attn.qkv", 3 * h, h)
+            out.append((p + f"{s}_attn.norm.query_norm.scale", (hd,)))
+            out.append((p + f"{s}_attn.norm.key_norm.scale", (hd,)))
+            lin(p + f"{s}_attn.proj", h, h)
+            lin(p + f"{s}_mlp.0", m, h)
+            lin(p + f"{s}_mlp.2", h, m)
+    for i in range(cfg.depth_single_blocks):
+        p = f"single_blocks.{i}."
+        lin(p + "linear1", 3 * h + m, h)
+        lin(p + "linear2", h, h + m)
+        out.append((p + "norm.query_norm.scale", (hd,)))
+        out.append((p + "norm.key_norm.scale", (hd,)))
+        lin(p + "modulation.lin", 3 * h, h)
+    lin("final_layer.linear", cfg.in_channels, h)
+    lin("final_layer.adaLN_modulation.1", 2 * h, h)
+    return out
+
+
+def step_flops(cfg: FluxConfig, l_txt, l_img):
+    """Algorithmic FLOPs of one transformer forward (2 per MAC): linears + attention."""
+    h, m, H = cfg.hidden_size, cfg.mlp_hidden, cfg.num_heads
+    L = l_txt + l_img
+    dbl = 2 * L * h * (3 * h + h + m + m) + 4 * L * L * h
+    sgl = 2 * L * h * (3 * h + m) + 2 * L * (h + m) * h + 4 * L * L * h
+    stems = 2 * l_txt * cfg.context_in_dim * h + 2 * l_img * cfg.in_channels * h + 2 * l_img * h * cfg.in_channels
+    return cfg.depth * dbl + cfg.depth_single_blocks * sgl + stems
+
+
 class FluxTransformer:
     def __init__(self, cfg: FluxConfig, max_txt=512, max_img=4096, device=0):
         init(device)
