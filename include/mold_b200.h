@@ -110,6 +110,21 @@ MB_API mb_status mb_qlinear(const mb_weight* w, const void* x, int x_dtype, int6
                      int64_t ldy, const float* bias, int epilogue, int64_t gelu_from, const float* gate,
                      const float* residual, int64_t ldr, void* stream);
 
+/* Same as mb_qlinear with an f32 x, but allocates nothing. No counterpart in the
+ * reference: it is for callers that cannot let the library call cudaMalloc (code
+ * running during CUDA-graph capture, callers whose device memory comes from their
+ * own pool or arena, hosts that forbid allocation after start-up). The bf16 copy of
+ * x is staged in a fixed 8 MiB array in the library's device image (M * K must be
+ * <= 4,194,304; larger inputs are rejected with MB_ERR_INVALID); every GPU that
+ * loads the library holds that array until exit. mb_init must have been called on
+ * the device first (else MB_ERR_NOT_READY). The first call on a device looks up the
+ * array's device address, so make it before any stream capture. All calls on a
+ * device share the array: calls whose execution overlaps on the GPU race. */
+MB_API mb_status mb_qlinear_f32_static(const mb_weight* w, const float* x, int64_t M, int64_t ldx, void* y,
+                                       int y_dtype, int64_t ldy, const float* bias, int epilogue,
+                                       int64_t gelu_from, const float* gate, const float* residual, int64_t ldr,
+                                       void* stream);
+
 /* K3. Quantized GEMV for the modulation vectors: y[N] = W silu?(x)[K] + bias.
  * Replaces Modulation1/2::forward's silu(vec)->Linear (flux/offload.rs:117-156). */
 MB_API mb_status mb_qgemv(const mb_weight* w, const float* x, int apply_silu, const float* bias, float* y, void* stream);

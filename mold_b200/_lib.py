@@ -30,6 +30,7 @@ SIGNATURES = {
     "mb_dequant": (I32, [P, P, I32, P]),
     "mb_qlinear": (I32, [P, P, I32, I64, I64, P, I32, I64, P, I32, I64, P, P, I64, P]),
     "mb_qgemv": (I32, [P, P, I32, P, P, P]),
+    "mb_qlinear_f32_static": (I32, [P, P, I64, I64, P, I32, I64, P, I32, I64, P, P, I64, P]),
     "mb_ln_modulate": (I32, [P, I64, I64, I64, P, P, P, I64, P]),
     "mb_rope_table": (I32, [P, I64, I32, P, I32, P, P]),
     "mb_qk_norm_rope": (I32, [P, I64, I64, I32, P, P, P, I64, I64, P, P, P, P]),

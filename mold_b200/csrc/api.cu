@@ -23,6 +23,12 @@ int* device_status_ptr() {
   return g_status[dev];
 }
 
+bool device_status_ready() {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  return dev >= 0 && dev < 64 && g_status[dev] != nullptr;
+}
+
 static thread_local std::string t_last_error;
 
 mb_status set_error(mb_status s, const std::string& msg) {

@@ -33,7 +33,8 @@ mb_status cuda_error(cudaError_t e, const char* what);
   } while (0)
 
 int num_sms();
-int* device_status_ptr();  // per-device status word (allocated on first use)
+int* device_status_ptr();
+bool device_status_ready();  // true once mb_init allocated the status word on the current device  // per-device status word (allocated on first use)
 int64_t row_bytes_of(int ggml_type, int64_t n_cols);  // -1 if unsupported / not divisible
 bool ggml_type_supported(int ggml_type);
 
