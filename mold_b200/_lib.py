@@ -7,7 +7,7 @@ import ctypes
 import os
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(_HERE, "libmold_b200.so")
+LIB_PATH = os.environ.get("MOLD_B200_LIB") or os.path.join(_HERE, "libmold_b200.so")
 
 MB_OK, MB_ERR_INVALID, MB_ERR_UNSUPPORTED, MB_ERR_CUDA, MB_ERR_TIMEOUT, MB_ERR_NOMEM, MB_ERR_NOT_READY = range(7)
 GGML_F32, GGML_F16, GGML_Q8_0, GGML_Q4_K, GGML_BF16 = 0, 1, 8, 12, 30

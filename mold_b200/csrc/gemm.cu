@@ -12,9 +12,9 @@
 //     (TMA write + MMA read) plus the raw blocks.
 //   * X (activations, bf16, K-major) is TMA-loaded with the 128-byte swizzle into
 //     an 8-stage ring and read by tcgen05.mma as the B operand.
-//   * Raw weight bytes are TMA-loaded per 64-wide K stage (Q4_K: the 16-byte
-//     header + the 32 bytes of nibbles of that stage; Q8_0: the 80-byte window
-//     holding the stage's two 34-byte blocks; BF16: 128 bytes).
+//   * Raw weight bytes are TMA-loaded in their GGUF layout (Q4_K: whole 144-byte
+//     super-blocks, one TMA per 4 stages, scales decoded once per super-block; Q8_0:
+//     the 80-byte window holding a stage's two 34-byte blocks; BF16: 128 bytes).
 //   * Tile = 128 weight rows x 256 activation rows, so each decoded weight feeds
 //     256 MACs (the dequant rate needed is 16 values per SM clock at full MMA
 //     rate). TMEM: the 128x256 f32 accumulator in columns [0, 256) and an
@@ -51,15 +51,15 @@ template <int WT>
 struct Cfg;
 template <>
 struct Cfg<MB_GGML_Q4_K> {
-  static constexpr int kRawRow = 48, kSR = 8, kSX = 5;
+  static constexpr int kRawRow = 144, kSPC = 4, kSR = 3, kSX = 5;  // whole super-blocks
 };
 template <>
 struct Cfg<MB_GGML_Q8_0> {
-  static constexpr int kRawRow = 80, kSR = 6, kSX = 5;
+  static constexpr int kRawRow = 80, kSPC = 1, kSR = 6, kSX = 5;
 };
 template <>
 struct Cfg<MB_GGML_BF16> {
-  static constexpr int kRawRow = 128, kSR = 4, kSX = 5;
+  static constexpr int kRawRow = 128, kSPC = 1, kSR = 4, kSX = 5;
 };
 
 template <int WT>
@@ -72,7 +72,14 @@ struct Params {
   int tiles_m, tiles_n;
   GemmEpilogue epi;
   int* status;
+  int ablate;  // builds with -DMB_TRACE only: 1 decode, 2 X loads, 4 raw loads, 8 TMEM stores, 16 epilogue
 };
+
+#ifdef MB_TRACE
+#define ABL(bit) ((p.ablate & (bit)) != 0)
+#else
+#define ABL(bit) false
+#endif
 
 // ---- packed f32x2 arithmetic (sm_100): two IEEE single-precision ops per instruction ----
 MB_DEV uint64_t f2(float a, float b) {
@@ -177,7 +184,7 @@ template <int WT>
 __global__ void __launch_bounds__(kThreads, 1)
     k_qgemm(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_r0,
             const __grid_constant__ CUtensorMap tm_r1, const Params p) {
-  constexpr int kSR = Cfg<WT>::kSR, SX = Cfg<WT>::kSX;
+  constexpr int kSR = Cfg<WT>::kSR, SX = Cfg<WT>::kSX, kSPC = Cfg<WT>::kSPC;
   constexpr uint32_t kRawStage = TN * Cfg<WT>::kRawRow;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
@@ -215,7 +222,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tm_x);
     tma_prefetch_desc(&tm_r0);
-    if (WT == MB_GGML_Q4_K) tma_prefetch_desc(&tm_r1);
   }
   tc_fence_before();
   __syncthreads();
@@ -225,27 +231,36 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0) {
     // ------------------------------------------------ TMA producer
     if (lane == 0) {
-      uint32_t it = 0;
+      uint32_t it = 0, ic = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x) {
         const int m0 = (tile % p.tiles_m) * TM, n0 = (tile / p.tiles_m) * TN;
         for (int ks = 0; ks < nks && ok; ks++, it++) {
           const uint32_t sx = it % SX, px = (it / SX) & 1;
           if (!(ok = mbar_wait(&x_empty[sx], px ^ 1, abort_flag, p.status, kDevTimeoutGemm))) break;
-          mbar_expect_tx(&x_full[sx], kXStageBytes);
-          tma_load_2d(xs + sx * kXStageBytes, &tm_x, &x_full[sx], ks * BK, m0);
-          const uint32_t sr = it % kSR, pr = (it / kSR) & 1;
-          if (!(ok = mbar_wait(&r_empty[sr], pr ^ 1, abort_flag, p.status, kDevTimeoutGemm))) break;
-          mbar_expect_tx(&r_full[sr], kRawStage);
-          uint8_t* rdst = rs + sr * kRawStage;
-          if (WT == MB_GGML_Q4_K) {
-            const int kb = ks >> 2, g = ks & 3;
-            tma_load_2d(rdst, &tm_r0, &r_full[sr], kb * 144, n0);
-            tma_load_2d(rdst + TN * 16, &tm_r1, &r_full[sr], kb * 144 + 16 + 32 * g, n0);
-          } else if (WT == MB_GGML_Q8_0) {
-            tma_load_2d(rdst, &tm_r0, &r_full[sr], (68 * ks) & ~15, n0);
+          if (ABL(2)) {
+            mbar_arrive(&x_full[sx]);
           } else {
-            tma_load_2d(rdst, &tm_r0, &r_full[sr], ks * 128, n0);
+            mbar_expect_tx(&x_full[sx], kXStageBytes);
+            tma_load_2d(xs + sx * kXStageBytes, &tm_x, &x_full[sx], ks * BK, m0);
+          }
+          if (ks % kSPC == 0) {  // one raw chunk (kSPC stages) per 128-row weight block
+            const uint32_t sr = ic % kSR, pr = (ic / kSR) & 1;
+            ic++;
+            if (!(ok = mbar_wait(&r_empty[sr], pr ^ 1, abort_flag, p.status, kDevTimeoutGemm))) break;
+            if (ABL(4)) {
+              mbar_arrive(&r_full[sr]);
+              continue;
+            }
+            mbar_expect_tx(&r_full[sr], kRawStage);
+            uint8_t* rdst = rs + sr * kRawStage;
+            if (WT == MB_GGML_Q4_K) {
+              tma_load_2d(rdst, &tm_r0, &r_full[sr], (ks >> 2) * 144, n0);
+            } else if (WT == MB_GGML_Q8_0) {
+              tma_load_2d(rdst, &tm_r0, &r_full[sr], (68 * ks) & ~15, n0);
+            } else {
+              tma_load_2d(rdst, &tm_r0, &r_full[sr], ks * 128, n0);
+            }
           }
         }
       }
@@ -286,68 +301,88 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int hh = (warp - 2) >> 2;       // K half of the stage (32 values)
     const int r = q * 32 + lane;          // weight row within the tile == TMEM lane
     const uint32_t lane_addr = (uint32_t)(q * 32) << 16;
-    uint32_t it = 0;
+    uint32_t it = 0, ic = 0;
     bool ok = true;
     for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x) {
-      for (int ks = 0; ks < nks; ks++, it++) {
-        const uint32_t sr = it % kSR, pr = (it / kSR) & 1;
-        const uint32_t sa = it % SAT, pa = (it / SAT) & 1;
+      for (int kc = 0; kc < nks / kSPC && ok; kc++, ic++) {
+        const uint32_t sr = ic % kSR, pr = (ic / kSR) & 1;
         if (!(ok = mbar_wait(&r_full[sr], pr, abort_flag, p.status, kDevTimeoutGemm))) break;
         const uint8_t* R = rs + sr * kRawStage;
-        uint32_t o[16];
+        // Q4_K: this thread's four sub-blocks (2j + hh, j = 0..3) of the super-block, decoded once.
+        // High nibbles (hh = 1) are used in place (16 q) with the scale divided by 16: still exact.
+        float d1v[kSPC], m1v[kSPC];
         if (WT == MB_GGML_Q4_K) {
-          const uint4 h = *(const uint4*)(R + r * 16);
-          const uint4* qp = (const uint4*)(R + TN * 16 + r * 32);
-          const uint4 qa = qp[0], qb = qp[1];
+          const uint4 h = *(const uint4*)(R + r * 144);
           const float d = h16(h.x), dmin = h16(h.x >> 16);
-          int sc, mm;
-          q4k_scale_min(2 * (ks & 3) + hh, h.y, h.z, h.w, sc, mm);
-          const float d1 = d * (float)sc, m1 = dmin * (float)mm;
-          const float c1 = -(d1 * 8388608.f);
-          const uint64_t D1 = f2(d1, d1), C1 = f2(c1, c1), M1 = f2(m1, m1);
-          const uint32_t w[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
 #pragma unroll
-          for (int i = 0; i < 8; i++) {
-            const uint32_t nib = hh ? ((w[i] >> 4) & 0x0F0F0F0Fu) : (w[i] & 0x0F0F0F0Fu);
-            dq4(nib, D1, C1, M1, o[2 * i], o[2 * i + 1]);
-          }
-        } else if (WT == MB_GGML_Q8_0) {
-          const int off = (68 * ks) & 15;  // window offset of block 0 (0,4,8,12)
-          const int base16 = hh ? 32 : 0;  // 16-aligned start of the 48-byte window
-          const uint4* src = (const uint4*)(R + r * 80 + base16);
-          const uint4 a0 = src[0], a1 = src[1], a2 = src[2];
-          const uint32_t W[12] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w, a2.x, a2.y, a2.z, a2.w};
-          // block start within the window: hh=0 -> off ; hh=1 -> off + 34 - 32
-          const int P = hh ? off + 2 : off;
-          switch (P) {
-            case 0: q8_block<0>(W, o); break;
-            case 4: q8_block<4>(W, o); break;
-            case 8: q8_block<8>(W, o); break;
-            case 12: q8_block<12>(W, o); break;
-            case 2: q8_block<2>(W, o); break;
-            case 6: q8_block<6>(W, o); break;
-            case 10: q8_block<10>(W, o); break;
-            default: q8_block<14>(W, o); break;
-          }
-        } else {
-          const uint4* src = (const uint4*)(R + r * 128 + hh * 64);
-#pragma unroll
-          for (int i = 0; i < 4; i++) {
-            const uint4 v = src[i];
-            o[4 * i] = v.x; o[4 * i + 1] = v.y; o[4 * i + 2] = v.z; o[4 * i + 3] = v.w;
+          for (int j = 0; j < kSPC; j++) {
+            int sc, mm;
+            q4k_scale_min(2 * j + hh, h.y, h.z, h.w, sc, mm);
+            d1v[j] = d * (float)sc;
+            m1v[j] = dmin * (float)mm;
+            if (hh) d1v[j] *= 0.0625f;
           }
         }
-        // generic-proxy reads of this raw stage are ordered before the TMA that will refill it
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&r_empty[sr]);
-        if (!(ok = mbar_wait(&a_empty[sa], pa ^ 1, abort_flag, p.status, kDevTimeoutGemm))) break;
-        tc_fence_after();
-        tmem_st16(tmem + lane_addr + kTmemA + sa * 32 + hh * 16, o);
-        tmem_wait_st();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&a_full[sa]);
+#pragma unroll
+        for (int j = 0; j < kSPC; j++, it++) {
+          const int ks = kc * kSPC + j;
+          const uint32_t sa = it % SAT, pa = (it / SAT) & 1;
+          uint32_t o[16];
+          if (ABL(1)) {
+#pragma unroll
+            for (int i = 0; i < 16; i++) o[i] = 0x3c003c00u ^ (uint32_t)(ks + i);
+          } else if (WT == MB_GGML_Q4_K) {
+            const uint4* qp = (const uint4*)(R + r * 144 + 16 + 32 * j);
+            const uint4 qa = qp[0], qb = qp[1];
+            const float d1 = d1v[j], m1 = m1v[j];
+            const float c1 = -(d1 * 8388608.f);
+            const uint64_t D1 = f2(d1, d1), C1 = f2(c1, c1), M1 = f2(m1, m1);
+            const uint32_t mask = hh ? 0xF0F0F0F0u : 0x0F0F0F0Fu;
+            const uint32_t w[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+#pragma unroll
+            for (int i = 0; i < 8; i++) dq4(w[i] & mask, D1, C1, M1, o[2 * i], o[2 * i + 1]);
+          } else if (WT == MB_GGML_Q8_0) {
+            const int off = (68 * ks) & 15;  // window offset of block 0 (0,4,8,12)
+            const int base16 = hh ? 32 : 0;  // 16-aligned start of the 48-byte window
+            const uint4* src = (const uint4*)(R + r * 80 + base16);
+            const uint4 a0 = src[0], a1 = src[1], a2 = src[2];
+            const uint32_t W[12] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w, a2.x, a2.y, a2.z, a2.w};
+            // block start within the window: hh=0 -> off ; hh=1 -> off + 34 - 32
+            const int P = hh ? off + 2 : off;
+            switch (P) {
+              case 0: q8_block<0>(W, o); break;
+              case 4: q8_block<4>(W, o); break;
+              case 8: q8_block<8>(W, o); break;
+              case 12: q8_block<12>(W, o); break;
+              case 2: q8_block<2>(W, o); break;
+              case 6: q8_block<6>(W, o); break;
+              case 10: q8_block<10>(W, o); break;
+              default: q8_block<14>(W, o); break;
+            }
+          } else {
+            const uint4* src = (const uint4*)(R + r * 128 + hh * 64);
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+              const uint4 v = src[i];
+              o[4 * i] = v.x; o[4 * i + 1] = v.y; o[4 * i + 2] = v.z; o[4 * i + 3] = v.w;
+            }
+          }
+          if (j == kSPC - 1) {
+            // generic-proxy reads of this raw chunk are ordered before the TMA that will refill it
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&r_empty[sr]);
+          }
+          if (!(ok = mbar_wait(&a_empty[sa], pa ^ 1, abort_flag, p.status, kDevTimeoutGemm))) break;
+          tc_fence_after();
+          if (!ABL(8)) {
+            tmem_st16(tmem + lane_addr + kTmemA + sa * 32 + hh * 16, o);
+            tmem_wait_st();
+          }
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&a_full[sa]);
+        }
       }
     }
   } else {
@@ -367,32 +402,76 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float bias = (nvalid && e.bias) ? e.bias[n] : 0.f;
       const float gate = (nvalid && e.kind == MB_EPI_GATE_RESIDUAL) ? e.gate[n] : 0.f;
       const bool do_gelu = e.kind == MB_EPI_GELU_TANH && n >= e.gelu_from;
-#pragma unroll 1
-      for (int c = 0; c < 4; c++) {
-        uint32_t v[32];
-        tmem_ld32(tmem + lane_addr + ch * 128 + c * 32, v);
-        tmem_wait_ld();
-        if (c == 3) {  // the accumulator is free as soon as the last columns are in registers
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(acc_empty);
-        }
-        const int mb = m0 + c * 32;
-        if (nvalid) {
+      const bool fast_bf16 = e.out_bf16 && e.kind != MB_EPI_GATE_RESIDUAL && (p.N & 1) == 0;
+      if (ABL(16)) {
+        __syncwarp();
+        if (lane == 0) mbar_arrive(acc_empty);
+      } else if (fast_bf16) {
+        // bf16 output: pull the warp's 128 accumulator columns into registers as packed bf16
+        // pairs (rows m, m+1 of feature n), free the accumulator, then store 32-bit words:
+        // lanes 2j / 2j+1 exchange halves so each writes features (n, n+1) of one row.
+        uint32_t pk[64];
 #pragma unroll
-          for (int i = 0; i < 32; i++) {
-            const int m = mb + i;
-            if (m < p.M) {
-              float a = __uint_as_float(v[i]) + bias;
-              if (e.kind == MB_EPI_GATE_RESIDUAL) {
-                const float rv = e.res[(int64_t)m * e.ldr + n];
-                ((float*)e.y)[(int64_t)m * e.ldy + n] = rv + gate * a;
-              } else {
-                if (do_gelu) a = gelu_tanh(a);
-                if (e.out_bf16)
-                  ((__nv_bfloat16*)e.y)[(int64_t)m * e.ldy + n] = __float2bfloat16_rn(a);
-                else
-                  ((float*)e.y)[(int64_t)m * e.ldy + n] = a;
+        for (int c = 0; c < 4; c++) {
+          uint32_t v[32];
+          tmem_ld32(tmem + lane_addr + ch * 128 + c * 32, v);
+          tmem_wait_ld();
+#pragma unroll
+          for (int j = 0; j < 16; j++) {
+            float a0 = __uint_as_float(v[2 * j]) + bias, a1 = __uint_as_float(v[2 * j + 1]) + bias;
+            if (do_gelu) {
+              a0 = gelu_tanh(a0);
+              a1 = gelu_tanh(a1);
+            }
+            pk[c * 16 + j] = pack_bf16x2(a0, a1);
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(acc_empty);
+        const bool odd = lane & 1;
+        const int ncol = n - (odd ? 1 : 0);  // even feature of the pair this lane writes
+#pragma unroll
+        for (int c = 0; c < 4; c++) {
+#pragma unroll
+          for (int j = 0; j < 16; j++) {
+            const uint32_t r = pk[c * 16 + j];
+            const uint32_t r2 = __shfl_xor_sync(0xffffffffu, r, 1);
+            // even lane: (own lo, partner lo) = row m ; odd lane: (partner hi, own hi) = row m + 1
+            const uint32_t wv = odd ? __byte_perm(r2, r, 0x7632) : __byte_perm(r, r2, 0x5410);
+            const int m = m0 + c * 32 + 2 * j + (odd ? 1 : 0);
+            if (m < p.M && ncol < p.N)
+              *(uint32_t*)((__nv_bfloat16*)e.y + (int64_t)m * e.ldy + ncol) = wv;
+          }
+        }
+      } else {
+#pragma unroll 1
+        for (int c = 0; c < 4; c++) {
+          uint32_t v[32];
+          tmem_ld32(tmem + lane_addr + ch * 128 + c * 32, v);
+          tmem_wait_ld();
+          if (c == 3) {  // the accumulator is free as soon as the last columns are in registers
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(acc_empty);
+          }
+          const int mb = m0 + c * 32;
+          if (nvalid) {
+#pragma unroll
+            for (int i = 0; i < 32; i++) {
+              const int m = mb + i;
+              if (m < p.M) {
+                float a = __uint_as_float(v[i]) + bias;
+                if (e.kind == MB_EPI_GATE_RESIDUAL) {
+                  const float rv = e.res[(int64_t)m * e.ldr + n];
+                  ((float*)e.y)[(int64_t)m * e.ldy + n] = rv + gate * a;
+                } else {
+                  if (do_gelu) a = gelu_tanh(a);
+                  if (e.out_bf16)
+                    ((__nv_bfloat16*)e.y)[(int64_t)m * e.ldy + n] = __float2bfloat16_rn(a);
+                  else
+                    ((float*)e.y)[(int64_t)m * e.ldy + n] = a;
+                }
               }
             }
           }
@@ -409,6 +488,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+int g_gemm_ablate = 0;
+
 template <int WT>
 cudaError_t launch_t(const mb_weight* w, const void* x, int64_t M, int64_t ldx, const GemmEpilogue& epi,
                      cudaStream_t st) {
@@ -417,16 +498,10 @@ cudaError_t launch_t(const mb_weight* w, const void* x, int64_t M, int64_t ldx, 
                     BK, TM, CU_TENSOR_MAP_SWIZZLE_128B))
     return cudaErrorInvalidValue;
   const uint64_t rb = (uint64_t)w->row_bytes, nr = (uint64_t)w->n_rows;
-  if (WT == MB_GGML_Q4_K) {
-    if (!make_tmap_2d(&tr0, w->dev, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, rb, nr, rb, 16, TN, CU_TENSOR_MAP_SWIZZLE_NONE) ||
-        !make_tmap_2d(&tr1, w->dev, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, rb, nr, rb, 32, TN, CU_TENSOR_MAP_SWIZZLE_NONE))
-      return cudaErrorInvalidValue;
-  } else {
-    const uint32_t box = WT == MB_GGML_Q8_0 ? 80 : 128;
-    if (!make_tmap_2d(&tr0, w->dev, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, rb, nr, rb, box, TN, CU_TENSOR_MAP_SWIZZLE_NONE))
-      return cudaErrorInvalidValue;
-    tr1 = tr0;
-  }
+  const uint32_t box = WT == MB_GGML_Q4_K ? 144 : (WT == MB_GGML_Q8_0 ? 80 : 128);
+  if (!make_tmap_2d(&tr0, w->dev, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, rb, nr, rb, box, TN, CU_TENSOR_MAP_SWIZZLE_NONE))
+    return cudaErrorInvalidValue;
+  tr1 = tr0;
   Params p;
   p.M = (int)M;
   p.N = (int)w->n_rows;
@@ -435,6 +510,7 @@ cudaError_t launch_t(const mb_weight* w, const void* x, int64_t M, int64_t ldx, 
   p.tiles_n = (int)((w->n_rows + TN - 1) / TN);
   p.epi = epi;
   p.status = device_status_ptr();
+  p.ablate = g_gemm_ablate;
   const int tiles = p.tiles_m * p.tiles_n;
   const int grid = tiles < num_sms() ? tiles : num_sms();
   constexpr size_t smem = smem_bytes<WT>();
@@ -451,6 +527,10 @@ cudaError_t launch_t(const mb_weight* w, const void* x, int64_t M, int64_t ldx, 
 }
 
 }  // namespace gemm
+
+#ifdef MB_TRACE
+extern "C" __attribute__((visibility("default"))) void mb_debug_set_gemm_ablate(int flags) { gemm::g_gemm_ablate = flags; }
+#endif
 
 cudaError_t launch_qgemm(const mb_weight* w, const void* x_bf16, int64_t M, int64_t ldx, const GemmEpilogue& epi,
                          cudaStream_t st) {
