@@ -19,6 +19,8 @@
 //                           input of single-block linear2 (and [3h, 3h+m) of double-block mlp.2)
 //   q,k,v bf16 [H, L, 128]  attention layout written by the fused QK-norm/RoPE kernel
 //   pe  f32  [L, 64, 2, 2]  RoPE table (computed once per denoise call)
+#include <cstdio>
+#include <cstdlib>
 #include <map>
 #include <string>
 #include <vector>
@@ -57,6 +59,43 @@ __global__ void k_step_prologue(const double* sched, int* counter, float* scal) 
 struct Seg {  // a row range of the joint sequence
   int64_t row0, rows;
 };
+
+// Opt-in per-op timing of an eager forward (MOLD_B200_PROFILE=1): CUDA events around every
+// launch, summed per op category and printed to stderr. Off by default; never inside a graph.
+struct OpProfiler {
+  std::vector<std::pair<std::string, std::pair<cudaEvent_t, cudaEvent_t>>> ev;
+  void begin(cudaStream_t st) {
+    cudaEvent_t a, b;
+    cudaEventCreate(&a);
+    cudaEventCreate(&b);
+    cudaEventRecord(a, st);
+    ev.push_back({"", {a, b}});
+  }
+  void end(cudaStream_t st, const std::string& cat) {
+    ev.back().first = cat;
+    cudaEventRecord(ev.back().second.second, st);
+  }
+  void report() {
+    cudaDeviceSynchronize();
+    std::map<std::string, std::pair<int, double>> agg;
+    double tot = 0;
+    for (auto& e : ev) {
+      float ms = 0;
+      cudaEventElapsedTime(&ms, e.second.first, e.second.second);
+      agg[e.first].first++;
+      agg[e.first].second += ms;
+      tot += ms;
+      cudaEventDestroy(e.second.first);
+      cudaEventDestroy(e.second.second);
+    }
+    fprintf(stderr, "[mold_b200 profile] %zu launches, %.3f ms of kernel time\n", ev.size(), tot);
+    for (auto& a : agg)
+      fprintf(stderr, "[mold_b200 profile] %-28s %5d launches %9.3f ms %5.1f%%\n", a.first.c_str(), a.second.first,
+              a.second.second, 100.0 * a.second.second / tot);
+    ev.clear();
+  }
+};
+OpProfiler* g_prof = nullptr;
 
 }  // namespace
 
@@ -164,6 +203,13 @@ mb_status check_launch(cudaError_t e, const char* what) {
     mb_status s__ = (expr);          \
     if (s__ != MB_OK) return s__;    \
   } while (0)
+#define TIMED(cat, expr)               \
+  do {                                 \
+    if (g_prof) g_prof->begin(st);     \
+    mb_status s__ = (expr);            \
+    if (s__ != MB_OK) return s__;      \
+    if (g_prof) g_prof->end(st, cat);  \
+  } while (0)
 
 const mb_weight* W(const mb_flux* m, const std::string& n) { return m->mats.at(n); }
 const float* B(const mb_flux* m, const std::string& n) { return m->vecs.at(n).dev; }
@@ -180,7 +226,15 @@ mb_status linear(const mb_flux* m, const std::string& name, const void* x, int64
   e.gate = gate;
   e.res = (const float*)y;
   e.ldr = ldy;
-  return check_launch(launch_qgemm(W(m, name + ".weight"), x, M, ldx, e, st), name.c_str());
+  if (g_prof) g_prof->begin(st);
+  mb_status s = check_launch(launch_qgemm(W(m, name + ".weight"), x, M, ldx, e, st), name.c_str());
+  if (g_prof) {
+    std::string role = name;
+    const size_t d = role.find("blocks.");
+    if (d != std::string::npos) role = role.substr(role.find('.', d + 7) + 1);
+    g_prof->end(st, "gemm " + role + " M=" + std::to_string(M));
+  }
+  return s;
 }
 
 // Builds the three GEMV job tables: [0] stem in_layers, [1] stem out_layers, [2] all modulations.
@@ -201,7 +255,7 @@ mb_status finalize(mb_flux* m) {
     j.x_slot = slot;
     const int id = (int)jobs.size();
     jobs.push_back(j);
-    for (int r = 0; r < j.n_rows; r += 8) {
+    for (int r = 0; r < j.n_rows; r += kGemvRowsPerBlock) {
       blocks.push_back(id);
       blocks.push_back(r);
     }
@@ -266,9 +320,9 @@ mb_status run_forward(mb_flux* m, const float* img, int64_t Li, const float* txt
   const int64_t h = m->h(), H = m->H(), mh = m->mh(), L = Lt + Li, ldY = m->ldY();
   const mb_flux_config& c = m->cfg;
   // ---- conditioning vector: temb(t), temb(g), y -> stem MLPs -> all modulations
-  MB_TRY(check_launch(launch_timestep_embedding(m->scal, 1000.f, m->temb, 256, st), "temb t"));
+  TIMED("timestep_embedding", check_launch(launch_timestep_embedding(m->scal, 1000.f, m->temb, 256, st), "temb t"));
   if (c.guidance_embed)
-    MB_TRY(check_launch(launch_timestep_embedding(m->scal + 1, 1000.f, m->temb + 256, 256, st), "temb g"));
+    TIMED("timestep_embedding", check_launch(launch_timestep_embedding(m->scal + 1, 1000.f, m->temb + 256, 256, st), "temb g"));
   {
     GemvInput in[3] = {};
     in[0].parts[0] = m->temb;
@@ -277,12 +331,12 @@ mb_status run_forward(mb_flux* m, const float* img, int64_t Li, const float* txt
     in[1].n_parts = 1;
     in[2].parts[0] = y;
     in[2].n_parts = 1;
-    MB_TRY(gemv_table(m, 0, in, 3, 4096, st));
+    TIMED("gemv stems", gemv_table(m, 0, in, 3, 4096, st));
     for (int i = 0; i < 3; i++) {
       in[i].parts[0] = m->hid + i * h;
       in[i].apply_silu = 1;
     }
-    MB_TRY(gemv_table(m, 1, in, 3, 4096, st));
+    TIMED("gemv stems", gemv_table(m, 1, in, 3, 4096, st));
     GemvInput v = {};
     v.parts[0] = m->parts;
     v.parts[1] = m->parts + 2 * h;
@@ -292,13 +346,13 @@ mb_status run_forward(mb_flux* m, const float* img, int64_t Li, const float* txt
       v.n_parts = 3;
     }
     v.apply_silu = 1;
-    MB_TRY(gemv_table(m, 2, &v, 1, 4096, st));
+    TIMED("gemv modulations", gemv_table(m, 2, &v, 1, 4096, st));
   }
   // ---- stems: txt_in, img_in into the residual stream
-  MB_TRY(check_launch(launch_cast_f32_bf16(txt, Lt, c.context_in_dim, c.context_in_dim, m->txt_bf, c.context_in_dim, st),
+  TIMED("cast_f32_bf16", check_launch(launch_cast_f32_bf16(txt, Lt, c.context_in_dim, c.context_in_dim, m->txt_bf, c.context_in_dim, st),
                       "cast txt"));
   MB_TRY(linear(m, "txt_in", m->txt_bf, Lt, c.context_in_dim, m->x, h, false, MB_EPI_NONE, 0, nullptr, st));
-  MB_TRY(check_launch(launch_cast_f32_bf16(img, Li, c.in_channels, c.in_channels, m->img_bf, c.in_channels, st),
+  TIMED("cast_f32_bf16", check_launch(launch_cast_f32_bf16(img, Li, c.in_channels, c.in_channels, m->img_bf, c.in_channels, st),
                       "cast img"));
   MB_TRY(linear(m, "img_in", m->img_bf, Li, c.in_channels, m->x + Lt * h, h, false, MB_EPI_NONE, 0, nullptr, st));
 
@@ -311,17 +365,17 @@ mb_status run_forward(mb_flux* m, const float* img, int64_t Li, const float* txt
       const Seg g = segs[s];
       const std::string S = s == 0 ? "txt" : "img";
       const float* mo = md + (s == 0 ? 6 * h : 0);  // img_mod first, then txt_mod
-      MB_TRY(check_launch(launch_ln_modulate(m->x + g.row0 * h, g.rows, h, h, mo, mo + h, m->xm + g.row0 * h, h, st),
+      TIMED("ln_modulate", check_launch(launch_ln_modulate(m->x + g.row0 * h, g.rows, h, h, mo, mo + h, m->xm + g.row0 * h, h, st),
                           "ln_mod1"));
       MB_TRY(linear(m, p + S + "_attn.qkv", m->xm + g.row0 * h, g.rows, h, m->Y + g.row0 * ldY, ldY, true,
                     MB_EPI_NONE, 0, nullptr, st));
-      MB_TRY(check_launch(launch_qk_norm_rope(m->Y + g.row0 * ldY, g.rows, ldY, (int)H,
+      TIMED("qk_norm_rope", check_launch(launch_qk_norm_rope(m->Y + g.row0 * ldY, g.rows, ldY, (int)H,
                                               B(m, p + S + "_attn.norm.query_norm.scale"),
                                               B(m, p + S + "_attn.norm.key_norm.scale"), m->pe, g.row0, L, m->q, m->k,
                                               m->v, st),
                           "qk_norm_rope"));
     }
-    MB_TRY(check_launch(launch_attention(m->q, m->k, m->v, (int)H, L, L, L, m->Y + 2 * h, ldY, st), "attention"));
+    TIMED("attention", check_launch(launch_attention(m->q, m->k, m->v, (int)H, L, L, L, m->Y + 2 * h, ldY, st), "attention"));
     for (int s = 0; s < 2; s++) {
       const Seg g = segs[s];
       const std::string S = s == 0 ? "txt" : "img";
@@ -329,7 +383,7 @@ mb_status run_forward(mb_flux* m, const float* img, int64_t Li, const float* txt
       float* xr = m->x + g.row0 * h;
       MB_TRY(linear(m, p + S + "_attn.proj", m->Y + g.row0 * ldY + 2 * h, g.rows, ldY, xr, h, false,
                     MB_EPI_GATE_RESIDUAL, 0, mo + 2 * h, st));
-      MB_TRY(check_launch(launch_ln_modulate(xr, g.rows, h, h, mo + 3 * h, mo + 4 * h, m->xm + g.row0 * h, h, st),
+      TIMED("ln_modulate", check_launch(launch_ln_modulate(xr, g.rows, h, h, mo + 3 * h, mo + 4 * h, m->xm + g.row0 * h, h, st),
                           "ln_mod2"));
       MB_TRY(linear(m, p + S + "_mlp.0", m->xm + g.row0 * h, g.rows, h, m->Y + g.row0 * ldY + 3 * h, ldY, true,
                     MB_EPI_GELU_TANH, 0, nullptr, st));
@@ -341,18 +395,18 @@ mb_status run_forward(mb_flux* m, const float* img, int64_t Li, const float* txt
   for (int i = 0; i < c.depth_single; i++) {
     const std::string p = "single_blocks." + std::to_string(i) + ".";
     const float* mo = m->mods + m->mod_off_single[i];
-    MB_TRY(check_launch(launch_ln_modulate(m->x, L, h, h, mo, mo + h, m->xm, h, st), "ln_mod"));
+    TIMED("ln_modulate", check_launch(launch_ln_modulate(m->x, L, h, h, mo, mo + h, m->xm, h, st), "ln_mod"));
     MB_TRY(linear(m, p + "linear1", m->xm, L, h, m->Y, ldY, true, MB_EPI_GELU_TANH, 3 * h, nullptr, st));
-    MB_TRY(check_launch(launch_qk_norm_rope(m->Y, L, ldY, (int)H, B(m, p + "norm.query_norm.scale"),
+    TIMED("qk_norm_rope", check_launch(launch_qk_norm_rope(m->Y, L, ldY, (int)H, B(m, p + "norm.query_norm.scale"),
                                             B(m, p + "norm.key_norm.scale"), m->pe, 0, L, m->q, m->k, m->v, st),
                         "qk_norm_rope"));
-    MB_TRY(check_launch(launch_attention(m->q, m->k, m->v, (int)H, L, L, L, m->Y + 2 * h, ldY, st), "attention"));
+    TIMED("attention", check_launch(launch_attention(m->q, m->k, m->v, (int)H, L, L, L, m->Y + 2 * h, ldY, st), "attention"));
     MB_TRY(linear(m, p + "linear2", m->Y + 2 * h, L, ldY, m->x, h, false, MB_EPI_GATE_RESIDUAL, 0, mo + 2 * h, st));
   }
   // ---- final layer on the img rows
   {
     const float* mo = m->mods + m->mod_off_final;
-    MB_TRY(check_launch(launch_ln_modulate(m->x + Lt * h, Li, h, h, mo, mo + h, m->xm + Lt * h, h, st), "ln_final"));
+    TIMED("ln_modulate", check_launch(launch_ln_modulate(m->x + Lt * h, Li, h, h, mo, mo + h, m->xm + Lt * h, h, st), "ln_final"));
     MB_TRY(linear(m, "final_layer.linear", m->xm + Lt * h, Li, h, m->pred, c.in_channels, false, MB_EPI_NONE, 0,
                   nullptr, st));
   }
@@ -523,7 +577,15 @@ mb_status mb_flux_forward(mb_flux* m, const float* img, const float* img_ids, in
   cudaStream_t st = (cudaStream_t)stream;
   MB_TRY(prepare(m, img_ids, L_img, txt_ids, L_txt, st));
   k_set_scalars<<<1, 1, 0, st>>>(m->scal, t, guidance);
-  MB_TRY(run_forward(m, img, L_img, txt, L_txt, y, st));
+  const char* pe = getenv("MOLD_B200_PROFILE");
+  OpProfiler prof;
+  if (pe && pe[0] == '1') g_prof = &prof;
+  mb_status fs = run_forward(m, img, L_img, txt, L_txt, y, st);
+  if (g_prof) {
+    g_prof = nullptr;
+    prof.report();
+  }
+  MB_TRY(fs);
   MB_CUDA(cudaMemcpyAsync(pred, m->pred, L_img * m->cfg.in_channels * sizeof(float), cudaMemcpyDeviceToDevice, st));
   return MB_OK;
 }

@@ -444,6 +444,42 @@ __global__ void __launch_bounds__(kThreads, 1)
               *(uint32_t*)((__nv_bfloat16*)e.y + (int64_t)m * e.ldy + ncol) = wv;
           }
         }
+      } else if (e.kind == MB_EPI_GATE_RESIDUAL) {
+        // f32 residual output: u = gate * (acc + bias) is pulled out of TMEM as packed bf16
+        // pairs (rows m, m+1), the accumulator is freed, then y = residual + u in f32.
+        uint32_t pk[64];
+#pragma unroll
+        for (int c = 0; c < 4; c++) {
+          uint32_t v[32];
+          tmem_ld32(tmem + lane_addr + ch * 128 + c * 32, v);
+          tmem_wait_ld();
+#pragma unroll
+          for (int j = 0; j < 16; j++)
+            pk[c * 16 + j] = pack_bf16x2(gate * (__uint_as_float(v[2 * j]) + bias),
+                                         gate * (__uint_as_float(v[2 * j + 1]) + bias));
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(acc_empty);
+        if (nvalid) {
+          // y usually aliases res: issue a batch of 16 residual loads before any store so
+          // their latencies overlap (the compiler cannot reorder loads past aliasing stores).
+#pragma unroll
+          for (int c = 0; c < 8; c++) {
+            float rv[16];
+#pragma unroll
+            for (int i = 0; i < 16; i++) {
+              const int m = m0 + c * 16 + i;
+              rv[i] = m < p.M ? e.res[(int64_t)m * e.ldr + n] : 0.f;
+            }
+#pragma unroll
+            for (int i = 0; i < 16; i++) {
+              const int m = m0 + c * 16 + i;
+              const uint32_t r = pk[c * 8 + (i >> 1)];
+              if (m < p.M) ((float*)e.y)[(int64_t)m * e.ldy + n] = rv[i] + ((i & 1) ? bf16_hi(r) : bf16_lo(r));
+            }
+          }
+        }
       } else {
 #pragma unroll 1
         for (int c = 0; c < 4; c++) {

@@ -10,7 +10,8 @@
 namespace mb {
 namespace gemv {
 
-constexpr int kWarps = 8;  // rows per block
+constexpr int kWarps = 8;
+constexpr int kRowsPerWarp = 4;
 constexpr int kMaxLen = 4096;
 
 struct Inputs {
@@ -19,89 +20,146 @@ struct Inputs {
 
 MB_DEV float h16(uint32_t v) { return __half2float(__ushort_as_half((unsigned short)(v & 0xFFFFu))); }
 
+MB_DEV uint32_t sb(uint32_t sy, uint32_t sz, uint32_t sw, int k) {
+  const uint32_t w = k < 4 ? sy : (k < 8 ? sz : sw);
+  return (w >> ((k & 3) * 8)) & 0xFFu;
+}
+MB_DEV void q4k_sm(int j, uint32_t sy, uint32_t sz, uint32_t sw, int& sc, int& m) {
+  if (j < 4) {
+    sc = sb(sy, sz, sw, j) & 63;
+    m = sb(sy, sz, sw, j + 4) & 63;
+  } else {
+    sc = (sb(sy, sz, sw, j + 4) & 0xF) | ((sb(sy, sz, sw, j - 4) >> 6) << 4);
+    m = (sb(sy, sz, sw, j + 4) >> 4) | ((sb(sy, sz, sw, j) >> 6) << 4);
+  }
+}
+
+// One block = 8 warps x 4 rows of one job. The input vector (silu of the sum of its
+// parts) and its 32-value partial sums are staged once per block in shared memory;
+// each warp streams its 4 weight rows and reuses every staged x value for all 4.
 __global__ void __launch_bounds__(kWarps * 32)
     k_gemv(const GemvJob* __restrict__ jobs, const int2* __restrict__ blocks, GemvJob inline_job, Inputs ins) {
-  __shared__ float xs[kMaxLen];
+  __shared__ __align__(16) float xs[kMaxLen];
   __shared__ float xsum[kMaxLen / 32];
-  const int2 bj = jobs ? blocks[blockIdx.x] : make_int2(0, blockIdx.x * kWarps);
+  const int2 bj = jobs ? blocks[blockIdx.x] : make_int2(0, blockIdx.x * kGemvRowsPerBlock);
   const GemvJob job = jobs ? jobs[bj.x] : inline_job;
   const GemvInput in = ins.in[job.x_slot];
   const int K = job.n_cols;
-  for (int i = threadIdx.x; i < K; i += blockDim.x) {
-    float v = 0.f;
-    for (int t = 0; t < in.n_parts; t++) v += in.parts[t][i];
-    xs[i] = in.apply_silu ? silu(v) : v;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int i = threadIdx.x * 4; i < K; i += blockDim.x * 4) {
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int t = 0; t < in.n_parts; t++) {
+      const float4 u = *(const float4*)(in.parts[t] + i);
+      v.x += u.x; v.y += u.y; v.z += u.z; v.w += u.w;
+    }
+    if (in.apply_silu) {
+      v.x = silu(v.x); v.y = silu(v.y); v.z = silu(v.z); v.w = silu(v.w);
+    }
+    *(float4*)(xs + i) = v;
   }
   __syncthreads();
-  for (int i = threadIdx.x; i < K / 32; i += blockDim.x) {
-    float s = 0.f;
-    for (int t = 0; t < 32; t++) s += xs[i * 32 + t];
-    xsum[i] = s;
+  for (int c = warp; c < K / 32; c += kWarps) {
+    float v = xs[c * 32 + lane];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    if (lane == 0) xsum[c] = v;
   }
   __syncthreads();
 
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int row = bj.y + warp;
-  if (row >= job.n_rows) return;
-  const uint8_t* wr = (const uint8_t*)job.w + (int64_t)row * job.row_bytes;
-  float acc = 0.f;
+  const int r0 = bj.y + warp * kRowsPerWarp;
+  if (r0 >= job.n_rows) return;
+  const int nr = min(kRowsPerWarp, job.n_rows - r0);
+  const uint8_t* wbase = (const uint8_t*)job.w + (int64_t)r0 * job.row_bytes;
+  float acc[kRowsPerWarp] = {0.f, 0.f, 0.f, 0.f};
   if (job.type == MB_GGML_Q4_K) {
-    const int units = K / 64;
-    for (int u = lane; u < units; u += 32) {
+    for (int u = lane; u < K / 64; u += 32) {
       const int kb = u >> 2, g = u & 3;
-      const uint8_t* b = wr + kb * 144;
-      const uint4 h = *(const uint4*)b;
-      const uint4 qa = *(const uint4*)(b + 16 + 32 * g), qb = *(const uint4*)(b + 32 + 32 * g);
-      const float d = h16(h.x), dmin = h16(h.x >> 16);
-      const uint8_t* s = b + 4;
-      int sc0, m0, sc1, m1;
-      const int j0 = 2 * g, j1 = 2 * g + 1;
-      if (j0 < 4) { sc0 = s[j0] & 63; m0 = s[j0 + 4] & 63; }
-      else { sc0 = (s[j0 + 4] & 0xF) | ((s[j0 - 4] >> 6) << 4); m0 = (s[j0 + 4] >> 4) | ((s[j0] >> 6) << 4); }
-      if (j1 < 4) { sc1 = s[j1] & 63; m1 = s[j1 + 4] & 63; }
-      else { sc1 = (s[j1 + 4] & 0xF) | ((s[j1 - 4] >> 6) << 4); m1 = (s[j1 + 4] >> 4) | ((s[j1] >> 6) << 4); }
-      const uint32_t w[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
-      const float* x = xs + kb * 256 + g * 64;
-      float dlo = 0.f, dhi = 0.f;
-#pragma unroll
-      for (int i = 0; i < 8; i++) {
-#pragma unroll
-        for (int t = 0; t < 4; t++) {
-          const uint32_t byte = (w[i] >> (8 * t)) & 0xFFu;
-          dlo += (float)(byte & 0xF) * x[4 * i + t];
-          dhi += (float)(byte >> 4) * x[32 + 4 * i + t];
-        }
-      }
-      const float* xsm = xsum + (kb * 256 + g * 64) / 32;
-      acc += d * (float)sc0 * dlo - dmin * (float)m0 * xsm[0] + d * (float)sc1 * dhi - dmin * (float)m1 * xsm[1];
-    }
-  } else if (job.type == MB_GGML_Q8_0) {
-    const int nb = K / 32;
-    for (int bidx = lane; bidx < nb; bidx += 32) {
-      const uint16_t* b = (const uint16_t*)(wr + bidx * 34);
-      const float d = h16(b[0]);
-      const float* x = xs + bidx * 32;
-      float s = 0.f;
+      const float* xl = xs + kb * 256 + g * 64;
+      float x[64];
 #pragma unroll
       for (int i = 0; i < 16; i++) {
-        const uint32_t two = b[1 + i];
-        s += (float)(int8_t)(two & 0xFF) * x[2 * i] + (float)(int8_t)(two >> 8) * x[2 * i + 1];
+        const float4 t = *(const float4*)(xl + 4 * i);
+        x[4 * i] = t.x; x[4 * i + 1] = t.y; x[4 * i + 2] = t.z; x[4 * i + 3] = t.w;
       }
-      acc += d * s;
+      const float s_lo = xsum[(kb * 256 + g * 64) / 32], s_hi = xsum[(kb * 256 + g * 64) / 32 + 1];
+#pragma unroll
+      for (int rr = 0; rr < kRowsPerWarp; rr++) {
+        if (rr < nr) {
+          const uint8_t* b = wbase + (int64_t)rr * job.row_bytes + kb * 144;
+          const uint4 h = __ldg((const uint4*)b);
+          const uint4 qa = __ldg((const uint4*)(b + 16 + 32 * g)), qb = __ldg((const uint4*)(b + 32 + 32 * g));
+          const float d = h16(h.x), dmin = h16(h.x >> 16);
+          int sc0, m0, sc1, m1;
+          q4k_sm(2 * g, h.y, h.z, h.w, sc0, m0);
+          q4k_sm(2 * g + 1, h.y, h.z, h.w, sc1, m1);
+          const uint32_t w[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+          float dlo = 0.f, dhi = 0.f;
+#pragma unroll
+          for (int i = 0; i < 8; i++) {
+#pragma unroll
+            for (int t = 0; t < 4; t++) {
+              const uint32_t byte = (w[i] >> (8 * t)) & 0xFFu;
+              dlo += (float)(byte & 0xF) * x[4 * i + t];
+              dhi += (float)(byte >> 4) * x[32 + 4 * i + t];
+            }
+          }
+          acc[rr] += d * (float)sc0 * dlo - dmin * (float)m0 * s_lo + d * (float)sc1 * dhi - dmin * (float)m1 * s_hi;
+        }
+      }
     }
-  } else if (job.type == MB_GGML_F32) {
-    const float* wf = (const float*)wr;
-    for (int i = lane; i < K; i += 32) acc += wf[i] * xs[i];
-  } else if (job.type == MB_GGML_F16) {
-    const __half* wf = (const __half*)wr;
-    for (int i = lane; i < K; i += 32) acc += __half2float(wf[i]) * xs[i];
+  } else if (job.type == MB_GGML_Q8_0) {
+    for (int bi = lane; bi < K / 32; bi += 32) {
+      const float* xl = xs + bi * 32;
+      float x[32];
+#pragma unroll
+      for (int i = 0; i < 8; i++) {
+        const float4 t = *(const float4*)(xl + 4 * i);
+        x[4 * i] = t.x; x[4 * i + 1] = t.y; x[4 * i + 2] = t.z; x[4 * i + 3] = t.w;
+      }
+#pragma unroll
+      for (int rr = 0; rr < kRowsPerWarp; rr++) {
+        if (rr < nr) {
+          const uint8_t* b = wbase + (int64_t)rr * job.row_bytes + bi * 34;
+          const uint32_t* a4 = (const uint32_t*)((uintptr_t)b & ~(uintptr_t)3);
+          const bool sh = ((uintptr_t)b & 3) != 0;  // block starts 2 bytes into a word
+          uint32_t wv[10];
+#pragma unroll
+          for (int i = 0; i < 10; i++) wv[i] = __ldg(a4 + i);
+          const float d = sh ? h16(wv[0] >> 16) : h16(wv[0]);
+          float sum = 0.f;
+#pragma unroll
+          for (int i = 0; i < 8; i++) {
+            const uint32_t q = sh ? wv[i + 1] : __byte_perm(wv[i], wv[i + 1], 0x5432);
+#pragma unroll
+            for (int t = 0; t < 4; t++) sum += (float)(int8_t)((q >> (8 * t)) & 0xFF) * x[4 * i + t];
+          }
+          acc[rr] += d * sum;
+        }
+      }
+    }
   } else {
-    const uint16_t* wf = (const uint16_t*)wr;
-    for (int i = lane; i < K; i += 32) acc += __uint_as_float((uint32_t)wf[i] << 16) * xs[i];
+    for (int i = lane; i < K; i += 32) {
+      const float xv = xs[i];
+#pragma unroll
+      for (int rr = 0; rr < kRowsPerWarp; rr++) {
+        if (rr < nr) {
+          const uint8_t* row = wbase + (int64_t)rr * job.row_bytes;
+          float wv;
+          if (job.type == MB_GGML_F32) wv = ((const float*)row)[i];
+          else if (job.type == MB_GGML_F16) wv = __half2float(((const __half*)row)[i]);
+          else wv = __uint_as_float((uint32_t)((const uint16_t*)row)[i] << 16);
+          acc[rr] += wv * xv;
+        }
+      }
+    }
   }
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-  if (lane == 0) job.y[row] = acc + (job.bias ? job.bias[row] : 0.f);
+  for (int rr = 0; rr < kRowsPerWarp; rr++) {
+    float v = acc[rr];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    if (lane == 0 && rr < nr) job.y[r0 + rr] = v + (job.bias ? job.bias[r0 + rr] : 0.f);
+  }
 }
 
 }  // namespace gemv
@@ -135,7 +193,7 @@ cudaError_t launch_gemv_single(const mb_weight* w, const float* x, int apply_sil
   ins.in[0].n_parts = 1;
   ins.in[0].apply_silu = apply_silu;
   ins.in[0].len = (int)w->n_cols;
-  const int blocks = (int)((w->n_rows + gemv::kWarps - 1) / gemv::kWarps);
+  const int blocks = (int)((w->n_rows + kGemvRowsPerBlock - 1) / kGemvRowsPerBlock);
   gemv::k_gemv<<<blocks, gemv::kWarps * 32, 0, st>>>(nullptr, nullptr, j, ins);
   return cudaGetLastError();
 }

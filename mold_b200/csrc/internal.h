@@ -84,6 +84,7 @@ struct GemvInput {
   int apply_silu;
   int len;
 };
+constexpr int kGemvRowsPerBlock = 32;  // rows of one job handled by one GEMV block
 // Runs a batch of GEMV jobs in one launch. jobs_dev / block_job_dev live in device memory.
 cudaError_t launch_gemv_batch(const GemvJob* jobs_dev, int n_jobs, const int* block_job_dev, int n_blocks,
                               const GemvInput* inputs, int n_inputs, int max_len, cudaStream_t st);

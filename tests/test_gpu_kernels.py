@@ -111,7 +111,9 @@ def test_qgemm_gate_residual_strided(cuda):
     rt = torch.from_numpy(res).to(cuda)
     w.forward(xt, bias=torch.from_numpy(b).to(cuda), epilogue=mb.EPI_GATE_RESIDUAL, gate=torch.from_numpy(g).to(cuda),
               residual=rt, out=rt)
-    assert rel_l2(rt.cpu().numpy(), ref) < 1e-3
+    # the update gate*(xW^T+b) is rounded once to bf16 before the f32 residual add
+    assert rel_l2(rt.cpu().numpy(), ref) < 4e-3
+    assert rel_l2(rt.cpu().numpy() - res, ref - res) < 4e-3
 
 
 def test_qlinear_f32_input(cuda):
