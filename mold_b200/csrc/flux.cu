@@ -237,6 +237,36 @@ mb_status linear(const mb_flux* m, const std::string& name, const void* x, int64
   return s;
 }
 
+// The text- and image-stream linears of a double block ("<p>txt<suffix>", "<p>img<suffix>")
+// as one grouped GEMM launch. For the gate-residual epilogue y is also the residual.
+mb_status linear_pair(const mb_flux* m, const std::string& p, const char* suffix, const Seg* segs,
+                      const void* const* xs, int64_t ldx, void* const* ys, int64_t ldy, bool out_bf16, int epi,
+                      const float* const* gates, cudaStream_t st) {
+  GemmProblem g[2];
+  const char* S[2] = {"txt", "img"};
+  for (int s = 0; s < 2; s++) {
+    const std::string name = p + S[s] + suffix;
+    GemmEpilogue& e = g[s].epi;
+    e.kind = epi;
+    e.out_bf16 = out_bf16;
+    e.gelu_from = epi == MB_EPI_GELU_TANH ? 0 : (int64_t)1 << 40;
+    e.y = ys[s];
+    e.ldy = ldy;
+    e.bias = B(m, name + ".bias");
+    e.gate = gates[s];
+    e.res = (const float*)ys[s];
+    e.ldr = ldy;
+    g[s].w = W(m, name + ".weight");
+    g[s].x = xs[s];
+    g[s].M = segs[s].rows;
+    g[s].ldx = ldx;
+  }
+  if (g_prof) g_prof->begin(st);
+  mb_status r = check_launch(launch_qgemm_group(2, g, st), suffix);
+  if (g_prof) g_prof->end(st, std::string("gemm txt+img") + suffix);
+  return r;
+}
+
 // Builds the three GEMV job tables: [0] stem in_layers, [1] stem out_layers, [2] all modulations.
 mb_status finalize(mb_flux* m) {
   const int64_t h = m->h();
@@ -357,38 +387,50 @@ mb_status run_forward(mb_flux* m, const float* img, int64_t Li, const float* txt
   MB_TRY(linear(m, "img_in", m->img_bf, Li, c.in_channels, m->x + Lt * h, h, false, MB_EPI_NONE, 0, nullptr, st));
 
   const Seg segs[2] = {{0, Lt}, {Lt, Li}};  // txt, img
-  // ---- double-stream blocks
+  // ---- double-stream blocks: each linear of the two streams runs as one grouped launch
   for (int i = 0; i < c.depth; i++) {
     const std::string p = "double_blocks." + std::to_string(i) + ".";
     const float* md = m->mods + m->mod_off_double[i];
-    for (int s = 0; s < 2; s++) {
-      const Seg g = segs[s];
-      const std::string S = s == 0 ? "txt" : "img";
-      const float* mo = md + (s == 0 ? 6 * h : 0);  // img_mod first, then txt_mod
-      TIMED("ln_modulate", check_launch(launch_ln_modulate(m->x + g.row0 * h, g.rows, h, h, mo, mo + h, m->xm + g.row0 * h, h, st),
-                          "ln_mod1"));
-      MB_TRY(linear(m, p + S + "_attn.qkv", m->xm + g.row0 * h, g.rows, h, m->Y + g.row0 * ldY, ldY, true,
-                    MB_EPI_NONE, 0, nullptr, st));
-      TIMED("qk_norm_rope", check_launch(launch_qk_norm_rope(m->Y + g.row0 * ldY, g.rows, ldY, (int)H,
-                                              B(m, p + S + "_attn.norm.query_norm.scale"),
-                                              B(m, p + S + "_attn.norm.key_norm.scale"), m->pe, g.row0, L, m->q, m->k,
-                                              m->v, st),
-                          "qk_norm_rope"));
+    const float* mos[2] = {md + 6 * h, md};  // txt_mod, img_mod
+    const std::string S[2] = {"txt", "img"};
+    for (int s = 0; s < 2; s++)
+      TIMED("ln_modulate", check_launch(launch_ln_modulate(m->x + segs[s].row0 * h, segs[s].rows, h, h, mos[s],
+                                                           mos[s] + h, m->xm + segs[s].row0 * h, h, st),
+                                        "ln_mod1"));
+    {
+      const void* xs[2] = {m->xm, m->xm + Lt * h};
+      void* ys[2] = {m->Y, m->Y + Lt * ldY};
+      const float* gates[2] = {nullptr, nullptr};
+      MB_TRY(linear_pair(m, p, "_attn.qkv", segs, xs, h, ys, ldY, true, MB_EPI_NONE, gates, st));
     }
+    for (int s = 0; s < 2; s++)
+      TIMED("qk_norm_rope", check_launch(launch_qk_norm_rope(m->Y + segs[s].row0 * ldY, segs[s].rows, ldY, (int)H,
+                                                             B(m, p + S[s] + "_attn.norm.query_norm.scale"),
+                                                             B(m, p + S[s] + "_attn.norm.key_norm.scale"), m->pe,
+                                                             segs[s].row0, L, m->q, m->k, m->v, st),
+                                        "qk_norm_rope"));
     TIMED("attention", check_launch(launch_attention(m->q, m->k, m->v, (int)H, L, L, L, m->Y + 2 * h, ldY, st), "attention"));
-    for (int s = 0; s < 2; s++) {
-      const Seg g = segs[s];
-      const std::string S = s == 0 ? "txt" : "img";
-      const float* mo = md + (s == 0 ? 6 * h : 0);
-      float* xr = m->x + g.row0 * h;
-      MB_TRY(linear(m, p + S + "_attn.proj", m->Y + g.row0 * ldY + 2 * h, g.rows, ldY, xr, h, false,
-                    MB_EPI_GATE_RESIDUAL, 0, mo + 2 * h, st));
-      TIMED("ln_modulate", check_launch(launch_ln_modulate(xr, g.rows, h, h, mo + 3 * h, mo + 4 * h, m->xm + g.row0 * h, h, st),
-                          "ln_mod2"));
-      MB_TRY(linear(m, p + S + "_mlp.0", m->xm + g.row0 * h, g.rows, h, m->Y + g.row0 * ldY + 3 * h, ldY, true,
-                    MB_EPI_GELU_TANH, 0, nullptr, st));
-      MB_TRY(linear(m, p + S + "_mlp.2", m->Y + g.row0 * ldY + 3 * h, g.rows, ldY, xr, h, false, MB_EPI_GATE_RESIDUAL,
-                    0, mo + 5 * h, st));
+    {
+      const void* xs[2] = {m->Y + 2 * h, m->Y + Lt * ldY + 2 * h};
+      void* ys[2] = {m->x, m->x + Lt * h};
+      const float* gates[2] = {mos[0] + 2 * h, mos[1] + 2 * h};
+      MB_TRY(linear_pair(m, p, "_attn.proj", segs, xs, ldY, ys, h, false, MB_EPI_GATE_RESIDUAL, gates, st));
+    }
+    for (int s = 0; s < 2; s++)
+      TIMED("ln_modulate", check_launch(launch_ln_modulate(m->x + segs[s].row0 * h, segs[s].rows, h, h, mos[s] + 3 * h,
+                                                           mos[s] + 4 * h, m->xm + segs[s].row0 * h, h, st),
+                                        "ln_mod2"));
+    {
+      const void* xs[2] = {m->xm, m->xm + Lt * h};
+      void* ys[2] = {m->Y + 3 * h, m->Y + Lt * ldY + 3 * h};
+      const float* gates[2] = {nullptr, nullptr};
+      MB_TRY(linear_pair(m, p, "_mlp.0", segs, xs, h, ys, ldY, true, MB_EPI_GELU_TANH, gates, st));
+    }
+    {
+      const void* xs[2] = {m->Y + 3 * h, m->Y + Lt * ldY + 3 * h};
+      void* ys[2] = {m->x, m->x + Lt * h};
+      const float* gates[2] = {mos[0] + 5 * h, mos[1] + 5 * h};
+      MB_TRY(linear_pair(m, p, "_mlp.2", segs, xs, ldY, ys, h, false, MB_EPI_GATE_RESIDUAL, gates, st));
     }
   }
   // ---- single-stream blocks over cat[txt, img] == x

@@ -67,10 +67,15 @@ constexpr size_t smem_bytes() {
   return 1024 + (size_t)Cfg<WT>::kSX * kXStageBytes + (size_t)Cfg<WT>::kSR * TN * Cfg<WT>::kRawRow + 512;
 }
 
-struct Params {
+struct Prob {  // one GEMM of a (possibly grouped) launch
   int M, N, K;
-  int tiles_m, tiles_n;
+  int tiles_m, tiles_n, tile0;  // tile0: first global tile index of this problem
   GemmEpilogue epi;
+};
+struct Params {
+  Prob pr[2];
+  int nprob;
+  int n_tiles;
   int* status;
   int ablate;  // builds with -DMB_TRACE only: 1 decode, 2 X loads, 4 raw loads, 8 TMEM stores, 16 epilogue
 };
@@ -182,8 +187,8 @@ MB_DEV void umma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t i
 
 template <int WT>
 __global__ void __launch_bounds__(kThreads, 1)
-    k_qgemm(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_r0,
-            const __grid_constant__ CUtensorMap tm_r1, const Params p) {
+    k_qgemm(const __grid_constant__ CUtensorMap tm_x0, const __grid_constant__ CUtensorMap tm_w0,
+            const __grid_constant__ CUtensorMap tm_x1, const __grid_constant__ CUtensorMap tm_w1, const Params p) {
   constexpr int kSR = Cfg<WT>::kSR, SX = Cfg<WT>::kSX, kSPC = Cfg<WT>::kSPC;
   constexpr uint32_t kRawStage = TN * Cfg<WT>::kRawRow;
   extern __shared__ uint8_t smem_raw[];
@@ -203,8 +208,18 @@ __global__ void __launch_bounds__(kThreads, 1)
   volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int nks = p.K / BK;
-  const int n_tiles = p.tiles_m * p.tiles_n;
+  const int n_tiles = p.n_tiles;
+  // problem of a global tile index and the tile's origin within it
+#define TILE_SETUP(tile)                                                   \
+  const int pi_ = (p.nprob > 1 && (tile) >= p.pr[1].tile0) ? 1 : 0;      \
+  const Prob& P = p.pr[pi_];                                               \
+  const int lt_ = (tile) - P.tile0;                                        \
+  const int nks = P.K / BK;                                                \
+  const CUtensorMap* tm_x = pi_ ? &tm_x1 : &tm_x0;                         \
+  const CUtensorMap* tm_w = pi_ ? &tm_w1 : &tm_w0;                         \
+  (void)tm_x;                                                              \
+  (void)tm_w;                                                              \
+  (void)nks;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < SX; i++) { mbar_init(&x_full[i], 1); mbar_init(&x_empty[i], 1); }
@@ -220,8 +235,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     tmem_relinquish();
   }
   if (warp == 0 && lane == 0) {
-    tma_prefetch_desc(&tm_x);
-    tma_prefetch_desc(&tm_r0);
+    tma_prefetch_desc(&tm_x0);
+    tma_prefetch_desc(&tm_w0);
+    if (p.nprob > 1) {
+      tma_prefetch_desc(&tm_x1);
+      tma_prefetch_desc(&tm_w1);
+    }
   }
   tc_fence_before();
   __syncthreads();
@@ -234,7 +253,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t it = 0, ic = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x) {
-        const int m0 = (tile % p.tiles_m) * TM, n0 = (tile / p.tiles_m) * TN;
+        TILE_SETUP(tile);
+        const int m0 = (lt_ % P.tiles_m) * TM, n0 = (lt_ / P.tiles_m) * TN;
         for (int ks = 0; ks < nks && ok; ks++, it++) {
           const uint32_t sx = it % SX, px = (it / SX) & 1;
           if (!(ok = mbar_wait(&x_empty[sx], px ^ 1, abort_flag, p.status, kDevTimeoutGemm))) break;
@@ -242,7 +262,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_arrive(&x_full[sx]);
           } else {
             mbar_expect_tx(&x_full[sx], kXStageBytes);
-            tma_load_2d(xs + sx * kXStageBytes, &tm_x, &x_full[sx], ks * BK, m0);
+            tma_load_2d(xs + sx * kXStageBytes, tm_x, &x_full[sx], ks * BK, m0);
           }
           if (ks % kSPC == 0) {  // one raw chunk (kSPC stages) per 128-row weight block
             const uint32_t sr = ic % kSR, pr = (ic / kSR) & 1;
@@ -255,11 +275,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_expect_tx(&r_full[sr], kRawStage);
             uint8_t* rdst = rs + sr * kRawStage;
             if (WT == MB_GGML_Q4_K) {
-              tma_load_2d(rdst, &tm_r0, &r_full[sr], (ks >> 2) * 144, n0);
+              tma_load_2d(rdst, tm_w, &r_full[sr], (ks >> 2) * 144, n0);
             } else if (WT == MB_GGML_Q8_0) {
-              tma_load_2d(rdst, &tm_r0, &r_full[sr], (68 * ks) & ~15, n0);
+              tma_load_2d(rdst, tm_w, &r_full[sr], (68 * ks) & ~15, n0);
             } else {
-              tma_load_2d(rdst, &tm_r0, &r_full[sr], ks * 128, n0);
+              tma_load_2d(rdst, tm_w, &r_full[sr], ks * 128, n0);
             }
           }
         }
@@ -271,6 +291,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t it = 0, tcount = 0;
     bool ok = true;
     for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x, tcount++) {
+      TILE_SETUP(tile);
       if (!(ok = mbar_wait(acc_empty, (tcount & 1) ^ 1, abort_flag, p.status, kDevTimeoutGemm))) break;
       tc_fence_after();
       for (int ks = 0; ks < nks; ks++, it++) {
@@ -304,6 +325,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t it = 0, ic = 0;
     bool ok = true;
     for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x) {
+      TILE_SETUP(tile);
       for (int kc = 0; kc < nks / kSPC && ok; kc++, ic++) {
         const uint32_t sr = ic % kSR, pr = (ic / kSR) & 1;
         if (!(ok = mbar_wait(&r_full[sr], pr, abort_flag, p.status, kDevTimeoutGemm))) break;
@@ -390,19 +412,20 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int q = warp & 3;
     const int ch = (warp - 2 - kDW) >> 2;  // which 128 of the tile's 256 activation rows
     const uint32_t lane_addr = (uint32_t)(q * 32) << 16;
-    const GemmEpilogue& e = p.epi;
     uint32_t tcount = 0;
     bool ok = true;
     for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x, tcount++) {
-      const int m0 = (tile % p.tiles_m) * TM + ch * 128, n0 = (tile / p.tiles_m) * TN;
+      TILE_SETUP(tile);
+      const GemmEpilogue& e = P.epi;
+      const int m0 = (lt_ % P.tiles_m) * TM + ch * 128, n0 = (lt_ / P.tiles_m) * TN;
       const int n = n0 + q * 32 + lane;
       if (!(ok = mbar_wait(acc_full, tcount & 1, abort_flag, p.status, kDevTimeoutGemm))) break;
       tc_fence_after();
-      const bool nvalid = n < p.N;
+      const bool nvalid = n < P.N;
       const float bias = (nvalid && e.bias) ? e.bias[n] : 0.f;
       const float gate = (nvalid && e.kind == MB_EPI_GATE_RESIDUAL) ? e.gate[n] : 0.f;
       const bool do_gelu = e.kind == MB_EPI_GELU_TANH && n >= e.gelu_from;
-      const bool fast_bf16 = e.out_bf16 && e.kind != MB_EPI_GATE_RESIDUAL && (p.N & 1) == 0;
+      const bool fast_bf16 = e.out_bf16 && e.kind != MB_EPI_GATE_RESIDUAL && (P.N & 1) == 0;
       if (ABL(16)) {
         __syncwarp();
         if (lane == 0) mbar_arrive(acc_empty);
@@ -440,7 +463,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             // even lane: (own lo, partner lo) = row m ; odd lane: (partner hi, own hi) = row m + 1
             const uint32_t wv = odd ? __byte_perm(r2, r, 0x7632) : __byte_perm(r, r2, 0x5410);
             const int m = m0 + c * 32 + 2 * j + (odd ? 1 : 0);
-            if (m < p.M && ncol < p.N)
+            if (m < P.M && ncol < P.N)
               *(uint32_t*)((__nv_bfloat16*)e.y + (int64_t)m * e.ldy + ncol) = wv;
           }
         }
@@ -470,13 +493,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int i = 0; i < 16; i++) {
               const int m = m0 + c * 16 + i;
-              rv[i] = m < p.M ? e.res[(int64_t)m * e.ldr + n] : 0.f;
+              rv[i] = m < P.M ? e.res[(int64_t)m * e.ldr + n] : 0.f;
             }
 #pragma unroll
             for (int i = 0; i < 16; i++) {
               const int m = m0 + c * 16 + i;
               const uint32_t r = pk[c * 8 + (i >> 1)];
-              if (m < p.M) ((float*)e.y)[(int64_t)m * e.ldy + n] = rv[i] + ((i & 1) ? bf16_hi(r) : bf16_lo(r));
+              if (m < P.M) ((float*)e.y)[(int64_t)m * e.ldy + n] = rv[i] + ((i & 1) ? bf16_hi(r) : bf16_lo(r));
             }
           }
         }
@@ -496,7 +519,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int i = 0; i < 32; i++) {
               const int m = mb + i;
-              if (m < p.M) {
+              if (m < P.M) {
                 float a = __uint_as_float(v[i]) + bias;
                 if (e.kind == MB_EPI_GATE_RESIDUAL) {
                   const float rv = e.res[(int64_t)m * e.ldr + n];
@@ -527,27 +550,42 @@ __global__ void __launch_bounds__(kThreads, 1)
 int g_gemm_ablate = 0;
 
 template <int WT>
-cudaError_t launch_t(const mb_weight* w, const void* x, int64_t M, int64_t ldx, const GemmEpilogue& epi,
-                     cudaStream_t st) {
-  CUtensorMap tx, tr0, tr1;
-  if (!make_tmap_2d(&tx, x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)w->n_cols, (uint64_t)M, (uint64_t)ldx * 2,
-                    BK, TM, CU_TENSOR_MAP_SWIZZLE_128B))
-    return cudaErrorInvalidValue;
+bool make_maps(const mb_weight* w, const void* x, int64_t M, int64_t ldx, CUtensorMap* tx, CUtensorMap* tw) {
+  if (!make_tmap_2d(tx, x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)w->n_cols, (uint64_t)M, (uint64_t)ldx * 2, BK,
+                    TM, CU_TENSOR_MAP_SWIZZLE_128B))
+    return false;
   const uint64_t rb = (uint64_t)w->row_bytes, nr = (uint64_t)w->n_rows;
   const uint32_t box = WT == MB_GGML_Q4_K ? 144 : (WT == MB_GGML_Q8_0 ? 80 : 128);
-  if (!make_tmap_2d(&tr0, w->dev, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, rb, nr, rb, box, TN, CU_TENSOR_MAP_SWIZZLE_NONE))
-    return cudaErrorInvalidValue;
-  tr1 = tr0;
+  return make_tmap_2d(tw, w->dev, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, rb, nr, rb, box, TN, CU_TENSOR_MAP_SWIZZLE_NONE);
+}
+
+// Launches one persistent kernel over the tiles of n (1 or 2) GEMMs with the same weight type.
+template <int WT>
+cudaError_t launch_t(int n, const GemmProblem* g, cudaStream_t st) {
+  CUtensorMap tx[2], tw[2];
   Params p;
-  p.M = (int)M;
-  p.N = (int)w->n_rows;
-  p.K = (int)w->n_cols;
-  p.tiles_m = (int)((M + TM - 1) / TM);
-  p.tiles_n = (int)((w->n_rows + TN - 1) / TN);
-  p.epi = epi;
+  int tiles = 0;
+  for (int i = 0; i < n; i++) {
+    if (!make_maps<WT>(g[i].w, g[i].x, g[i].M, g[i].ldx, &tx[i], &tw[i])) return cudaErrorInvalidValue;
+    Prob& P = p.pr[i];
+    P.M = (int)g[i].M;
+    P.N = (int)g[i].w->n_rows;
+    P.K = (int)g[i].w->n_cols;
+    P.tiles_m = (int)((g[i].M + TM - 1) / TM);
+    P.tiles_n = (int)((g[i].w->n_rows + TN - 1) / TN);
+    P.tile0 = tiles;
+    P.epi = g[i].epi;
+    tiles += P.tiles_m * P.tiles_n;
+  }
+  if (n == 1) {
+    tx[1] = tx[0];
+    tw[1] = tw[0];
+    p.pr[1] = p.pr[0];
+  }
+  p.nprob = n;
+  p.n_tiles = tiles;
   p.status = device_status_ptr();
   p.ablate = g_gemm_ablate;
-  const int tiles = p.tiles_m * p.tiles_n;
   const int grid = tiles < num_sms() ? tiles : num_sms();
   constexpr size_t smem = smem_bytes<WT>();
   static int attr_done[64];  // per template instance and device
@@ -558,7 +596,7 @@ cudaError_t launch_t(const mb_weight* w, const void* x, int64_t M, int64_t ldx, 
     if (e != cudaSuccess) return e;
     attr_done[dev & 63] = 1;
   }
-  k_qgemm<WT><<<grid, kThreads, smem, st>>>(tx, tr0, tr1, p);
+  k_qgemm<WT><<<grid, kThreads, smem, st>>>(tx[0], tw[0], tx[1], tw[1], p);
   return cudaGetLastError();
 }
 
@@ -568,15 +606,23 @@ cudaError_t launch_t(const mb_weight* w, const void* x, int64_t M, int64_t ldx, 
 extern "C" __attribute__((visibility("default"))) void mb_debug_set_gemm_ablate(int flags) { gemm::g_gemm_ablate = flags; }
 #endif
 
+cudaError_t launch_qgemm_group(int n, const GemmProblem* g, cudaStream_t st) {
+  if (n < 1 || n > 2) return cudaErrorInvalidValue;
+  for (int i = 0; i < n; i++)
+    if (g[i].M <= 0 || g[i].w->type != g[0].w->type) return cudaErrorInvalidValue;
+  switch (g[0].w->type) {
+    case MB_GGML_Q4_K: return gemm::launch_t<MB_GGML_Q4_K>(n, g, st);
+    case MB_GGML_Q8_0: return gemm::launch_t<MB_GGML_Q8_0>(n, g, st);
+    case MB_GGML_BF16: return gemm::launch_t<MB_GGML_BF16>(n, g, st);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
 cudaError_t launch_qgemm(const mb_weight* w, const void* x_bf16, int64_t M, int64_t ldx, const GemmEpilogue& epi,
                          cudaStream_t st) {
   if (M <= 0) return cudaSuccess;
-  switch (w->type) {
-    case MB_GGML_Q4_K: return gemm::launch_t<MB_GGML_Q4_K>(w, x_bf16, M, ldx, epi, st);
-    case MB_GGML_Q8_0: return gemm::launch_t<MB_GGML_Q8_0>(w, x_bf16, M, ldx, epi, st);
-    case MB_GGML_BF16: return gemm::launch_t<MB_GGML_BF16>(w, x_bf16, M, ldx, epi, st);
-    default: return cudaErrorInvalidValue;
-  }
+  GemmProblem g{w, x_bf16, M, ldx, epi};
+  return launch_qgemm_group(1, &g, st);
 }
 
 }  // namespace mb

@@ -63,6 +63,15 @@ struct GemmEpilogue {
 };
 cudaError_t launch_qgemm(const mb_weight* w, const void* x_bf16, int64_t M, int64_t ldx, const GemmEpilogue& epi,
                          cudaStream_t st);
+// Up to two independent GEMMs (same weight type) in one persistent launch (e.g. the text and
+// image streams of a double block), so the small one fills SMs the large one leaves idle.
+struct GemmProblem {
+  const mb_weight* w;
+  const void* x;
+  int64_t M, ldx;
+  GemmEpilogue epi;
+};
+cudaError_t launch_qgemm_group(int n, const GemmProblem* g, cudaStream_t st);
 cudaError_t launch_dequant(int type, const void* raw, int64_t n_rows, int64_t n_cols, int64_t row_bytes, void* out,
                            int out_bf16, cudaStream_t st);
 cudaError_t launch_cast_f32_bf16(const float* x, int64_t M, int64_t K, int64_t ldx, void* y, int64_t ldy,
