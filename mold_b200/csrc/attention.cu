@@ -4,14 +4,19 @@
 // the [H, L, L] score matrix) and Qwen's masked attention
 // (qwen_image/quantized_transformer.rs:799-816) without ever forming L x L.
 //
-// One CTA = 128 query rows of one head. Warp roles (192 threads):
-//   warp 0   TMA: Q once, then K_j and V_j (128 keys each) into a 2-deep ring.
-//   warp 1   MMA: S_j = Q K_j^T into TMEM (two S buffers, so S_{j+1} runs on the
-//            tensor core while softmax works on S_j), then O += P_j V_j with O in TMEM.
-//   warps 2-5 softmax, one thread per query row (= TMEM lane): row max, exp2,
-//            row sum, P_j (bf16) into shared memory in the UMMA K-major 128B-swizzled
-//            layout. O is rescaled lazily: only when the running max grows by more
-//            than 2^8 (FA4-style), which leaves the final O / l unchanged.
+// One CTA = 256 query rows (two 128-row tiles) of one head, sharing every K/V block.
+//   warp 0      TMA: both Q tiles once, then K_j and V_j (128 keys) into a 2-deep ring.
+//   warp 1      MMA issuer. Per KV block j the tensor core runs, in order,
+//                 PV_0(j), S_0(j+1) = Q_0 K_{j+1}^T, PV_1(j), S_1(j+1)
+//               so while one tile's softmax works, the tensor core serves the other.
+//   warps 4-7   softmax of tile 0, warps 8-11 softmax of tile 1: one thread per query
+//               row (= TMEM lane). Row max, exp2, row sum; P (bf16) is written back into
+//               TMEM over the S columns it was computed from and consumed directly as the
+//               A operand of O += P V (O in TMEM). O is rescaled lazily, only when the row
+//               max grows by more than 2^8, which leaves the final O / l unchanged.
+//               A fixed share of each row's exp2 is evaluated with a polynomial on the FMA
+//               pipe instead of the MUFU unit (which alone would cap the kernel).
+// TMEM (512 columns): S_0 [0,128), S_1 [128,256), O_0 [256,384), O_1 [384,512).
 // V is consumed in its natural [keys, d] layout as an MN-major B operand.
 #include "common.cuh"
 #include "internal.h"
@@ -19,13 +24,14 @@
 namespace mb {
 namespace attn {
 
-constexpr int BQ = 128, BKV = 128, D = 128;
-constexpr int kThreads = 192;
+constexpr int BQ = 128, BKV = 128, D = 128, NT = 2;
+constexpr int kThreads = 384;
 constexpr uint32_t kTile = 128 * 128 * 2;  // 32 KB: one 128x128 bf16 tile (two 64-wide swizzle atoms)
 constexpr uint32_t kHalf = kTile / 2;      // 16 KB: one 64-wide atom column
-constexpr size_t kSmem = 1024 + 7 * (size_t)kTile + 256;
+constexpr size_t kSmem = 1024 + 6 * (size_t)kTile + 256;
 constexpr float kScaleLog2 = 0.12751743082459868f;  // log2(e) / sqrt(128)
 constexpr float kRescaleThreshold = 8.f;
+constexpr int kPolyPerChunk = 6;  // of every 32 exponentials, this many use the FMA-pipe polynomial
 
 struct Params {
   int H, Lq, Lk, n_valid, n_kv;
@@ -34,29 +40,107 @@ struct Params {
   int* status;
 };
 
+// 2^x for x <= ~8 (arguments below -125 return 0). x = n + f with n = round(x), |f| <= 1/2;
+// 2^f from its Taylor series in f*ln2 to 4th order (relative error < 5e-5, well below the
+// bf16 rounding P is stored with); 2^n is added to the exponent field.
+MB_DEV float exp2_poly(float x) {
+  const float t = x + 12582912.f;  // 1.5 * 2^23: rounds x to an integer in the low mantissa bits
+  const float n = t - 12582912.f;
+  const float f = x - n;
+  float p = 0.009618129107628477f;  // ln2^4 / 24
+  p = fmaf(p, f, 0.05550410866482158f);  // ln2^3 / 6
+  p = fmaf(p, f, 0.2402265069591007f);   // ln2^2 / 2
+  p = fmaf(p, f, 0.6931471805599453f);   // ln2
+  p = fmaf(p, f, 1.0f);
+  const int e = (int)((uint32_t)(__float_as_int(t) - 0x4B400000) << 23);
+  return x < -125.f ? 0.f : __int_as_float(__float_as_int(p) + e);
+}
+
+// ---- packed f32x2 helpers (sm_100): two IEEE single-precision ops per instruction
+MB_DEV uint64_t pk2(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1,%2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+MB_DEV void up2(uint64_t v, float& a, float& b) { asm("mov.b64 {%0,%1}, %2;" : "=f"(a), "=f"(b) : "l"(v)); }
+MB_DEV uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+MB_DEV uint64_t add2(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+MB_DEV uint64_t sub2(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+MB_DEV float max3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+// exp2_poly on a pair (same method as exp2_poly, packed arithmetic).
+MB_DEV void exp2_poly2(uint64_t x2, float& e0, float& e1) {
+  const uint64_t magic = pk2(12582912.f, 12582912.f);
+  const uint64_t t2 = add2(x2, magic);
+  const uint64_t f = sub2(x2, sub2(t2, magic));
+  uint64_t p = pk2(0.009618129107628477f, 0.009618129107628477f);
+  p = fma2(p, f, pk2(0.05550410866482158f, 0.05550410866482158f));
+  p = fma2(p, f, pk2(0.2402265069591007f, 0.2402265069591007f));
+  p = fma2(p, f, pk2(0.6931471805599453f, 0.6931471805599453f));
+  p = fma2(p, f, pk2(1.0f, 1.0f));
+  float t0, t1, p0, p1, x0, x1;
+  up2(t2, t0, t1);
+  up2(p, p0, p1);
+  up2(x2, x0, x1);
+  // 2^n enters through the exponent field: (bits(t) - bits(1.5*2^23)) << 23 == bits(t) << 23 (mod 2^32)
+  e0 = x0 < -125.f ? 0.f : __int_as_float(__float_as_int(p0) + (int)((uint32_t)__float_as_int(t0) << 23));
+  e1 = x1 < -125.f ? 0.f : __int_as_float(__float_as_int(p1) + (int)((uint32_t)__float_as_int(t1) << 23));
+}
+
+MB_DEV void tmem_st16a(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
+          taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
+
+// D(tmem) (+)= A(tmem) * B(smem desc)^T
+MB_DEV void umma_ts_a(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(
+          d_tmem),
+      "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 __global__ void __launch_bounds__(kThreads, 1)
     k_attention(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                 const __grid_constant__ CUtensorMap tv, const Params p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-  uint8_t* sQ = smem;
-  uint8_t* sK = smem + kTile;          // 2 stages
-  uint8_t* sV = smem + 3 * kTile;      // 2 stages
-  uint8_t* sP = smem + 5 * kTile;      // 2 buffers
-  uint64_t* bars = (uint64_t*)(smem + 7 * kTile);
+  uint8_t* sQ = smem;                  // 2 tiles
+  uint8_t* sK = smem + 2 * kTile;      // 2 stages
+  uint8_t* sV = smem + 4 * kTile;      // 2 stages
+  uint64_t* bars = (uint64_t*)(smem + 6 * kTile);
   uint64_t* q_full = bars;
-  uint64_t* k_full = bars + 1;   // [2]
-  uint64_t* v_full = bars + 3;   // [2]
-  uint64_t* kv_empty = bars + 5; // [2]
-  uint64_t* s_full = bars + 7;   // [2]
-  uint64_t* p_full = bars + 9;   // [2]
-  uint64_t* p_empty = bars + 11; // [2]
-  uint64_t* o_full = bars + 13;
-  uint32_t* tmem_slot = (uint32_t*)(bars + 14);
+  uint64_t* k_full = bars + 1;    // [2] per stage
+  uint64_t* v_full = bars + 3;    // [2]
+  uint64_t* kv_empty = bars + 5;  // [2]
+  uint64_t* s_full = bars + 7;    // [2] per tile
+  uint64_t* p_full = bars + 9;    // [2] per tile
+  uint64_t* o_full = bars + 11;   // [2] per tile
+  uint32_t* tmem_slot = (uint32_t*)(bars + 13);
   volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int h = blockIdx.y, q0 = blockIdx.x * BQ;
+  const int h = blockIdx.y, q0 = blockIdx.x * (NT * BQ);
   const int n_kv = p.n_kv;
 
   if (threadIdx.x == 0) {
@@ -67,9 +151,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&kv_empty[i], 1);
       mbar_init(&s_full[i], 1);
       mbar_init(&p_full[i], 4);
-      mbar_init(&p_empty[i], 1);
+      mbar_init(&o_full[i], 1);
     }
-    mbar_init(o_full, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -81,16 +164,17 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t tS = tmem, tO = tmem + 256;
 
   if (warp == 0) {
     if (lane == 0) {
       tma_prefetch_desc(&tq);
       tma_prefetch_desc(&tk);
       tma_prefetch_desc(&tv);
-      mbar_expect_tx(q_full, kTile);
-      tma_load_3d(sQ, &tq, q_full, 0, q0, h);
-      tma_load_3d(sQ + kHalf, &tq, q_full, 64, q0, h);
+      mbar_expect_tx(q_full, 2 * kTile);
+      for (int t = 0; t < NT; t++) {
+        tma_load_3d(sQ + t * kTile, &tq, q_full, 0, q0 + t * BQ, h);
+        tma_load_3d(sQ + t * kTile + kHalf, &tq, q_full, 64, q0 + t * BQ, h);
+      }
       for (int j = 0; j < n_kv; j++) {
         const int s = j & 1;
         const uint32_t ph = (j >> 1) & 1;
@@ -106,156 +190,167 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     constexpr uint32_t idesc_s = idesc_bf16(BQ, BKV, false);
     constexpr uint32_t idesc_o = idesc_bf16(BQ, D, true);
-    bool ok = mbar_wait(q_full, 0, abort_flag, p.status, kDevTimeoutAttn);
     const uint32_t qa = smem_u32(sQ);
-    for (int j = 0; j <= n_kv && ok; j++) {
-      if (j < n_kv) {
-        const int s = j & 1;
-        if (!(ok = mbar_wait(&k_full[s], (j >> 1) & 1, abort_flag, p.status, kDevTimeoutAttn))) break;
-        tc_fence_after();
-        if (lane == 0) {
-          const uint32_t ka = smem_u32(sK + s * kTile);
+    bool ok = mbar_wait(q_full, 0, abort_flag, p.status, kDevTimeoutAttn);
+    // S_t = Q_t K_j^T into the tile's S columns
+    auto issue_s = [&](int t, int j) {
+      if (lane == 0) {
+        const uint32_t ka = smem_u32(sK + (j & 1) * kTile);
 #pragma unroll
-          for (int kk = 0; kk < D / 16; kk++) {
-            const uint32_t off = (kk >> 2) * kHalf + (kk & 3) * 32;
-            umma_f16(tS + s * 128, sw128_desc(qa + off, 16, 1024), sw128_desc(ka + off, 16, 1024), idesc_s, kk > 0);
-          }
-          umma_commit(&s_full[s]);
+        for (int kk = 0; kk < D / 16; kk++) {
+          const uint32_t off = (kk >> 2) * kHalf + (kk & 3) * 32;
+          umma_f16(tmem + t * 128, sw128_desc(qa + t * kTile + off, 16, 1024), sw128_desc(ka + off, 16, 1024),
+                   idesc_s, kk > 0);
         }
-        __syncwarp();
+        umma_commit(&s_full[t]);
       }
-      if (j >= 1) {
-        const int jj = j - 1, b = jj & 1;
-        const uint32_t ph = (jj >> 1) & 1;
-        if (!(ok = mbar_wait(&p_full[b], ph, abort_flag, p.status, kDevTimeoutAttn))) break;
-        if (!(ok = mbar_wait(&v_full[b], ph, abort_flag, p.status, kDevTimeoutAttn))) break;
-        tc_fence_after();
-        if (lane == 0) {
-          const uint32_t pa = smem_u32(sP + b * kTile), va = smem_u32(sV + b * kTile);
+      __syncwarp();
+    };
+    // O_t += P_t V_j with P_t read from TMEM (bf16 pairs over the S columns)
+    auto issue_pv = [&](int t, int j) {
+      if (lane == 0) {
+        const uint32_t va = smem_u32(sV + (j & 1) * kTile);
 #pragma unroll
-          for (int kk = 0; kk < BKV / 16; kk++) {
-            const uint64_t adesc = sw128_desc(pa + (kk >> 2) * kHalf + (kk & 3) * 32, 16, 1024);
-            // V [keys, d]: MN-major; 64-wide d chunks kHalf apart (LBO), 8-key groups 1024 B apart (SBO).
-            const uint64_t bdesc = sw128_desc(va + kk * 16 * 128, kHalf, 1024);
-            umma_f16(tO, adesc, bdesc, idesc_o, (jj > 0 || kk > 0) ? 1u : 0u);
-          }
-          umma_commit(&p_empty[b]);
-          umma_commit(&kv_empty[b]);
+        for (int kk = 0; kk < BKV / 16; kk++) {
+          // V [keys, d]: MN-major; 64-wide d chunks kHalf apart (LBO), 8-key groups 1024 B apart (SBO).
+          const uint64_t bdesc = sw128_desc(va + kk * 16 * 128, kHalf, 1024);
+          umma_ts_a(tmem + 256 + t * 128, tmem + t * 128 + kk * 8, bdesc, idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
         }
-        __syncwarp();
+      }
+      __syncwarp();
+    };
+    if (ok && n_kv > 0) {
+      if ((ok = mbar_wait(&k_full[0], 0, abort_flag, p.status, kDevTimeoutAttn))) {
+        tc_fence_after();
+        issue_s(0, 0);
+        issue_s(1, 0);
       }
     }
-    if (ok && lane == 0) umma_commit(o_full);
+    for (int j = 0; j < n_kv && ok; j++) {
+      const uint32_t ph = (j >> 1) & 1;
+      if (!(ok = mbar_wait(&v_full[j & 1], ph, abort_flag, p.status, kDevTimeoutAttn))) break;
+      const bool more = j + 1 < n_kv;
+      if (!(ok = mbar_wait(&p_full[0], j & 1, abort_flag, p.status, kDevTimeoutAttn))) break;
+      tc_fence_after();
+      issue_pv(0, j);
+      if (more) {
+        if (!(ok = mbar_wait(&k_full[(j + 1) & 1], ((j + 1) >> 1) & 1, abort_flag, p.status, kDevTimeoutAttn))) break;
+        tc_fence_after();
+        issue_s(0, j + 1);
+      }
+      if (!(ok = mbar_wait(&p_full[1], j & 1, abort_flag, p.status, kDevTimeoutAttn))) break;
+      tc_fence_after();
+      issue_pv(1, j);
+      if (lane == 0) umma_commit(&kv_empty[j & 1]);
+      __syncwarp();
+      if (more) issue_s(1, j + 1);
+    }
+    if (ok && lane == 0) {
+      umma_commit(&o_full[0]);
+      umma_commit(&o_full[1]);
+    }
     __syncwarp();
-  } else {
-    // ---------------------------------------------------------------- softmax
+  } else if (warp >= 4) {
+    // ---------------------------------------------------------------- softmax (one tile per warpgroup)
+    const int t = (warp - 4) >> 2;
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;
     const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
+    const uint32_t tS = tmem + t * 128 + lane_addr, tO = tmem + 256 + t * 128 + lane_addr;
     float m_run = -INFINITY, l_run = 0.f;
     bool ok = true;
     for (int j = 0; j < n_kv; j++) {
-      const int s = j & 1;
-      if (!(ok = mbar_wait(&s_full[s], (j >> 1) & 1, abort_flag, p.status, kDevTimeoutAttn))) break;
+      if (!(ok = mbar_wait(&s_full[t], j & 1, abort_flag, p.status, kDevTimeoutAttn))) break;
       tc_fence_after();
       const int valid = p.n_valid - j * BKV;  // keys >= valid are masked in this block
-      const uint32_t sa = tS + s * 128 + lane_addr;
+      // the whole S row in registers: one TMEM round trip per block
+      uint32_t v[128];
+#pragma unroll
+      for (int c = 0; c < 4; c++) tmem_ld32(tS + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&v[32 * c]));
+      tmem_wait_ld();
+      if (valid < BKV) {
+#pragma unroll
+        for (int i = 0; i < 128; i++)
+          if (i >= valid) v[i] = __float_as_uint(-INFINITY);
+      }
       float mx = -INFINITY;
 #pragma unroll
-      for (int c = 0; c < 4; c++) {
-        uint32_t v[32];
-        tmem_ld32(sa + c * 32, v);
-        tmem_wait_ld();
-        if (valid >= BKV) {
-#pragma unroll
-          for (int i = 0; i < 32; i++) mx = fmaxf(mx, __uint_as_float(v[i]));
-        } else {
-#pragma unroll
-          for (int i = 0; i < 32; i++)
-            if (c * 32 + i < valid) mx = fmaxf(mx, __uint_as_float(v[i]));
-        }
-      }
+      for (int i = 0; i < 128; i += 2) mx = max3(mx, __uint_as_float(v[i]), __uint_as_float(v[i + 1]));
       const float m_new = fmaxf(m_run, mx * kScaleLog2);
       if (j == 0) {
         m_run = m_new;
       } else {
+        // S_t(j) complete implies PV_t(j-1) complete (same issuing thread, in order): O_t is stable.
         const bool need = m_new > m_run + kRescaleThreshold;
         if (__any_sync(0xffffffffu, need)) {
-          const int jp = j - 1;
-          if (!(ok = mbar_wait(&p_empty[jp & 1], (jp >> 1) & 1, abort_flag, p.status, kDevTimeoutAttn))) break;
-          tc_fence_after();
           const float alpha = need ? ex2_approx(m_run - m_new) : 1.f;
 #pragma unroll 1
           for (int c = 0; c < 4; c++) {
             uint32_t o[32];
-            tmem_ld32(tO + lane_addr + c * 32, o);
+            tmem_ld32(tO + c * 32, o);
             tmem_wait_ld();
 #pragma unroll
             for (int i = 0; i < 32; i++) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-            tmem_st32(tO + lane_addr + c * 32, o);
+            tmem_st32(tO + c * 32, o);
           }
           tmem_wait_st();
           l_run *= alpha;
           if (need) m_run = m_new;
         }
       }
-      if (j >= 2) {
-        if (!(ok = mbar_wait(&p_empty[s], ((j >> 1) - 1) & 1, abort_flag, p.status, kDevTimeoutAttn))) break;
-      }
-      uint8_t* prow = sP + s * kTile + r * 128;
-      const int sw = r & 7;
-      float sum = 0.f;
+      const uint64_t sc2 = pk2(kScaleLog2, kScaleLog2), nm2 = pk2(-m_run, -m_run);
+      uint64_t sum2 = pk2(0.f, 0.f);
 #pragma unroll
       for (int c = 0; c < 4; c++) {
-        uint32_t v[32];
-        tmem_ld32(sa + c * 32, v);
-        tmem_wait_ld();
-        float e[32];
+        uint32_t pk[16];
 #pragma unroll
-        for (int i = 0; i < 32; i++) {
-          const float x = __uint_as_float(v[i]) * kScaleLog2 - m_run;
-          e[i] = (valid >= BKV || c * 32 + i < valid) ? ex2_approx(x) : 0.f;
-          sum += e[i];
+        for (int i = 0; i < 16; i++) {
+          const uint64_t x2 = fma2(pk2(__uint_as_float(v[32 * c + 2 * i]), __uint_as_float(v[32 * c + 2 * i + 1])),
+                                   sc2, nm2);
+          float e0, e1;
+          if (2 * i < kPolyPerChunk) {
+            exp2_poly2(x2, e0, e1);
+          } else {
+            float x0, x1;
+            up2(x2, x0, x1);
+            e0 = ex2_approx(x0);
+            e1 = ex2_approx(x1);
+          }
+          sum2 = add2(sum2, pk2(e0, e1));
+          pk[i] = pack_bf16x2(e0, e1);
         }
-        // keys c*32 .. c*32+31 -> atom column (c >> 1), 16-byte chunks (c & 1)*4 .. +3
-        uint8_t* base = prow + (c >> 1) * kHalf;
-#pragma unroll
-        for (int t = 0; t < 4; t++) {
-          const int chunk = (c & 1) * 4 + t;
-          uint4 u;
-          u.x = pack_bf16x2(e[8 * t + 0], e[8 * t + 1]);
-          u.y = pack_bf16x2(e[8 * t + 2], e[8 * t + 3]);
-          u.z = pack_bf16x2(e[8 * t + 4], e[8 * t + 5]);
-          u.w = pack_bf16x2(e[8 * t + 6], e[8 * t + 7]);
-          *(uint4*)(base + ((chunk ^ sw) << 4)) = u;
-        }
+        // P columns 16c..16c+15 overwrite S columns already held in registers
+        tmem_st16a(tS + c * 16, pk);
       }
+      float sa, sb;
+      up2(sum2, sa, sb);
+      const float sum = sa + sb;
+      tmem_wait_st();
       l_run += sum;
-      fence_proxy_async_smem();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&p_full[s]);
+      if (lane == 0) mbar_arrive(&p_full[t]);
     }
-    if (ok) ok = mbar_wait(o_full, 0, abort_flag, p.status, kDevTimeoutAttn);
+    if (ok) ok = mbar_wait(&o_full[t], 0, abort_flag, p.status, kDevTimeoutAttn);
     if (ok) {
       tc_fence_after();
-      const int qrow = q0 + r;
+      const int qrow = q0 + t * BQ + r;
       const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
       __nv_bfloat16* orow = p.out + (int64_t)qrow * p.ldo + (int64_t)h * D;
 #pragma unroll 1
       for (int c = 0; c < 4; c++) {
         uint32_t o[32];
-        tmem_ld32(tO + lane_addr + c * 32, o);
+        tmem_ld32(tO + c * 32, o);
         tmem_wait_ld();
         if (qrow < p.Lq) {
 #pragma unroll
-          for (int t = 0; t < 4; t++) {
-            uint4 u;
-            u.x = pack_bf16x2(__uint_as_float(o[8 * t + 0]) * inv, __uint_as_float(o[8 * t + 1]) * inv);
-            u.y = pack_bf16x2(__uint_as_float(o[8 * t + 2]) * inv, __uint_as_float(o[8 * t + 3]) * inv);
-            u.z = pack_bf16x2(__uint_as_float(o[8 * t + 4]) * inv, __uint_as_float(o[8 * t + 5]) * inv);
-            u.w = pack_bf16x2(__uint_as_float(o[8 * t + 6]) * inv, __uint_as_float(o[8 * t + 7]) * inv);
-            *(uint4*)(orow + c * 32 + t * 8) = u;
+          for (int u = 0; u < 4; u++) {
+            uint4 w4;
+            w4.x = pack_bf16x2(__uint_as_float(o[8 * u + 0]) * inv, __uint_as_float(o[8 * u + 1]) * inv);
+            w4.y = pack_bf16x2(__uint_as_float(o[8 * u + 2]) * inv, __uint_as_float(o[8 * u + 3]) * inv);
+            w4.z = pack_bf16x2(__uint_as_float(o[8 * u + 4]) * inv, __uint_as_float(o[8 * u + 5]) * inv);
+            w4.w = pack_bf16x2(__uint_as_float(o[8 * u + 6]) * inv, __uint_as_float(o[8 * u + 7]) * inv);
+            *(uint4*)(orow + c * 32 + u * 8) = w4;
           }
         }
       }
@@ -301,7 +396,7 @@ cudaError_t launch_attention(const void* q, const void* k, const void* v, int H,
     if (e != cudaSuccess) return e;
     attr_done[dev & 63] = 1;
   }
-  dim3 grid((unsigned)((Lq + BQ - 1) / BQ), (unsigned)H);
+  dim3 grid((unsigned)((Lq + NT * BQ - 1) / (NT * BQ)), (unsigned)H);
   k_attention<<<grid, kThreads, kSmem, st>>>(tq, tk, tv, p);
   return cudaGetLastError();
 }
