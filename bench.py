@@ -310,6 +310,27 @@ def phys_gpu(local):
     return str(local)
 
 
+# ------------------------------------------------------------------ replica plumbing (one image per GPU)
+def image_seed(rank):
+    """Each rank denoises its own image: seed = rank (offset so it never equals the weight seed)."""
+    return 1000 + rank
+
+
+def max_over_ranks(value, world, device):
+    """Max of a per-rank float over all ranks (the job time is the slowest rank's)."""
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([float(value)], device=device)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def whole_job_rate(units_per_rank, world, ms_max):
+    """Units of all ranks per second, timed by the slowest rank (weak scaling)."""
+    return world * units_per_rank / (ms_max / 1e3)
+
+
 # ------------------------------------------------------------------ main arm
 def main():
     args = parse()
@@ -343,7 +364,7 @@ def main():
 
     model, cfg, keep = build_flux(args.quant, local, seed=0)
 
-    gen = torch.Generator(device=dev).manual_seed(1000 + rank)  # image seed = rank
+    gen = torch.Generator(device=dev).manual_seed(image_seed(rank))
     latent = torch.randn((16, LAT_H, LAT_W), generator=gen, device=dev)
     img0 = mb.sampling.patchify(latent).contiguous()
     img_ids = mb.sampling.img_ids(LAT_H // 2, LAT_W // 2, device=dev)
@@ -378,13 +399,9 @@ def main():
         model.denoise(img, img_ids, txt, txt_ids, y, steps_schedule(args.steps), GUIDANCE)
         e1.record(st)
         barrier()
-    ms = e0.elapsed_time(e1)
-    t = torch.tensor([ms], device=dev)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms_max = float(t.item())
+    ms_max = max_over_ranks(e0.elapsed_time(e1), world, dev)
     finite = bool(torch.isfinite(img).all().item())
-    steps_per_s = world * args.steps / (ms_max / 1e3)
+    steps_per_s = whole_job_rate(args.steps, world, ms_max)
     ms_per_step = ms_max / args.steps
 
     # ---- end to end through the public denoise call: pinned host buffers, copies inside the timed region
@@ -404,13 +421,9 @@ def main():
         h_out.copy_(img, non_blocking=True)
         e1.record(st)
         barrier()
-        ems = e0.elapsed_time(e1)
-        te = torch.tensor([ems], device=dev)
-        if world > 1:
-            dist.all_reduce(te, op=dist.ReduceOp.MAX)
-        ems = float(te.item())
+        ems = max_over_ranks(e0.elapsed_time(e1), world, dev)
         h2d = (h_img.numel() + h_txt.numel() + h_y.numel()) * 4
-        e2e = {"value": world * n_e2e / (ems / 1e3), "unit": "steps/s",
+        e2e = {"value": whole_job_rate(n_e2e, world, ems), "unit": "steps/s",
                "h2d_bytes_per_step": h2d / n_e2e, "d2h_bytes_per_step": h_out.numel() * 4 / n_e2e,
                "images_per_s": world / (ems / 1e3),
                "note": "one mb_flux_denoise call per image (28 steps) from pinned host inputs to the host latent"}
