@@ -436,8 +436,8 @@ def main():
         dist.destroy_process_group()
         return
 
-    cpu = None
-    if not args.no_cpu:
+    cpu = None  # the CPU sample is taken at N=1 only (rank 0 is the only rank there)
+    if not args.no_cpu and world == 1:
         try:
             s = CpuSample(args.quant)
             s.run()

@@ -158,6 +158,38 @@ MB_API mb_status mb_qk_norm_rope(const void* qkv, int64_t M, int64_t ld_qkv, int
 MB_API mb_status mb_attention(const void* q, const void* k, const void* v, int H, int64_t Lq, int64_t Lk,
                        int64_t n_valid_keys, void* out, int64_t ldo, void* stream);
 
+/* K6 with a key order: as mb_qk_norm_rope, but the k and v of sequence row r are
+ * written to row kv_pos[r] (device int32 [L_total], NULL = r) while q stays at row r.
+ * Attention is invariant to the order of its keys, so a caller that places the keys a
+ * mask keeps first can pass n_valid_keys to mb_attention_ex instead of a mask.
+ * Replaces the key-mask half of Qwen's JointAttention (qwen_image/quantized_transformer.rs:
+ * 716-770: QK-RMSNorm, apply_rotary_emb, cat[txt, img] and the [txt_mask, ones] key mask). */
+MB_API mb_status mb_qk_norm_rope_ex(const void* qkv, int64_t M, int64_t ld_qkv, int H, const float* q_scale,
+                                    const float* k_scale, const float* pe, int64_t row_offset, int64_t L_total,
+                                    void* q, void* k, void* v, const int* kv_pos, void* stream);
+
+/* K4 with a split output: rows [0, split_row) of the result go to out (row stride ldo),
+ * rows [split_row, Lq) to out2 from its row 0, so the text and image halves of the joint
+ * sequence land in separate buffers (qwen_image/quantized_transformer.rs:772-780,
+ * narrow(1, 0, txt) / narrow(1, txt, img)). split_row < 0: everything to out. */
+MB_API mb_status mb_attention_ex(const void* q, const void* k, const void* v, int H, int64_t Lq, int64_t Lk,
+                                 int64_t n_valid_keys, void* out, int64_t ldo, int64_t split_row, void* out2,
+                                 void* stream);
+
+/* RMSNorm rows with a learned weight: y bf16 [M, C] = x / sqrt(mean(x^2) + eps) * w;
+ * x f32 [M, C] (row stride ldx), w f32 [C], C % 128 == 0, C <= 8192.
+ * Replaces DynamicRmsNorm::forward (qwen_image/quantized_transformer.rs:102-108; txt_norm). */
+MB_API mb_status mb_rms_norm(const float* x, int64_t M, int64_t C, int64_t ldx, const float* w, float eps, void* y,
+                             int64_t ldy, void* stream);
+
+/* Classifier-free guidance with norm rescale fused with the Euler step, on packed latents
+ * img, cond, uncond f32 [n_tok, C * pp] (feature c * pp + j for pixel j of the patch):
+ * comb = u + g (c - u); pred = comb * ||c|| / max(||comb||, 1e-8) (norms over the C
+ * channels of one pixel); img += pred * dt.
+ * Replaces qwen_image/pipeline.rs:2693-2698 + QwenImageScheduler::step (sampling.rs:117-129). */
+MB_API mb_status mb_cfg_euler_step(float* img, const float* cond, const float* uncond, int64_t n_tok, int C, int pp,
+                                   float guidance, float dt, void* stream);
+
 /* K9. Euler step of the flow-matching loop: img += pred * (t_prev - t_curr), f32 [n].
  * Replaces flux/transformer.rs:84 and qwen_image/sampling.rs:117-129. */
 MB_API mb_status mb_euler_step(float* img, const float* pred, int64_t n, float dt, void* stream);
@@ -210,6 +242,61 @@ MB_API mb_status mb_flux_forward(mb_flux* m, const float* img, const float* img_
 MB_API mb_status mb_flux_denoise(mb_flux* m, float* img, const float* img_ids, int64_t L_img, const float* txt,
                           const float* txt_ids, int64_t L_txt, const float* y, const double* timesteps,
                           int n_timesteps, float guidance, void* stream);
+
+/* ------------------------------------------------------------------ Qwen-Image model */
+
+typedef struct mb_qwen mb_qwen;
+
+typedef struct {
+  int in_channels;          /* 64 = 16 latent channels x patch 2 x 2 */
+  int out_channels;         /* 16 */
+  int patch_size;           /* 2 */
+  int joint_attention_dim;  /* 3584 (text encoder width) */
+  int hidden_size;          /* 3072 = num_heads * 128 */
+  int num_heads;            /* 24 */
+  int num_layers;           /* 60 */
+  int mlp_hidden;           /* 12288 */
+  int axes_dim[3];          /* 16, 56, 56 */
+  int theta;                /* 10000 */
+} mb_qwen_config;
+
+/* Create a Qwen-Image transformer on the current device for up to max_batch sequences
+ * (2 = conditional + unconditional CFG batch) of max_txt + max_img tokens. Replaces
+ * `QuantizedQwenImageTransformer2DModel::new` (qwen_image/quantized_transformer.rs:1004-1040),
+ * the `QwenImageTransformer::Quantized` arm (qwen_image/pipeline.rs:177,258-275). */
+MB_API mb_status mb_qwen_create(const mb_qwen_config* cfg, int64_t max_txt, int64_t max_img, int max_batch,
+                                mb_qwen** out);
+MB_API mb_status mb_qwen_destroy(mb_qwen* m);
+
+/* Hand one GGUF tensor to the model by name (e.g. "transformer_blocks.0.attn.to_q.weight";
+ * names as built at qwen_image/quantized_transformer.rs:577-1040). 1-D tensors (biases, norm
+ * weights) have n_rows = 1. Biases are optional, as in `qlinear` (:79-94). */
+MB_API mb_status mb_qwen_set_tensor(mb_qwen* m, const char* name, int ggml_type, int64_t n_rows, int64_t n_cols,
+                                    const void* data, size_t nbytes, int data_on_device);
+
+/* Names of required tensors the model still lacks (newline separated) — 0 bytes when complete. */
+MB_API mb_status mb_qwen_missing(const mb_qwen* m, char* buf, size_t buflen);
+
+/* One transformer forward over `batch` sequences. Device pointers:
+ *   img f32 [batch, L_img, in_channels] packed latents (L_img = h_tokens * w_tokens, raster order),
+ *   txt f32 [batch, L_txt, joint_attention_dim] encoder states,
+ *   txt_mask u8 [batch, L_txt] (1 = attend; NULL = all ones), pred f32 [batch, L_img, in_channels].
+ * t is the timestep value (sigma * 1000). The mask is read back to the host once per call.
+ * Replaces `QuantizedQwenImageTransformer2DModel::forward` (quantized_transformer.rs:1048-1139)
+ * on packed latents (the patchify / unpatchify reshapes stay with the caller). */
+MB_API mb_status mb_qwen_forward(mb_qwen* m, const float* img, int64_t h_tokens, int64_t w_tokens, const float* txt,
+                                 const uint8_t* txt_mask, int64_t L_txt, int batch, float t, float* pred,
+                                 void* stream);
+
+/* The denoising loop in place on img (f32 [L_img, in_channels], device): for each step i,
+ * t = sigmas[i] * 1000, pred = forward(img); with batch == 2 (txt / txt_mask hold the
+ * conditional then the unconditional prompt) pred = CFG with norm rescale (guidance);
+ * img += pred * (sigmas[i+1] - sigmas[i]). sigmas: host f64 [n_sigmas]. One CUDA graph per
+ * shape is captured on first use and replayed. Replaces the Qwen step loop
+ * (qwen_image/pipeline.rs:2655-2716 without inpainting; scheduler sampling.rs:54-129). */
+MB_API mb_status mb_qwen_denoise(mb_qwen* m, float* img, int64_t h_tokens, int64_t w_tokens, const float* txt,
+                                 const uint8_t* txt_mask, int64_t L_txt, int batch, const double* sigmas, int n_sigmas,
+                                 float guidance, void* stream);
 
 #ifdef __cplusplus
 }

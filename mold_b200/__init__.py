@@ -4,6 +4,7 @@ Host-side mirror of the reference interfaces this library replaces:
   QTensor / QMatMul            candle-core-mold 0.9.10 (QMatMul::from_weights / forward)
   dequantize                   QTensor::dequantize (qwen_image/quantized_transformer.rs:60-67)
   FluxTransformer              crates/mold-inference/src/flux/transformer.rs (forward + denoise)
+  QwenTransformer              qwen_image/quantized_transformer.rs:991-1139 + the pipeline's step loop
   sampling.get_schedule, ...   candle flux::sampling as called in flux/pipeline.rs:2044-2158
 
 All arithmetic runs in libmold_b200.so behind the C ABI (include/mold_b200.h);
@@ -15,7 +16,8 @@ from ._lib import (  # noqa: F401
 )
 from .ops import (  # noqa: F401
     QTensor, QMatMul, init, dequantize, qlinear, qgemv, ln_modulate, rope_table, qk_norm_rope, attention,
-    euler_step, device_status,
+    euler_step, device_status, key_order, rms_norm, cfg_euler_step,
 )
 from .flux import FluxConfig, FluxTransformer  # noqa: F401
+from .qwen import QwenConfig, QwenTransformer  # noqa: F401
 from . import sampling  # noqa: F401

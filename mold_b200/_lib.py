@@ -35,6 +35,10 @@ SIGNATURES = {
     "mb_rope_table": (I32, [P, I64, I32, P, I32, P, P]),
     "mb_qk_norm_rope": (I32, [P, I64, I64, I32, P, P, P, I64, I64, P, P, P, P]),
     "mb_attention": (I32, [P, P, P, I32, I64, I64, I64, P, I64, P]),
+    "mb_qk_norm_rope_ex": (I32, [P, I64, I64, I32, P, P, P, I64, I64, P, P, P, P, P]),
+    "mb_attention_ex": (I32, [P, P, P, I32, I64, I64, I64, P, I64, I64, P, P]),
+    "mb_rms_norm": (I32, [P, I64, I64, I64, P, F32, P, I64, P]),
+    "mb_cfg_euler_step": (I32, [P, P, P, I64, I32, I32, F32, F32, P]),
     "mb_euler_step": (I32, [P, P, I64, F32, P]),
     "mb_flux_create": (I32, [P, I64, I64, P]),
     "mb_flux_destroy": (I32, [P]),
@@ -42,6 +46,12 @@ SIGNATURES = {
     "mb_flux_missing": (I32, [P, P, SZ]),
     "mb_flux_forward": (I32, [P, P, P, I64, P, P, I64, F32, P, F32, P, P]),
     "mb_flux_denoise": (I32, [P, P, P, I64, P, P, I64, P, P, I32, F32, P]),
+    "mb_qwen_create": (I32, [P, I64, I64, I32, P]),
+    "mb_qwen_destroy": (I32, [P]),
+    "mb_qwen_set_tensor": (I32, [P, ctypes.c_char_p, I32, I64, I64, P, SZ, I32]),
+    "mb_qwen_missing": (I32, [P, P, SZ]),
+    "mb_qwen_forward": (I32, [P, P, I64, I64, P, P, I64, I32, F32, P, P]),
+    "mb_qwen_denoise": (I32, [P, P, I64, I64, P, P, I64, I32, P, I32, F32, P]),
 }
 
 
@@ -55,6 +65,12 @@ class FluxConfigC(ctypes.Structure):
     _fields_ = [("in_channels", I32), ("vec_in_dim", I32), ("context_in_dim", I32), ("hidden_size", I32),
                 ("mlp_hidden", I32), ("num_heads", I32), ("depth", I32), ("depth_single", I32),
                 ("axes_dim", I32 * 3), ("theta", I32), ("guidance_embed", I32)]
+
+
+class QwenConfigC(ctypes.Structure):
+    _fields_ = [("in_channels", I32), ("out_channels", I32), ("patch_size", I32), ("joint_attention_dim", I32),
+                ("hidden_size", I32), ("num_heads", I32), ("num_layers", I32), ("mlp_hidden", I32),
+                ("axes_dim", I32 * 3), ("theta", I32)]
 
 
 _lib = None

@@ -320,6 +320,47 @@ mb_status mb_attention(const void* q, const void* k, const void* v, int H, int64
   return MB_OK;
 }
 
+mb_status mb_qk_norm_rope_ex(const void* qkv, int64_t M, int64_t ld_qkv, int H, const float* q_scale,
+                             const float* k_scale, const float* pe, int64_t row_offset, int64_t L_total, void* q,
+                             void* k, void* v, const int* kv_pos, void* stream) {
+  MB_CHECK(qkv && q_scale && k_scale && pe && q && k && v, MB_ERR_INVALID, "NULL argument");
+  MB_CHECK(H > 0 && ld_qkv >= 3LL * H * 128 && ld_qkv % 8 == 0 && row_offset >= 0 && row_offset + M <= L_total,
+           MB_ERR_INVALID, "bad qk_norm_rope shape");
+  MB_CUDA(launch_qk_norm_rope(qkv, M, ld_qkv, H, q_scale, k_scale, pe, row_offset, L_total, q, k, v,
+                              (cudaStream_t)stream, kv_pos));
+  return MB_OK;
+}
+
+mb_status mb_attention_ex(const void* q, const void* k, const void* v, int H, int64_t Lq, int64_t Lk,
+                          int64_t n_valid_keys, void* out, int64_t ldo, int64_t split_row, void* out2, void* stream) {
+  MB_CHECK(q && k && v && out, MB_ERR_INVALID, "NULL argument");
+  MB_CHECK(H > 0 && Lq > 0 && Lk > 0 && ldo >= (int64_t)H * 128 && ldo % 8 == 0, MB_ERR_INVALID,
+           "bad attention shape");
+  MB_CHECK(aligned16(q) && aligned16(k) && aligned16(v) && aligned16(out) && (!out2 || aligned16(out2)),
+           MB_ERR_INVALID, "attention buffers must be 16-byte aligned");
+  MB_CHECK(split_row < 0 || split_row >= Lq || out2, MB_ERR_INVALID, "split_row inside [0, Lq) needs out2");
+  if (n_valid_keys <= 0 || n_valid_keys > Lk) n_valid_keys = Lk;
+  MB_CUDA(launch_attention(q, k, v, H, Lq, Lk, n_valid_keys, out, ldo, (cudaStream_t)stream, split_row, out2));
+  return MB_OK;
+}
+
+mb_status mb_rms_norm(const float* x, int64_t M, int64_t C, int64_t ldx, const float* w, float eps, void* y,
+                      int64_t ldy, void* stream) {
+  MB_CHECK(x && w && y, MB_ERR_INVALID, "NULL argument");
+  MB_CHECK(M >= 0 && C > 0 && C % 128 == 0 && C <= 8192 && ldx >= C && ldx % 4 == 0 && ldy >= C && ldy % 4 == 0,
+           MB_ERR_INVALID, "rms_norm needs C % 128 == 0, C <= 8192, ldx, ldy >= C and multiples of 4");
+  MB_CHECK(aligned16(x) && aligned16(w) && ((uintptr_t)y & 7) == 0, MB_ERR_INVALID, "misaligned rms_norm buffers");
+  MB_CUDA(launch_rms_norm(x, M, C, ldx, w, eps, y, ldy, (cudaStream_t)stream));
+  return MB_OK;
+}
+
+mb_status mb_cfg_euler_step(float* img, const float* cond, const float* uncond, int64_t n_tok, int C, int pp,
+                            float guidance, float dt, void* stream) {
+  MB_CHECK(img && cond && uncond && n_tok >= 0 && C > 0 && pp > 0, MB_ERR_INVALID, "bad cfg_euler arguments");
+  MB_CUDA(launch_cfg_euler(img, cond, uncond, n_tok, C, pp, guidance, dt, nullptr, (cudaStream_t)stream));
+  return MB_OK;
+}
+
 mb_status mb_euler_step(float* img, const float* pred, int64_t n, float dt, void* stream) {
   MB_CHECK(img && pred && n >= 0, MB_ERR_INVALID, "bad euler arguments");
   MB_CUDA(launch_euler(img, pred, n, dt, (cudaStream_t)stream));

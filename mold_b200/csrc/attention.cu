@@ -35,8 +35,10 @@ constexpr int kPolyPerChunk = 6;  // of every 32 exponentials, this many use the
 
 struct Params {
   int H, Lq, Lk, n_valid, n_kv;
-  __nv_bfloat16* out;
+  __nv_bfloat16* out;   // rows [0, split)
+  __nv_bfloat16* out2;  // rows [split, Lq), from its row 0
   int64_t ldo;
+  int split;
   int* status;
 };
 
@@ -336,7 +338,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const int qrow = q0 + t * BQ + r;
       const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
-      __nv_bfloat16* orow = p.out + (int64_t)qrow * p.ldo + (int64_t)h * D;
+      __nv_bfloat16* orow =
+          (qrow < p.split ? p.out + (int64_t)qrow * p.ldo : p.out2 + (int64_t)(qrow - p.split) * p.ldo) + (int64_t)h * D;
 #pragma unroll 1
       for (int c = 0; c < 4; c++) {
         uint32_t o[32];
@@ -368,7 +371,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 }  // namespace attn
 
 cudaError_t launch_attention(const void* q, const void* k, const void* v, int H, int64_t Lq, int64_t Lk,
-                             int64_t n_valid, void* out, int64_t ldo, cudaStream_t st) {
+                             int64_t n_valid, void* out, int64_t ldo, cudaStream_t st, int64_t split_row,
+                             void* out2) {
   using namespace attn;
   CUtensorMap tq, tk, tv;
   const uint64_t rs = D * 2;
@@ -386,6 +390,8 @@ cudaError_t launch_attention(const void* q, const void* k, const void* v, int H,
   p.n_valid = (int)n_valid;
   p.n_kv = (int)((n_valid + BKV - 1) / BKV);
   p.out = (__nv_bfloat16*)out;
+  p.out2 = (__nv_bfloat16*)(out2 ? out2 : out);
+  p.split = (split_row < 0 || split_row > Lq) ? (int)Lq : (int)split_row;
   p.ldo = ldo;
   p.status = device_status_ptr();
   static int attr_done[64];

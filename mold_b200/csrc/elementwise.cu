@@ -129,7 +129,7 @@ __global__ void k_qk_norm_rope(const __nv_bfloat16* __restrict__ qkv, int64_t M,
                                const float* __restrict__ qs, const float* __restrict__ ks,
                                const float* __restrict__ pe, int64_t row_off, int64_t L_total,
                                __nv_bfloat16* __restrict__ q, __nv_bfloat16* __restrict__ k,
-                               __nv_bfloat16* __restrict__ v) {
+                               __nv_bfloat16* __restrict__ v, const int* __restrict__ kv_pos) {
   const int lane = threadIdx.x & 31;
   const int64_t total = M * H;
   const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
@@ -146,6 +146,7 @@ __global__ void k_qk_norm_rope(const __nv_bfloat16* __restrict__ qkv, int64_t M,
     const float4* per = (const float4*)(pe + prow * 256);
     const float4 p0 = per[lane * 2], p1 = per[lane * 2 + 1];
     const int64_t dst = ((int64_t)h * L_total + prow) * 128 + lane * 4;
+    const int64_t dkv = kv_pos ? ((int64_t)h * L_total + kv_pos[prow]) * 128 + lane * 4 : dst;
 #pragma unroll
     for (int which = 0; which < 2; which++) {
       const uint2 r = which ? rk : rq;
@@ -162,19 +163,22 @@ __global__ void k_qk_norm_rope(const __nv_bfloat16* __restrict__ qkv, int64_t M,
       uint2 o;
       o.x = pack_bf16x2(y0, y1);
       o.y = pack_bf16x2(y2, y3);
-      *(uint2*)((which ? k : q) + dst) = o;
+      if (which)
+        *(uint2*)(k + dkv) = o;
+      else
+        *(uint2*)(q + dst) = o;
     }
-    *(uint2*)(v + dst) = rv;
+    *(uint2*)(v + dkv) = rv;
   }
 }
 
 cudaError_t launch_qk_norm_rope(const void* qkv, int64_t M, int64_t ld_qkv, int H, const float* q_scale,
                                 const float* k_scale, const float* pe, int64_t row_offset, int64_t L_total, void* q,
-                                void* k, void* v, cudaStream_t st) {
+                                void* k, void* v, cudaStream_t st, const int* kv_pos) {
   if (M <= 0) return cudaSuccess;
   k_qk_norm_rope<<<grid_cap((M * H + 7) / 8), 256, 0, st>>>(
       (const __nv_bfloat16*)qkv, M, ld_qkv, H, q_scale, k_scale, pe, row_offset, L_total, (__nv_bfloat16*)q,
-      (__nv_bfloat16*)k, (__nv_bfloat16*)v);
+      (__nv_bfloat16*)k, (__nv_bfloat16*)v, kv_pos);
   return cudaGetLastError();
 }
 
@@ -194,6 +198,90 @@ cudaError_t launch_euler(float* img, const float* pred, int64_t n, float dt, cud
 cudaError_t launch_euler_dev(float* img, const float* pred, int64_t n, const float* dt_dev, cudaStream_t st) {
   if (n <= 0) return cudaSuccess;
   k_euler<<<grid_cap((n + 255) / 256), 256, 0, st>>>(img, pred, n, 0.f, dt_dev);
+  return cudaGetLastError();
+}
+
+// ------------------------------------------------------------------ RMSNorm rows
+// y = x / sqrt(mean(x^2) + eps) * w (qwen_image/quantized_transformer.rs:96-108, txt_norm);
+// one warp per row, row in registers (C <= 128 * VEC, C % 128 == 0).
+template <int VEC>
+__global__ void k_rms_norm(const float* __restrict__ x, int64_t M, int C, int64_t ldx, const float* __restrict__ w,
+                           float eps, __nv_bfloat16* __restrict__ y, int64_t ldy) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  const int nvec = C / 128;
+  for (int64_t row = blockIdx.x * (int64_t)(blockDim.x >> 5) + (threadIdx.x >> 5); row < M; row += warps) {
+    const float* xr = x + row * ldx;
+    float4 v[VEC];
+    float q = 0.f;
+#pragma unroll
+    for (int i = 0; i < VEC; i++) {
+      if (i < nvec) {
+        v[i] = *(const float4*)(xr + (i * 32 + lane) * 4);
+        q += (v[i].x * v[i].x + v[i].y * v[i].y) + (v[i].z * v[i].z + v[i].w * v[i].w);
+      }
+    }
+    const float r = 1.f / sqrtf(warp_sum(q) / (float)C + eps);
+    __nv_bfloat16* yr = y + row * ldy;
+#pragma unroll
+    for (int i = 0; i < VEC; i++) {
+      if (i < nvec) {
+        const int c = (i * 32 + lane) * 4;
+        const float4 g = *(const float4*)(w + c);
+        uint2 u;
+        u.x = pack_bf16x2(v[i].x * r * g.x, v[i].y * r * g.y);
+        u.y = pack_bf16x2(v[i].z * r * g.z, v[i].w * r * g.w);
+        *(uint2*)(yr + c) = u;
+      }
+    }
+  }
+}
+
+cudaError_t launch_rms_norm(const float* x, int64_t M, int64_t C, int64_t ldx, const float* w, float eps, void* y,
+                            int64_t ldy, cudaStream_t st) {
+  if (M <= 0) return cudaSuccess;
+  if (C % 128 != 0 || C > 8192) return cudaErrorInvalidValue;
+  const int g = grid_cap((M + 7) / 8);
+  __nv_bfloat16* yb = (__nv_bfloat16*)y;
+  if (C <= 4096)
+    k_rms_norm<32><<<g, 256, 0, st>>>(x, M, (int)C, ldx, w, eps, yb, ldy);
+  else
+    k_rms_norm<64><<<g, 256, 0, st>>>(x, M, (int)C, ldx, w, eps, yb, ldy);
+  return cudaGetLastError();
+}
+
+// ------------------------------------------------------------------ CFG + Euler
+// Packed latents [n_tok, C * pp] (feature = c * pp + j, j the pixel inside the patch).
+// Per pixel: comb = u + g (c - u); pred = comb * ||c|| / max(||comb||, 1e-8) over the C
+// channels (qwen_image/pipeline.rs:2693-2698); img += pred * dt (qwen_image/sampling.rs:117-129).
+__global__ void k_cfg_euler(float* __restrict__ img, const float* __restrict__ cond, const float* __restrict__ unc,
+                            int64_t n_pix, int C, int pp, float g, float dt, const float* __restrict__ dt_dev) {
+  const float d = dt_dev ? *dt_dev : dt;
+  for (int64_t u = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; u < n_pix; u += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t tok = u / pp;
+    const int j = (int)(u % pp);
+    const int64_t base = tok * (int64_t)C * pp + j;
+    float cn = 0.f, bn = 0.f;
+    for (int c = 0; c < C; c++) {
+      const float cv = cond[base + (int64_t)c * pp], uv = unc[base + (int64_t)c * pp];
+      const float b = uv + g * (cv - uv);
+      cn += cv * cv;
+      bn += b * b;
+    }
+    const float f = sqrtf(cn) / fmaxf(sqrtf(bn), 1e-8f);
+    for (int c = 0; c < C; c++) {
+      const int64_t i = base + (int64_t)c * pp;
+      const float cv = cond[i], uv = unc[i];
+      img[i] = img[i] + (uv + g * (cv - uv)) * f * d;
+    }
+  }
+}
+
+cudaError_t launch_cfg_euler(float* img, const float* cond, const float* uncond, int64_t n_tok, int C, int pp,
+                             float guidance, float dt, const float* dt_dev, cudaStream_t st) {
+  const int64_t n = n_tok * pp;
+  if (n <= 0) return cudaSuccess;
+  k_cfg_euler<<<grid_cap((n + 255) / 256), 256, 0, st>>>(img, cond, uncond, n, C, pp, guidance, dt, dt_dev);
   return cudaGetLastError();
 }
 

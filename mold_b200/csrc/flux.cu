@@ -27,6 +27,7 @@
 
 #include "common.cuh"
 #include "internal.h"
+#include "model_util.h"
 
 namespace mb {
 cudaError_t launch_gemv_single(const mb_weight* w, const float* x, int apply_silu, const float* bias, float* y,
@@ -34,70 +35,6 @@ cudaError_t launch_gemv_single(const mb_weight* w, const float* x, int apply_sil
 }
 
 using namespace mb;
-
-namespace {
-
-struct Vec1 {
-  float* dev = nullptr;
-  int64_t n = 0;
-};
-
-__global__ void k_set_scalars(float* dst, float a, float b) {
-  dst[0] = a;
-  dst[1] = b;
-}
-
-// t_cur = sched[i], dt = sched[i+1] - sched[i] (f64), then ++i. Runs at the start of each
-// replayed step so one captured graph serves every step of the schedule.
-__global__ void k_step_prologue(const double* sched, int* counter, float* scal) {
-  const int i = *counter;
-  scal[0] = (float)sched[i];
-  scal[2] = (float)(sched[i + 1] - sched[i]);
-  *counter = i + 1;
-}
-
-struct Seg {  // a row range of the joint sequence
-  int64_t row0, rows;
-};
-
-// Opt-in per-op timing of an eager forward (MOLD_B200_PROFILE=1): CUDA events around every
-// launch, summed per op category and printed to stderr. Off by default; never inside a graph.
-struct OpProfiler {
-  std::vector<std::pair<std::string, std::pair<cudaEvent_t, cudaEvent_t>>> ev;
-  void begin(cudaStream_t st) {
-    cudaEvent_t a, b;
-    cudaEventCreate(&a);
-    cudaEventCreate(&b);
-    cudaEventRecord(a, st);
-    ev.push_back({"", {a, b}});
-  }
-  void end(cudaStream_t st, const std::string& cat) {
-    ev.back().first = cat;
-    cudaEventRecord(ev.back().second.second, st);
-  }
-  void report() {
-    cudaDeviceSynchronize();
-    std::map<std::string, std::pair<int, double>> agg;
-    double tot = 0;
-    for (auto& e : ev) {
-      float ms = 0;
-      cudaEventElapsedTime(&ms, e.second.first, e.second.second);
-      agg[e.first].first++;
-      agg[e.first].second += ms;
-      tot += ms;
-      cudaEventDestroy(e.second.first);
-      cudaEventDestroy(e.second.second);
-    }
-    fprintf(stderr, "[mold_b200 profile] %zu launches, %.3f ms of kernel time\n", ev.size(), tot);
-    for (auto& a : agg)
-      fprintf(stderr, "[mold_b200 profile] %-28s %5d launches %9.3f ms %5.1f%%\n", a.first.c_str(), a.second.first,
-              a.second.second, 100.0 * a.second.second / tot);
-    ev.clear();
-  }
-};
-OpProfiler* g_prof = nullptr;
-
-}  // namespace
 
 struct mb_flux {
   mb_flux_config cfg;
@@ -186,30 +123,6 @@ std::vector<std::pair<std::string, std::vector<int64_t>>> expected_tensors(const
   lin("final_layer.adaLN_modulation.1", 2 * h, h);
   return out;
 }
-
-template <typename T>
-mb_status dalloc(T** p, size_t n) {
-  if (cudaMalloc((void**)p, n * sizeof(T)) != cudaSuccess)
-    return set_error(MB_ERR_NOMEM, "cudaMalloc of " + std::to_string(n * sizeof(T)) + " bytes failed");
-  return MB_OK;
-}
-
-mb_status check_launch(cudaError_t e, const char* what) {
-  if (e != cudaSuccess) return cuda_error(e, what);
-  return MB_OK;
-}
-#define MB_TRY(expr)                 \
-  do {                               \
-    mb_status s__ = (expr);          \
-    if (s__ != MB_OK) return s__;    \
-  } while (0)
-#define TIMED(cat, expr)               \
-  do {                                 \
-    if (g_prof) g_prof->begin(st);     \
-    mb_status s__ = (expr);            \
-    if (s__ != MB_OK) return s__;      \
-    if (g_prof) g_prof->end(st, cat);  \
-  } while (0)
 
 const mb_weight* W(const mb_flux* m, const std::string& n) { return m->mats.at(n); }
 const float* B(const mb_flux* m, const std::string& n) { return m->vecs.at(n).dev; }
@@ -531,26 +444,8 @@ mb_status mb_flux_set_tensor(mb_flux* m, const char* name, int ggml_type, int64_
   MB_CHECK(shape, MB_ERR_INVALID, "unknown FLUX tensor name '" + n + "'");
   if (shape->size() == 1) {
     MB_CHECK(n_rows * n_cols == (*shape)[0], MB_ERR_INVALID, "tensor '" + n + "' has the wrong length");
-    MB_CHECK(ggml_type == MB_GGML_F32 || ggml_type == MB_GGML_F16 || ggml_type == MB_GGML_BF16, MB_ERR_UNSUPPORTED,
-             "1-D tensor '" + n + "' must be F32, F16 or BF16");
-    const int64_t len = (*shape)[0];
-    MB_CHECK((int64_t)nbytes == len * (ggml_type == MB_GGML_F32 ? 4 : 2), MB_ERR_INVALID, "nbytes mismatch for " + n);
     Vec1 v;
-    v.n = len;
-    MB_TRY(dalloc(&v.dev, (size_t)len));
-    void* tmp = nullptr;
-    if (cudaMalloc(&tmp, nbytes) != cudaSuccess) {
-      cudaFree(v.dev);
-      return set_error(MB_ERR_NOMEM, "staging alloc failed");
-    }
-    cudaMemcpy(tmp, data, nbytes, data_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice);
-    cudaError_t e = launch_dequant(ggml_type, tmp, 1, len, len * (ggml_type == MB_GGML_F32 ? 4 : 2), v.dev, 0, 0);
-    cudaDeviceSynchronize();
-    cudaFree(tmp);
-    if (e != cudaSuccess) {
-      cudaFree(v.dev);
-      return cuda_error(e, "vector upload");
-    }
+    MB_TRY(upload_vec1(ggml_type, (*shape)[0], data, nbytes, data_on_device, &v));
     auto it = m->vecs.find(n);
     if (it != m->vecs.end()) cudaFree(it->second.dev);
     m->vecs[n] = v;
@@ -559,32 +454,10 @@ mb_status mb_flux_set_tensor(mb_flux* m, const char* name, int ggml_type, int64_
   MB_CHECK(n_rows == (*shape)[0] && n_cols == (*shape)[1], MB_ERR_INVALID,
            "tensor '" + n + "' has shape [" + std::to_string(n_rows) + ", " + std::to_string(n_cols) + "], expected [" +
                std::to_string((*shape)[0]) + ", " + std::to_string((*shape)[1]) + "]");
-  mb_weight* w = nullptr;
-  MB_TRY(mb_weight_create(ggml_type, n_rows, n_cols, data, nbytes, data_on_device, &w));
-  const bool gemm_ready = (w->type == MB_GGML_Q4_K || w->type == MB_GGML_Q8_0) ? n_cols % 256 == 0
-                                                                                 : w->type == MB_GGML_BF16;
   const bool gemv_only = n.find("_mod.lin") != std::string::npos || n.find("modulation") != std::string::npos ||
                          n.rfind("time_in", 0) == 0 || n.rfind("vector_in", 0) == 0 || n.rfind("guidance_in", 0) == 0;
-  if (!gemm_ready && !gemv_only) {
-    // Rows whose length is not a multiple of the quant block (or F32/F16 storage): keep a BF16 copy
-    // for the tensor-core path (e.g. img_in [3072, 64]).
-    mb_weight* wb = new mb_weight(*w);
-    wb->type = MB_GGML_BF16;
-    wb->row_bytes = n_cols * 2;
-    if (cudaMalloc(&wb->dev, (size_t)n_rows * n_cols * 2) != cudaSuccess) {
-      delete wb;
-      mb_weight_destroy(w);
-      return set_error(MB_ERR_NOMEM, "bf16 copy alloc failed");
-    }
-    cudaError_t e = launch_dequant(w->type, w->dev, n_rows, n_cols, w->row_bytes, wb->dev, 1, 0);
-    cudaDeviceSynchronize();
-    mb_weight_destroy(w);
-    if (e != cudaSuccess) {
-      mb_weight_destroy(wb);
-      return cuda_error(e, "bf16 conversion");
-    }
-    w = wb;
-  }
+  mb_weight* w = nullptr;
+  MB_TRY(upload_matrix(ggml_type, n_rows, n_cols, data, nbytes, data_on_device, !gemv_only, &w));
   auto it = m->mats.find(n);
   if (it != m->mats.end()) mb_weight_destroy(it->second);
   m->mats[n] = w;
@@ -618,10 +491,9 @@ mb_status mb_flux_forward(mb_flux* m, const float* img, const float* img_ids, in
   MB_TRY(check_complete(m));
   cudaStream_t st = (cudaStream_t)stream;
   MB_TRY(prepare(m, img_ids, L_img, txt_ids, L_txt, st));
-  k_set_scalars<<<1, 1, 0, st>>>(m->scal, t, guidance);
-  const char* pe = getenv("MOLD_B200_PROFILE");
+  MB_CUDA(launch_set_scalars(m->scal, t, guidance, st));
   OpProfiler prof;
-  if (pe && pe[0] == '1') g_prof = &prof;
+  if (profile_requested()) g_prof = &prof;
   mb_status fs = run_forward(m, img, L_img, txt, L_txt, y, st);
   if (g_prof) {
     g_prof = nullptr;
@@ -649,7 +521,7 @@ mb_status mb_flux_denoise(mb_flux* m, float* img, const float* img_ids, int64_t 
   }
   MB_CUDA(cudaMemcpyAsync(m->sched, timesteps, n_timesteps * sizeof(double), cudaMemcpyHostToDevice, st));
   MB_CUDA(cudaMemsetAsync(m->counter, 0, sizeof(int), st));
-  k_set_scalars<<<1, 1, 0, st>>>(m->scal, (float)timesteps[0], guidance);
+  MB_CUDA(launch_set_scalars(m->scal, (float)timesteps[0], guidance, st));
   const int64_t n_img = L_img * m->cfg.in_channels;
   const void* key[6] = {img, txt, y, m->sched, nullptr, nullptr};
   const bool reuse = m->graph && m->graph_lt == L_txt && m->graph_li == L_img &&
@@ -660,7 +532,7 @@ mb_status mb_flux_denoise(mb_flux* m, float* img, const float* img_ids, int64_t 
       m->graph = nullptr;
     }
     // Eager warm-up of the step so every kernel attribute is set before capture.
-    k_step_prologue<<<1, 1, 0, st>>>(m->sched, m->counter, m->scal);
+    MB_CUDA(launch_step_prologue(m->sched, m->counter, m->scal, st));
     MB_TRY(run_forward(m, img, L_img, txt, L_txt, y, st));
     MB_CUDA(cudaMemsetAsync(m->counter, 0, sizeof(int), st));
     MB_CUDA(cudaStreamSynchronize(st));
@@ -668,7 +540,7 @@ mb_status mb_flux_denoise(mb_flux* m, float* img, const float* img_ids, int64_t 
     MB_CUDA(cudaStreamCreateWithFlags(&cs, cudaStreamNonBlocking));
     cudaGraph_t g;
     MB_CUDA(cudaStreamBeginCapture(cs, cudaStreamCaptureModeThreadLocal));
-    k_step_prologue<<<1, 1, 0, cs>>>(m->sched, m->counter, m->scal);
+    launch_step_prologue(m->sched, m->counter, m->scal, cs);
     mb_status s = run_forward(m, img, L_img, txt, L_txt, y, cs);
     cudaError_t le = launch_euler_dev(img, m->pred, n_img, m->scal + 2, cs);
     cudaError_t ce = cudaStreamEndCapture(cs, &g);

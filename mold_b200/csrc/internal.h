@@ -104,9 +104,18 @@ cudaError_t launch_rope_table(const float* ids, int64_t L, int n_axes, const int
                               cudaStream_t st);
 cudaError_t launch_qk_norm_rope(const void* qkv, int64_t M, int64_t ld_qkv, int H, const float* q_scale,
                                 const float* k_scale, const float* pe, int64_t row_offset, int64_t L_total, void* q,
-                                void* k, void* v, cudaStream_t st);
+                                void* k, void* v, cudaStream_t st, const int* kv_pos = nullptr);
+// Output rows [0, split_row) go to out, rows [split_row, Lq) to out2 (from its row 0);
+// split_row < 0 writes every row to out.
 cudaError_t launch_attention(const void* q, const void* k, const void* v, int H, int64_t Lq, int64_t Lk,
-                             int64_t n_valid, void* out, int64_t ldo, cudaStream_t st);
+                             int64_t n_valid, void* out, int64_t ldo, cudaStream_t st, int64_t split_row = -1,
+                             void* out2 = nullptr);
+// RMSNorm over rows (f32 statistics, learned weight): y bf16 = x / sqrt(mean(x^2) + eps) * w.
+cudaError_t launch_rms_norm(const float* x, int64_t M, int64_t C, int64_t ldx, const float* w, float eps, void* y,
+                            int64_t ldy, cudaStream_t st);
+// Classifier-free guidance with norm rescale, then Euler, on packed latents [n_tok, C * p * p].
+cudaError_t launch_cfg_euler(float* img, const float* cond, const float* uncond, int64_t n_tok, int C, int pp,
+                             float guidance, float dt, const float* dt_dev, cudaStream_t st);
 cudaError_t launch_euler(float* img, const float* pred, int64_t n, float dt, cudaStream_t st);
 cudaError_t launch_euler_dev(float* img, const float* pred, int64_t n, const float* dt_dev, cudaStream_t st);
 cudaError_t launch_timestep_embedding(const float* t_dev, float scale, float* out, int dim, cudaStream_t st);

@@ -154,27 +154,70 @@ def rope_table(ids, axes_dim=(16, 56, 56), theta=10000):
     return pe
 
 
-def qk_norm_rope(qkv, H, q_scale, k_scale, pe, row_offset=0, L_total=None, q=None, k=None, v=None):
+def qk_norm_rope(qkv, H, q_scale, k_scale, pe, row_offset=0, L_total=None, q=None, k=None, v=None, kv_pos=None):
+    """kv_pos (int32 [L_total], optional): k / v of sequence row r go to row kv_pos[r]."""
     M = qkv.shape[0]
     L_total = L_total or M
     if q is None:
         q = torch.empty((H, L_total, 128), dtype=torch.bfloat16, device=qkv.device)
         k = torch.empty_like(q)
         v = torch.empty_like(q)
-    check(lib().mb_qk_norm_rope(_ptr(qkv), M, qkv.stride(0), H, _ptr(q_scale), _ptr(k_scale), _ptr(pe), row_offset,
-                                L_total, _ptr(q), _ptr(k), _ptr(v), _stream()))
+    if kv_pos is None:
+        check(lib().mb_qk_norm_rope(_ptr(qkv), M, qkv.stride(0), H, _ptr(q_scale), _ptr(k_scale), _ptr(pe),
+                                    row_offset, L_total, _ptr(q), _ptr(k), _ptr(v), _stream()))
+    else:
+        assert kv_pos.dtype == torch.int32 and kv_pos.numel() >= L_total
+        check(lib().mb_qk_norm_rope_ex(_ptr(qkv), M, qkv.stride(0), H, _ptr(q_scale), _ptr(k_scale), _ptr(pe),
+                                       row_offset, L_total, _ptr(q), _ptr(k), _ptr(v), _ptr(kv_pos), _stream()))
     return q, k, v
 
 
-def attention(q, k, v, n_valid_keys=None, out=None):
-    """q [H, Lq, 128], k/v [H, Lk, 128] bf16 -> out [Lq, H*128] bf16."""
+def key_order(txt_mask, l_img):
+    """Key order for a masked joint sequence cat[txt, img]: kept text keys, image keys, masked
+    text keys. Returns (kv_pos int32 [L], n_valid_keys) for qk_norm_rope / attention."""
+    m = torch.as_tensor(txt_mask).to("cpu", torch.bool).reshape(-1)
+    lt = m.numel()
+    nv = int(m.sum())
+    pos = torch.empty(lt + l_img, dtype=torch.int32)
+    pos[:lt][m] = torch.arange(nv, dtype=torch.int32)
+    pos[:lt][~m] = torch.arange(lt - nv, dtype=torch.int32) + nv + l_img
+    pos[lt:] = torch.arange(l_img, dtype=torch.int32) + nv
+    return pos, nv + l_img
+
+
+def attention(q, k, v, n_valid_keys=None, out=None, split_row=None, out2=None):
+    """q [H, Lq, 128], k/v [H, Lk, 128] bf16 -> out [Lq, H*128] bf16. With split_row, rows
+    [split_row, Lq) go to out2 (same row stride) instead."""
     H, Lq, D = q.shape
     Lk = k.shape[1]
     if out is None:
-        out = torch.empty((Lq, H * D), dtype=torch.bfloat16, device=q.device)
-    check(lib().mb_attention(_ptr(q), _ptr(k), _ptr(v), H, Lq, Lk, n_valid_keys or Lk, _ptr(out), out.stride(0),
-                             _stream()))
-    return out
+        out = torch.empty((Lq if split_row is None else split_row, H * D), dtype=torch.bfloat16, device=q.device)
+    if split_row is None:
+        check(lib().mb_attention(_ptr(q), _ptr(k), _ptr(v), H, Lq, Lk, n_valid_keys or Lk, _ptr(out),
+                                 out.stride(0), _stream()))
+        return out
+    if out2 is None:
+        out2 = torch.empty((Lq - split_row, H * D), dtype=torch.bfloat16, device=q.device)
+    assert out2.stride(0) == out.stride(0)
+    check(lib().mb_attention_ex(_ptr(q), _ptr(k), _ptr(v), H, Lq, Lk, n_valid_keys or Lk, _ptr(out), out.stride(0),
+                                split_row, _ptr(out2), _stream()))
+    return out, out2
+
+
+def rms_norm(x, w, eps=1e-6):
+    """DynamicRmsNorm: x f32 [M, C] -> bf16 x / sqrt(mean(x^2) + eps) * w."""
+    M, C = x.shape
+    y = torch.empty((M, C), dtype=torch.bfloat16, device=x.device)
+    check(lib().mb_rms_norm(_ptr(x), M, C, x.stride(0), _ptr(w), float(eps), _ptr(y), y.stride(0), _stream()))
+    return y
+
+
+def cfg_euler_step(img, cond, uncond, guidance, dt, channels=16, pp=4):
+    """img += CFG(cond, uncond) * dt on packed latents [n_tok, channels * pp] (f32, in place)."""
+    n_tok = img.shape[0]
+    check(lib().mb_cfg_euler_step(_ptr(img), _ptr(cond), _ptr(uncond), n_tok, channels, pp, float(guidance),
+                                  float(dt), _stream()))
+    return img
 
 
 def euler_step(img, pred, dt):

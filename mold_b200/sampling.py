@@ -11,6 +11,36 @@ import math
 
 import torch
 
+# ---- Qwen-Image scheduler (qwen_image/sampling.rs:12-129): FlowMatchEulerDiscreteScheduler
+# with exponential shift mu(seq_len) through (256, 0.5) and (8192, 0.9), shift_terminal 0.02.
+QWEN_NUM_TRAIN_TIMESTEPS = 1000
+
+
+def qwen_calculate_shift(image_seq_len, base_seq=256, max_seq=8192, base_shift=0.5, max_shift=0.9):
+    m = (max_shift - base_shift) / (max_seq - base_seq)
+    return image_seq_len * m + (base_shift - m * base_seq)
+
+
+def qwen_sigmas(num_steps, image_seq_len, shift_terminal=0.02):
+    """QwenImageScheduler::new: sigmas = linspace(1, 1/N, N) -> e^mu / (e^mu + (1/s - 1)) ->
+    stretched so the last equals shift_terminal -> append 0. Length N + 1."""
+    if num_steps == 1:
+        s = [1.0]
+    else:
+        step = (1.0 / num_steps - 1.0) / (num_steps - 1)
+        s = [1.0 + step * i for i in range(num_steps)]
+    e = math.exp(qwen_calculate_shift(image_seq_len))
+    s = [e / (e + (1.0 / x - 1.0)) for x in s]
+    one_minus_z = 1.0 - s[-1]
+    if abs(one_minus_z) >= 1e-12:
+        scale = one_minus_z / (1.0 - shift_terminal)
+        s = [1.0 - (1.0 - x) / scale for x in s]
+    return s + [0.0]
+
+
+def qwen_image_seq_len(latent_h, latent_w, patch_size=2):
+    return (latent_h // patch_size) * (latent_w // patch_size)
+
 
 def get_schedule(num_steps, image_seq_len=None, base_shift=0.5, max_shift=1.15):
     ts = [v / num_steps for v in range(num_steps + 1)][::-1]
