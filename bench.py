@@ -46,6 +46,8 @@ def parse():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--quant", default="q4_k", choices=["q4_k", "q8_0"])
+    ap.add_argument("--model", default="flux", choices=["flux", "qwen"],
+                    help="flux: the headline FLUX.1-dev line; qwen: Qwen-Image 1024x1024 with CFG (config 5)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline sample")
     ap.add_argument("--kernels-only", action="store_true", help="only the standalone kernel timings (profiling)")
@@ -187,6 +189,40 @@ def build_flux(quant, device, seed=0):
     return model, cfg, keep
 
 
+# ---- Qwen-Image (config 5): 60 dual-stream blocks, 4096 image + 256 text tokens, CFG batch 2, 30 steps
+Q_TXT, Q_STEPS, Q_GUIDANCE = 256, 30, 4.0
+
+
+def build_qwen(quant, device, seed=0):
+    import torch
+    import mold_b200 as mb
+    cfg = mb.QwenConfig()
+    model = mb.QwenTransformer(cfg, max_txt=Q_TXT, max_img=L_IMG, max_batch=2, device=device)
+    g = torch.Generator(device=f"cuda:{device}")
+    keep = {}
+    gtype = mb.GGML_Q4_K if quant == "q4_k" else mb.GGML_Q8_0
+    for i, (name, shape) in enumerate(mb.qwen.tensor_specs(cfg)):
+        g.manual_seed(seed * 1000003 + i)
+        x = torch.randn(shape, generator=g, device=f"cuda:{device}") * 0.02
+        if len(shape) == 2:
+            if shape[1] % 256 == 0:
+                raw = q4k_quantize_torch(x) if gtype == mb.GGML_Q4_K else q8_0_quantize_torch(x)
+                model.set_tensor(name, (raw, gtype, shape))
+            else:
+                raw = x.bfloat16().view(torch.uint8).reshape(shape[0], -1).contiguous()
+                model.set_tensor(name, (raw, mb.GGML_BF16, shape))
+            if name == "transformer_blocks.0.img_mlp.net.0.proj.weight":
+                keep["mlp0"] = (raw, gtype, shape)
+        else:
+            if "norm" in name:
+                x = x + 1.0
+            model.set_tensor(name, (x.contiguous().view(torch.uint8), mb.GGML_F32, shape))
+        del x
+    assert model.missing() == []
+    torch.cuda.synchronize()
+    return model, cfg, keep
+
+
 # ------------------------------------------------------------------ CPU oracle sample (cpu_baseline / reference arm)
 class CpuSample:
     """One FLUX single-stream block (BASELINE config 1 shape: 512 txt + 1024 img tokens,
@@ -227,20 +263,66 @@ class CpuSample:
             return os.cpu_count()
 
 
+class QwenCpuSample:
+    """One Qwen-Image block at 256 text + 1024 image tokens (hidden 3072) through the numpy
+    oracle; a full CFG step (2 sequences x 60 blocks at 256 + 4096 tokens) is extrapolated by
+    the ratio of algorithmic FLOPs."""
+
+    def __init__(self, quant, l_txt=256, l_img=1024):
+        from oracle import qwen_ref as Q
+        from oracle import flux_ref as F
+        import oracle
+        self.Q = Q
+        self.cfg = Q.QwenConfig(num_layers=1)
+        qt = oracle.GGML_Q4_K if quant == "q4_k" else oracle.GGML_Q8_0
+        self.W = Q.synth_weights(self.cfg, seed=0, qtype=qt, only=lambda n: n.startswith("transformer_blocks.0."))
+        side = int(round(l_img ** 0.5))
+        self.img = oracle.randn(1, (l_img, 3072))
+        self.txt = oracle.randn(2, (l_txt, 3072))
+        self.temb = oracle.randn(3, (3072,))
+        self.mask = np.ones(l_txt, bool)
+        ii, it = Q.rope_ids(1, side, l_img // side, l_txt)
+        self.pe_i = F.embed_nd(ii, self.cfg.axes_dim, self.cfg.theta)
+        self.pe_t = F.embed_nd(it, self.cfg.axes_dim, self.cfg.theta)
+        import mold_b200.qwen as mq
+        full = mq.step_flops(mq.QwenConfig(), Q_TXT, L_IMG, batch=2)
+        L, h, m = l_txt + l_img, 3072, 12288
+        self.ratio = full / (2 * L * h * 4 * h + 2 * L * 2 * h * m + 4 * L * L * h)
+        self.desc = f"1 Qwen-Image block at {l_txt}+{l_img} tokens"
+
+    def run(self):
+        t0 = time.perf_counter()
+        self.Q.block(self.W, "transformer_blocks.0.", self.cfg, self.img, self.txt, self.mask, self.temb,
+                     self.pe_i, self.pe_t)
+        return time.perf_counter() - t0
+
+    cores = staticmethod(CpuSample.cores)
+
+
+def cpu_sample(args):
+    return QwenCpuSample(args.quant) if args.model == "qwen" else CpuSample(args.quant)
+
+
+METRIC = {"flux": "flux_dev_1024_denoise_steps_per_s", "qwen": "qwen_image_1024_cfg_denoise_steps_per_s"}
+WORKLOAD = {"flux": "FLUX.1-dev {q} 1024x1024 (4096 img + 512 txt tokens), 28-step schedule, guidance 3.5, batch 1",
+            "qwen": "Qwen-Image {q} 1024x1024 (4096 img + 256 txt tokens), CFG batch 2 (cond + uncond), "
+                    "30-step schedule, guidance 4.0"}
+
+
 def reference_arm(args, rank):
     if rank != 0:
         return
-    s = CpuSample(args.quant)
+    s = cpu_sample(args)
     for _ in range(max(args.warmup, 1)):
         s.run()
     times = [s.run() for _ in range(args.steps)]
     t_step = statistics.mean(times) * s.ratio
     v = 1.0 / t_step
-    line = {"impl": "reference", "metric": "flux_dev_1024_denoise_steps_per_s", "value": v, "unit": "steps/s",
+    line = {"impl": "reference", "metric": METRIC[args.model], "value": v, "unit": "steps/s",
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": t_step * 1e3,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded N(0,0.02) weights quantized to GGUF, N(0,1) activations)",
-            "config": {"workload": f"FLUX.1-dev {args.quant.upper()} 1024x1024, 512 txt tokens, batch 1",
+            "config": {"workload": WORKLOAD[args.model].format(q=args.quant.upper()),
                        "sample": "%s per step, extrapolated x%.1f by FLOPs" % (s.desc, s.ratio)},
             "cpu_baseline": {"value": v, "unit": "steps/s", "cores": s.cores(), "kind": "port",
                              "sample": "numpy/OpenBLAS oracle, %s per step, extrapolated x%.1f by FLOPs to a "
@@ -251,19 +333,17 @@ def reference_arm(args, rank):
 
 
 # ------------------------------------------------------------------ kernel timings
-def time_kernels(keep, device, peaks, reps=20):
-    """Standalone CUDA-event timings of the dominant kernels on the launching stream."""
+def time_gemm(raw, gtype, shape, M, device, reps=20):
+    """CUDA-event time of one dequant-GEMM launch shape (the weight `raw` [N, K] in GGUF bytes,
+    M activation rows), timed alone on the launching stream after 3 warm-up launches."""
     import torch
     import mold_b200 as mb
     st = torch.cuda.current_stream()
-    out = {}
-    raw, gtype, shape = keep["linear1"]
     N, K = shape
     h = ctypes.c_void_p()
     mb._lib.check(mb.lib().mb_weight_create(gtype, N, K, ctypes.c_void_p(raw.data_ptr()), raw.numel(), 1,
                                             ctypes.byref(h)))
     w = mb.QMatMul(h, N, K, gtype, device)
-    M = L_TXT + L_IMG
     x = torch.randn((M, K), device=f"cuda:{device}").bfloat16()
     y = torch.empty((M, N), device=f"cuda:{device}", dtype=torch.bfloat16)
     for _ in range(3):
@@ -277,16 +357,23 @@ def time_kernels(keep, device, peaks, reps=20):
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / reps
     flops = 2.0 * M * N * K
-    out["gemm_linear1"] = {"shape": [M, N, K], "ms": ms, "tflops": flops / ms / 1e9,
-                           "weight_bytes": raw.numel(), "act_bytes": 2 * M * K + 2 * M * N}
-    # attention over the joint sequence, 24 heads
-    H = 24
-    q = torch.randn((H, M, 128), device=f"cuda:{device}").bfloat16()
+    del w
+    return {"shape": [M, N, K], "ms": ms, "tflops": flops / ms / 1e9, "weight_bytes": raw.numel(),
+            "act_bytes": 2 * M * K + 2 * M * N}
+
+
+def time_attention(L, H, device, reps=20):
+    """CUDA-event time of the joint attention over L tokens, H heads of 128."""
+    import torch
+    import mold_b200 as mb
+    st = torch.cuda.current_stream()
+    q = torch.randn((H, L, 128), device=f"cuda:{device}").bfloat16()
     k = torch.randn_like(q)
     v = torch.randn_like(q)
-    o = torch.empty((M, H * 128), device=f"cuda:{device}", dtype=torch.bfloat16)
+    o = torch.empty((L, H * 128), device=f"cuda:{device}", dtype=torch.bfloat16)
     for _ in range(3):
         mb.attention(q, k, v, out=o)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
     e0.record(st)
     for _ in range(reps):
@@ -294,10 +381,24 @@ def time_kernels(keep, device, peaks, reps=20):
     e1.record(st)
     torch.cuda.synchronize()
     ams = e0.elapsed_time(e1) / reps
-    aflops = 4.0 * M * M * 128 * H
-    out["attention"] = {"shape": [H, M, M, 128], "ms": ams, "tflops": aflops / ams / 1e9}
-    del w
-    return out
+    return {"shape": [H, L, L, 128], "ms": ams, "tflops": 4.0 * L * L * 128 * H / ams / 1e9}
+
+
+def time_kernels(keep, device, peaks, reps=20):
+    """Standalone CUDA-event timings of the dominant FLUX kernels on the launching stream."""
+    raw, gtype, shape = keep["linear1"]
+    return {"gemm_linear1": time_gemm(raw, gtype, shape, L_TXT + L_IMG, device, reps),
+            "attention": time_attention(L_TXT + L_IMG, 24, device, reps)}
+
+
+def profiled_traffic(name):
+    """dram read + write bytes per launch from a committed ncu summary in profiles/ (None if absent)."""
+    import re
+    p = os.path.join(ROOT, "profiles", name)
+    if not os.path.exists(p):
+        return None
+    m = re.search(r"traffic \(read \+ write\) \| ([0-9,]+) B per launch", open(p).read())
+    return int(m.group(1).replace(",", "")) if m else None
 
 
 def phys_gpu(local):
@@ -362,6 +463,9 @@ def main():
             print(json.dumps({"kernels": k}), flush=True)
         return
 
+    if args.model == "qwen":
+        return main_qwen(args, world, rank, local, dev, peaks)
+
     model, cfg, keep = build_flux(args.quant, local, seed=0)
 
     gen = torch.Generator(device=dev).manual_seed(image_seed(rank))
@@ -378,6 +482,8 @@ def main():
         ts = [sched[i % N_SCHEDULE] for i in range(n)]
         return ts + [sched[n % N_SCHEDULE] if n % N_SCHEDULE else 0.0]
 
+    # the dominant kernels timed alone first, at burst clocks (their roofline peak is the burst figure)
+    kern = time_kernels(keep, local, peaks) if rank == 0 else None
     img = img0.clone()
     st = torch.cuda.current_stream()
     # warm-up: first call captures the step graph, then W replays
@@ -428,8 +534,6 @@ def main():
                "images_per_s": world / (ems / 1e3),
                "note": "one mb_flux_denoise call per image (28 steps) from pinned host inputs to the host latent"}
 
-    kern = time_kernels(keep, local, peaks) if rank == 0 else None
-
     if world > 1:
         dist.barrier()
     if rank != 0:
@@ -451,11 +555,17 @@ def main():
 
     g = kern["gemm_linear1"]
     roof = {"bound": "tensor", "achieved": g["tflops"], "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
-            "frac": g["tflops"] / peaks["bf16_tflops"], "traffic": None,
-            "kernel": "k_qgemm<Q4_K> single_blocks.linear1 M=4608 N=21504 K=3072",
-            "peak_source": peaks["source"] + " bf16_tflops (burst; kernel timed alone)"}
+            "frac": g["tflops"] / peaks["bf16_tflops"],
+            "traffic": profiled_traffic("k_qgemm_q4k_linear1_4608x21504x3072.md") if args.quant == "q4_k" else None,
+            "algorithmic_bytes": g["weight_bytes"] + g["act_bytes"],
+            "kernel": "k_qgemm<%s> single_blocks.linear1 M=4608 N=21504 K=3072" % args.quant.upper(),
+            "peak_source": peaks["source"] + " bf16_tflops (burst; kernel timed alone)",
+            "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, one launch of the same shape "
+                              "(profiles/k_qgemm_q4k_linear1_4608x21504x3072.md)"}
     step_flops = mb.flux.step_flops(cfg, L_TXT, L_IMG)
-    n_launch = 1 + 2 + 3 + 4 + cfg.depth * 15 + cfg.depth_single_blocks * 5 + 2 + 1
+    # launches per replayed step: timestep embeddings (2), batched GEMVs (3), casts (2), stems (2),
+    # final LN + linear (2), Euler (1), prologue (1); 11 per double block, 5 per single block
+    n_launch = 13 + cfg.depth * 11 + cfg.depth_single_blocks * 5
     line = {
         "metric": "flux_dev_1024_denoise_steps_per_s", "value": steps_per_s, "unit": "steps/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
@@ -468,6 +578,123 @@ def main():
         "images_per_s": steps_per_s / N_SCHEDULE,
         "step_tflops": step_flops / 1e12, "step_frac_of_peak": step_flops * (steps_per_s / world) / 1e12 /
         peaks["bf16_tflops_sustained"],
+        "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": n_launch * args.steps,
+        "clocks": clk.summary(), "kernels": kern, "finite": finite,
+    }
+    print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def main_qwen(args, world, rank, local, dev, peaks):
+    """Config 5: Qwen-Image 1024x1024, one image per GPU, each step a CFG batch of 2 sequences
+    (conditional + unconditional prompt, 256 text tokens each) through mb_qwen_denoise."""
+    import torch
+    import torch.distributed as dist
+    import mold_b200 as mb
+    model, cfg, keep = build_qwen(args.quant, local, seed=0)
+    gen = torch.Generator(device=dev).manual_seed(image_seed(rank))
+    latent = torch.randn((16, LAT_H, LAT_W), generator=gen, device=dev)
+    img0 = mb.sampling.patchify(latent).contiguous()
+    txt = torch.randn((2, Q_TXT, cfg.joint_attention_dim), generator=gen, device=dev)
+    mask = torch.ones((2, Q_TXT), dtype=torch.uint8, device=dev)
+    hh, ww = LAT_H // 2, LAT_W // 2
+    sig = mb.sampling.qwen_sigmas(Q_STEPS, L_IMG)
+
+    def sigmas(n):
+        s = [sig[i % Q_STEPS] for i in range(n)]
+        return s + [sig[n % Q_STEPS] if n % Q_STEPS else 0.0]
+
+    kern = None  # the dominant kernels timed alone first, at burst clocks
+    if rank == 0:
+        raw, gtype, shape = keep["mlp0"]
+        kern = {"gemm_mlp0": time_gemm(raw, gtype, shape, 2 * L_IMG, local),
+                "attention": time_attention(Q_TXT + L_IMG, 24, local)}
+    st = torch.cuda.current_stream()
+    img = img0.clone()
+    model.denoise(img, txt, mask, hh, ww, sigmas(max(args.warmup, 1)), Q_GUIDANCE)
+    torch.cuda.synchronize()
+    if mb.device_status() != 0:
+        raise RuntimeError("a kernel reported a bounded-wait timeout during warm-up")
+    img.copy_(img0)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    with ClockSampler(phys_gpu(local)) as clk:
+        e0.record(st)
+        model.denoise(img, txt, mask, hh, ww, sigmas(args.steps), Q_GUIDANCE)
+        e1.record(st)
+        barrier()
+    ms_max = max_over_ranks(e0.elapsed_time(e1), world, dev)
+    finite = bool(torch.isfinite(img).all().item())
+    steps_per_s = whole_job_rate(args.steps, world, ms_max)
+
+    e2e = None
+    if not args.no_e2e:
+        h_img = img0.cpu().pin_memory()
+        h_txt = txt.cpu().pin_memory()
+        h_mask = mask.cpu().pin_memory()
+        h_out = torch.empty_like(h_img).pin_memory()
+        barrier()
+        e0.record(st)
+        img.copy_(h_img, non_blocking=True)
+        txt.copy_(h_txt, non_blocking=True)
+        mask.copy_(h_mask, non_blocking=True)
+        model.denoise(img, txt, mask, hh, ww, sig, Q_GUIDANCE)
+        h_out.copy_(img, non_blocking=True)
+        e1.record(st)
+        barrier()
+        ems = max_over_ranks(e0.elapsed_time(e1), world, dev)
+        h2d = h_img.numel() * 4 + h_txt.numel() * 4 + h_mask.numel()
+        e2e = {"value": whole_job_rate(Q_STEPS, world, ems), "unit": "steps/s",
+               "h2d_bytes_per_step": h2d / Q_STEPS, "d2h_bytes_per_step": h_out.numel() * 4 / Q_STEPS,
+               "images_per_s": world / (ems / 1e3),
+               "note": "one mb_qwen_denoise call per image (30 CFG steps) from pinned host inputs to the host latent"}
+
+    if world > 1:
+        dist.barrier()
+    if rank != 0:
+        dist.destroy_process_group()
+        return
+    cpu = None
+    if not args.no_cpu and world == 1:
+        try:
+            s = QwenCpuSample(args.quant)
+            s.run()
+            tt = [s.run() for _ in range(2)]
+            cpu = {"value": 1.0 / (statistics.mean(tt) * s.ratio), "unit": "steps/s", "cores": s.cores(),
+                   "kind": "port",
+                   "sample": "numpy/OpenBLAS oracle: %s (%s), mean of 2 timed runs, extrapolated x%.1f "
+                             "by FLOPs to one full CFG step" % (s.desc, args.quant.upper(), s.ratio)}
+        except Exception as ex:
+            cpu = {"value": None, "unit": "steps/s", "cores": None, "kind": "port", "sample": f"failed: {ex}"}
+    g = kern["gemm_mlp0"]
+    roof = {"bound": "tensor", "achieved": g["tflops"], "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+            "frac": g["tflops"] / peaks["bf16_tflops"], "traffic": None,
+            "algorithmic_bytes": g["weight_bytes"] + g["act_bytes"],
+            "kernel": "k_qgemm<%s> img_mlp.net.0.proj M=8192 N=12288 K=3072" % args.quant.upper(),
+            "peak_source": peaks["source"] + " bf16_tflops (burst; kernel timed alone)"}
+    step_flops = mb.qwen.step_flops(cfg, Q_TXT, L_IMG, batch=2)
+    # per replayed step: temb, 3 GEMVs, RMSNorm, txt_in, 2 casts, img_in, final LN + linear,
+    # CFG-Euler, prologue (13); per block 4 LN, 4 grouped GEMMs, 4 QK-norm, 2 attention
+    n_launch = 13 + cfg.num_layers * 14
+    line = {
+        "metric": METRIC["qwen"], "value": steps_per_s, "unit": "steps/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded N(0,0.02) weights quantized to GGUF on device, N(0,1) latents/text, "
+                "all text tokens kept)",
+        "config": {"workload": WORKLOAD["qwen"].format(q=args.quant.upper()),
+                   "parallelism": f"replicas x{world} (one image per GPU, no collective)",
+                   "l2": "inputs larger than L2 (11.5 GB of weights streamed per step)"},
+        "images_per_s": world / (ms_max / args.steps * Q_STEPS / 1e3),
+        "step_tflops": step_flops / 1e12,
+        "step_frac_of_peak": step_flops * steps_per_s / world / 1e12 / peaks["bf16_tflops"],
         "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": n_launch * args.steps,
         "clocks": clk.summary(), "kernels": kern, "finite": finite,
     }
