@@ -62,6 +62,7 @@ struct mb_flux {
   float* hid = nullptr;    // [3][h]
   float* parts = nullptr;  // [3][h]
   float* mods = nullptr;   // all modulation vectors
+  float* gemv_stage = nullptr;
   std::vector<int64_t> mod_off_double, mod_off_single;
   int64_t mod_off_final = 0, mod_total = 0;
   GemvJob* jobs_dev = nullptr;
@@ -251,9 +252,9 @@ mb_status finalize(mb_flux* m) {
   return MB_OK;
 }
 
-mb_status gemv_table(const mb_flux* m, int table, const GemvInput* ins, int n_in, int max_len, cudaStream_t st) {
+mb_status gemv_table(const mb_flux* m, int table, const GemvInput* ins, int n_in, cudaStream_t st) {
   return check_launch(launch_gemv_batch(m->jobs_dev, 0, m->blocks_dev + 2 * m->block0[table], m->n_blocks[table], ins,
-                                        n_in, max_len, st),
+                                        n_in, m->gemv_stage, st),
                       "gemv batch");
 }
 
@@ -270,17 +271,22 @@ mb_status run_forward(mb_flux* m, const float* img, int64_t Li, const float* txt
     GemvInput in[3] = {};
     in[0].parts[0] = m->temb;
     in[0].n_parts = 1;
+    in[0].len = 256;
     in[1].parts[0] = m->temb + 256;
     in[1].n_parts = 1;
+    in[1].len = 256;
     in[2].parts[0] = y;
     in[2].n_parts = 1;
-    TIMED("gemv stems", gemv_table(m, 0, in, 3, 4096, st));
+    in[2].len = c.vec_in_dim;
+    TIMED("gemv stems", gemv_table(m, 0, in, 3, st));
     for (int i = 0; i < 3; i++) {
       in[i].parts[0] = m->hid + i * h;
       in[i].apply_silu = 1;
+      in[i].len = (int)h;
     }
-    TIMED("gemv stems", gemv_table(m, 1, in, 3, 4096, st));
+    TIMED("gemv stems", gemv_table(m, 1, in, 3, st));
     GemvInput v = {};
+    v.len = (int)h;
     v.parts[0] = m->parts;
     v.parts[1] = m->parts + 2 * h;
     v.n_parts = 2;
@@ -289,7 +295,7 @@ mb_status run_forward(mb_flux* m, const float* img, int64_t Li, const float* txt
       v.n_parts = 3;
     }
     v.apply_silu = 1;
-    TIMED("gemv modulations", gemv_table(m, 2, &v, 1, 4096, st));
+    TIMED("gemv modulations", gemv_table(m, 2, &v, 1, st));
   }
   // ---- stems: txt_in, img_in into the residual stream
   TIMED("cast_f32_bf16", check_launch(launch_cast_f32_bf16(txt, Lt, c.context_in_dim, c.context_in_dim, m->txt_bf, c.context_in_dim, st),
@@ -393,6 +399,7 @@ mb_status mb_flux_create(const mb_flux_config* cfg, int64_t max_txt, int64_t max
   MB_CHECK(cfg->hidden_size % 256 == 0 && cfg->mlp_hidden % 256 == 0, MB_ERR_INVALID,
            "hidden and mlp sizes must be multiples of 256");
   MB_CHECK(cfg->context_in_dim % 64 == 0 && cfg->in_channels % 64 == 0 && cfg->vec_in_dim <= 4096 &&
+               cfg->vec_in_dim % 32 == 0 &&
                cfg->hidden_size <= 4096,
            MB_ERR_INVALID, "unsupported stem sizes");
   MB_CHECK(max_txt > 0 && max_img > 0, MB_ERR_INVALID, "max_txt and max_img must be positive");
@@ -409,7 +416,7 @@ mb_status mb_flux_create(const mb_flux_config* cfg, int64_t max_txt, int64_t max
       (s = dalloc(&m->txt_bf, max_txt * cfg->context_in_dim)) || (s = dalloc(&m->img_bf, max_img * cfg->in_channels)) ||
       (s = dalloc(&m->pred, max_img * cfg->in_channels)) || (s = dalloc(&m->scal, 4)) ||
       (s = dalloc(&m->counter, 1)) || (s = dalloc(&m->temb, 512)) || (s = dalloc(&m->hid, 3 * h)) ||
-      (s = dalloc(&m->parts, 3 * h))) {
+      (s = dalloc(&m->parts, 3 * h)) || (s = dalloc(&m->gemv_stage, gemv_stage_floats()))) {
     mb_flux_destroy(m);
     return s;
   }
@@ -425,7 +432,8 @@ mb_status mb_flux_destroy(mb_flux* m) {
   for (auto& kv : m->mats) mb_weight_destroy(kv.second);
   for (auto& kv : m->vecs) cudaFree(kv.second.dev);
   void* bufs[] = {m->x, m->xm, m->Y, m->q, m->k, m->v, m->pe, m->ids, m->txt_bf, m->img_bf, m->pred, m->scal,
-                  m->counter, m->sched, m->temb, m->hid, m->parts, m->mods, m->jobs_dev, m->blocks_dev};
+                  m->counter, m->sched, m->temb, m->hid, m->parts, m->mods, m->jobs_dev, m->blocks_dev,
+                  m->gemv_stage};
   for (void* b : bufs)
     if (b) cudaFree(b);
   delete m;

@@ -1,21 +1,25 @@
 // K3: batched quantized GEMV (M = 1) for the conditioning path: the stems'
-// MLPs (time_in / guidance_in / vector_in, flux/offload.rs:583-609) and every
-// block's AdaLN modulation silu(vec) -> Linear (flux/offload.rs:117-156).
-// All of a step's modulations depend only on vec, so they run as ONE launch over
-// a job table (one job per weight). Weight-bandwidth bound: each weight byte is
-// read once; one warp per output row, lanes stride over 64-value units.
+// MLPs (time_in / guidance_in / vector_in, flux/offload.rs:583-609; Qwen's timestep MLP)
+// and every block's AdaLN modulation silu(vec) -> Linear (flux/offload.rs:117-156,
+// qwen_image/quantized_transformer.rs:868-879). All of a step's modulations depend only on
+// vec, so they run as ONE launch over a job table (one job per weight), after one small
+// launch that stages the input vectors. Weight-bandwidth bound: each weight byte is read
+// once, with no shared memory or barrier between the loads; the staged x values a lane
+// needs stay in its registers across the rows it serves.
 #include "common.cuh"
 #include "internal.h"
 
 namespace mb {
 namespace gemv {
 
-constexpr int kWarps = 8;
-constexpr int kRowsPerWarp = 4;
+constexpr int kWarps = 4;                                 // warps per block
+constexpr int kRowsPerWarp = kGemvRowsPerBlock / kWarps;  // 8
 constexpr int kMaxLen = 4096;
+constexpr int kMaxInputs = 4;
+constexpr int kStageStride = kMaxLen + kMaxLen / 32;  // x, then its 32-value partial sums
 
 struct Inputs {
-  GemvInput in[4];
+  GemvInput in[kMaxInputs];
 };
 
 MB_DEV float h16(uint32_t v) { return __half2float(__ushort_as_half((unsigned short)(v & 0xFFFFu))); }
@@ -34,19 +38,13 @@ MB_DEV void q4k_sm(int j, uint32_t sy, uint32_t sz, uint32_t sw, int& sc, int& m
   }
 }
 
-// One block = 8 warps x 4 rows of one job. The input vector (silu of the sum of its
-// parts) and its 32-value partial sums are staged once per block in shared memory;
-// each warp streams its 4 weight rows and reuses every staged x value for all 4.
-__global__ void __launch_bounds__(kWarps * 32)
-    k_gemv(const GemvJob* __restrict__ jobs, const int2* __restrict__ blocks, GemvJob inline_job, Inputs ins) {
-  __shared__ __align__(16) float xs[kMaxLen];
-  __shared__ float xsum[kMaxLen / 32];
-  const int2 bj = jobs ? blocks[blockIdx.x] : make_int2(0, blockIdx.x * kGemvRowsPerBlock);
-  const GemvJob job = jobs ? jobs[bj.x] : inline_job;
-  const GemvInput in = ins.in[job.x_slot];
-  const int K = job.n_cols;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int i = threadIdx.x * 4; i < K; i += blockDim.x * 4) {
+// Stage every input vector once: x = silu?(sum of parts) and its 32-value partial sums
+// (the Q4_K min term needs sum(x) per sub-block). Block s handles input s.
+__global__ void k_gemv_stage(Inputs ins, float* __restrict__ stage) {
+  const GemvInput in = ins.in[blockIdx.x];
+  float* xs = stage + (int64_t)blockIdx.x * kStageStride;
+  float* xsum = xs + kMaxLen;
+  for (int i = threadIdx.x * 4; i < in.len; i += blockDim.x * 4) {
     float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
     for (int t = 0; t < in.n_parts; t++) {
       const float4 u = *(const float4*)(in.parts[t] + i);
@@ -58,127 +56,211 @@ __global__ void __launch_bounds__(kWarps * 32)
     *(float4*)(xs + i) = v;
   }
   __syncthreads();
-  for (int c = warp; c < K / 32; c += kWarps) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int c = warp; c < in.len / 32; c += blockDim.x >> 5) {
     float v = xs[c * 32 + lane];
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
     if (lane == 0) xsum[c] = v;
   }
-  __syncthreads();
+}
 
-  const int r0 = bj.y + warp * kRowsPerWarp;
-  if (r0 >= job.n_rows) return;
-  const int nr = min(kRowsPerWarp, job.n_rows - r0);
+// Reduce a per-lane partial over the LPR lanes of one row group and store the row result.
+template <int LPR>
+MB_DEV void finish_rows(const float (&acc)[kRowsPerWarp * LPR / 32], int r0, int sub, int sl, int nr,
+                        const GemvJob& job) {
+  constexpr int NSUB = 32 / LPR, RPL = kRowsPerWarp / NSUB;
+#pragma unroll
+  for (int i = 0; i < RPL; i++) {
+    float v = acc[i];
+#pragma unroll
+    for (int o = LPR / 2; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    const int rr = sub + i * NSUB;
+    if (sl == 0 && rr < nr) job.y[r0 + rr] = v + (job.bias ? job.bias[r0 + rr] : 0.f);
+  }
+}
+
+// Q4_K rows: a group of LPR lanes serves one row; lane sl takes the 64-value units
+// sl, sl + LPR, ... (unit = the low and high nibbles of one 32-byte quant run = sub-blocks
+// 2g and 2g+1), keeps the unit's 64 staged x values in registers and applies them to its
+// RPL rows.
+template <int LPR>
+MB_DEV void rows_q4k(const GemvJob& job, const float* __restrict__ xs, const float* __restrict__ xsum, int r0, int nr,
+                     int lane) {
+  constexpr int NSUB = 32 / LPR, RPL = kRowsPerWarp / NSUB, RB = RPL < 4 ? RPL : 4;
+  const int sub = lane / LPR, sl = lane % LPR;
+  const int U = job.n_cols / 64;
   const uint8_t* wbase = (const uint8_t*)job.w + (int64_t)r0 * job.row_bytes;
-  float acc[kRowsPerWarp] = {0.f, 0.f, 0.f, 0.f};
-  if (job.type == MB_GGML_Q4_K) {
-    for (int u = lane; u < K / 64; u += 32) {
-      const int kb = u >> 2, g = u & 3;
-      const float* xl = xs + kb * 256 + g * 64;
-      float x[64];
+  float acc[RPL];
 #pragma unroll
-      for (int i = 0; i < 16; i++) {
-        const float4 t = *(const float4*)(xl + 4 * i);
-        x[4 * i] = t.x; x[4 * i + 1] = t.y; x[4 * i + 2] = t.z; x[4 * i + 3] = t.w;
-      }
-      const float s_lo = xsum[(kb * 256 + g * 64) / 32], s_hi = xsum[(kb * 256 + g * 64) / 32 + 1];
+  for (int i = 0; i < RPL; i++) acc[i] = 0.f;
+  for (int u = sl; u < U; u += LPR) {
+    const int kb = u >> 2, g = u & 3;
+    float x[64];
 #pragma unroll
-      for (int rr = 0; rr < kRowsPerWarp; rr++) {
-        if (rr < nr) {
-          const uint8_t* b = wbase + (int64_t)rr * job.row_bytes + kb * 144;
-          const uint4 h = __ldg((const uint4*)b);
-          const uint4 qa = __ldg((const uint4*)(b + 16 + 32 * g)), qb = __ldg((const uint4*)(b + 32 + 32 * g));
-          const float d = h16(h.x), dmin = h16(h.x >> 16);
-          int sc0, m0, sc1, m1;
-          q4k_sm(2 * g, h.y, h.z, h.w, sc0, m0);
-          q4k_sm(2 * g + 1, h.y, h.z, h.w, sc1, m1);
-          const uint32_t w[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
-          float dlo = 0.f, dhi = 0.f;
-#pragma unroll
-          for (int i = 0; i < 8; i++) {
-#pragma unroll
-            for (int t = 0; t < 4; t++) {
-              const uint32_t byte = (w[i] >> (8 * t)) & 0xFFu;
-              dlo += (float)(byte & 0xF) * x[4 * i + t];
-              dhi += (float)(byte >> 4) * x[32 + 4 * i + t];
-            }
-          }
-          acc[rr] += d * (float)sc0 * dlo - dmin * (float)m0 * s_lo + d * (float)sc1 * dhi - dmin * (float)m1 * s_hi;
-        }
-      }
+    for (int i = 0; i < 16; i++) {
+      const float4 t = __ldg((const float4*)(xs + u * 64) + i);
+      x[4 * i] = t.x; x[4 * i + 1] = t.y; x[4 * i + 2] = t.z; x[4 * i + 3] = t.w;
     }
-  } else if (job.type == MB_GGML_Q8_0) {
-    for (int bi = lane; bi < K / 32; bi += 32) {
-      const float* xl = xs + bi * 32;
-      float x[32];
+    const float s_lo = __ldg(xsum + 2 * u), s_hi = __ldg(xsum + 2 * u + 1);
+    // rows in batches of RB: all loads of a batch first (rows past the job's end re-read its
+    // last row; finish_rows drops them)
 #pragma unroll
-      for (int i = 0; i < 8; i++) {
-        const float4 t = *(const float4*)(xl + 4 * i);
-        x[4 * i] = t.x; x[4 * i + 1] = t.y; x[4 * i + 2] = t.z; x[4 * i + 3] = t.w;
-      }
+    for (int i0 = 0; i0 < RPL; i0 += RB) {
+    uint4 H[RB], A[RB], B[RB];
 #pragma unroll
-      for (int rr = 0; rr < kRowsPerWarp; rr++) {
-        if (rr < nr) {
-          const uint8_t* b = wbase + (int64_t)rr * job.row_bytes + bi * 34;
-          const uint32_t* a4 = (const uint32_t*)((uintptr_t)b & ~(uintptr_t)3);
-          const bool sh = ((uintptr_t)b & 3) != 0;  // block starts 2 bytes into a word
-          uint32_t wv[10];
-#pragma unroll
-          for (int i = 0; i < 10; i++) wv[i] = __ldg(a4 + i);
-          const float d = sh ? h16(wv[0] >> 16) : h16(wv[0]);
-          float sum = 0.f;
-#pragma unroll
-          for (int i = 0; i < 8; i++) {
-            const uint32_t q = sh ? wv[i + 1] : __byte_perm(wv[i], wv[i + 1], 0x5432);
-#pragma unroll
-            for (int t = 0; t < 4; t++) sum += (float)(int8_t)((q >> (8 * t)) & 0xFF) * x[4 * i + t];
-          }
-          acc[rr] += d * sum;
-        }
-      }
+    for (int j = 0; j < RB; j++) {
+      const int rr = min(sub + (i0 + j) * NSUB, nr - 1);
+      const uint8_t* b = wbase + (int64_t)rr * job.row_bytes + kb * 144;
+      H[j] = __ldg((const uint4*)b);
+      A[j] = __ldg((const uint4*)(b + 16 + 32 * g));
+      B[j] = __ldg((const uint4*)(b + 32 + 32 * g));
     }
-  } else {
-    for (int i = lane; i < K; i += 32) {
-      const float xv = xs[i];
 #pragma unroll
-      for (int rr = 0; rr < kRowsPerWarp; rr++) {
-        if (rr < nr) {
-          const uint8_t* row = wbase + (int64_t)rr * job.row_bytes;
-          float wv;
-          if (job.type == MB_GGML_F32) wv = ((const float*)row)[i];
-          else if (job.type == MB_GGML_F16) wv = __half2float(((const __half*)row)[i]);
-          else wv = __uint_as_float((uint32_t)((const uint16_t*)row)[i] << 16);
-          acc[rr] += wv * xv;
-        }
+    for (int j = 0; j < RB; j++) {
+      const int i = i0 + j;
+      const float d = h16(H[j].x), dmin = h16(H[j].x >> 16);
+      int sc0, m0, sc1, m1;
+      q4k_sm(2 * g, H[j].y, H[j].z, H[j].w, sc0, m0);
+      q4k_sm(2 * g + 1, H[j].y, H[j].z, H[j].w, sc1, m1);
+      float dlo = 0.f, dhi = 0.f;
+#define MB_Q4_WORD(W, I)                                     \
+  _Pragma("unroll") for (int t = 0; t < 4; t++) {            \
+    const uint32_t byte = ((W) >> (8 * t)) & 0xFFu;          \
+    dlo = fmaf((float)(byte & 0xF), x[4 * (I) + t], dlo);    \
+    dhi = fmaf((float)(byte >> 4), x[32 + 4 * (I) + t], dhi); \
+  }
+      MB_Q4_WORD(A[j].x, 0) MB_Q4_WORD(A[j].y, 1) MB_Q4_WORD(A[j].z, 2) MB_Q4_WORD(A[j].w, 3)
+      MB_Q4_WORD(B[j].x, 4) MB_Q4_WORD(B[j].y, 5) MB_Q4_WORD(B[j].z, 6) MB_Q4_WORD(B[j].w, 7)
+#undef MB_Q4_WORD
+      acc[i] += d * (float)sc0 * dlo - dmin * (float)m0 * s_lo + d * (float)sc1 * dhi - dmin * (float)m1 * s_hi;
+    }
+    }
+  }
+  finish_rows<LPR>(acc, r0, sub, sl, nr, job);
+}
+
+// Q8_0 rows: unit = one 34-byte block (fp16 d + 32 int8) of 32 values.
+template <int LPR>
+MB_DEV void rows_q8(const GemvJob& job, const float* __restrict__ xs, int r0, int nr, int lane) {
+  constexpr int NSUB = 32 / LPR, RPL = kRowsPerWarp / NSUB, RB = RPL < 4 ? RPL : 4;
+  const int sub = lane / LPR, sl = lane % LPR;
+  const int U = job.n_cols / 32;
+  const uint8_t* wbase = (const uint8_t*)job.w + (int64_t)r0 * job.row_bytes;
+  float acc[RPL];
+#pragma unroll
+  for (int i = 0; i < RPL; i++) acc[i] = 0.f;
+  for (int u = sl; u < U; u += LPR) {
+    float x[32];
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+      const float4 t = __ldg((const float4*)(xs + u * 32) + i);
+      x[4 * i] = t.x; x[4 * i + 1] = t.y; x[4 * i + 2] = t.z; x[4 * i + 3] = t.w;
+    }
+#pragma unroll
+    for (int i0 = 0; i0 < RPL; i0 += RB) {
+    uint32_t wv[RB][10];
+    bool sh[RB];  // the 34-byte block starts 2 bytes into a word
+#pragma unroll
+    for (int j = 0; j < RB; j++) {
+      const int rr = min(sub + (i0 + j) * NSUB, nr - 1);
+      const uint8_t* b = wbase + (int64_t)rr * job.row_bytes + u * 34;
+      const uint32_t* a4 = (const uint32_t*)((uintptr_t)b & ~(uintptr_t)3);
+      sh[j] = ((uintptr_t)b & 3) != 0;
+#pragma unroll
+      for (int k = 0; k < 10; k++) wv[j][k] = __ldg(a4 + k);
+    }
+#pragma unroll
+    for (int j = 0; j < RB; j++) {
+      const float d = sh[j] ? h16(wv[j][0] >> 16) : h16(wv[j][0]);
+      float sum = 0.f;
+#pragma unroll
+      for (int k = 0; k < 8; k++) {
+        const uint32_t q = sh[j] ? wv[j][k + 1] : __byte_perm(wv[j][k], wv[j][k + 1], 0x5432);
+#pragma unroll
+        for (int t = 0; t < 4; t++) sum = fmaf((float)(int8_t)((q >> (8 * t)) & 0xFF), x[4 * k + t], sum);
+      }
+      acc[i0 + j] += d * sum;
+    }
+    }
+  }
+  finish_rows<LPR>(acc, r0, sub, sl, nr, job);
+}
+
+// F32 / F16 / BF16 rows: the whole warp serves one row at a time.
+MB_DEV void rows_plain(const GemvJob& job, const float* __restrict__ xs, int r0, int nr, int lane) {
+  const uint8_t* wbase = (const uint8_t*)job.w + (int64_t)r0 * job.row_bytes;
+  float acc[kRowsPerWarp];
+#pragma unroll
+  for (int i = 0; i < kRowsPerWarp; i++) acc[i] = 0.f;
+  for (int c = lane; c < job.n_cols; c += 32) {
+    const float xv = __ldg(xs + c);
+#pragma unroll
+    for (int i = 0; i < kRowsPerWarp; i++) {
+      if (i < nr) {
+        const uint8_t* row = wbase + (int64_t)i * job.row_bytes;
+        float wv;
+        if (job.type == MB_GGML_F32) wv = ((const float*)row)[c];
+        else if (job.type == MB_GGML_F16) wv = __half2float(((const __half*)row)[c]);
+        else wv = __uint_as_float((uint32_t)((const uint16_t*)row)[c] << 16);
+        acc[i] = fmaf(wv, xv, acc[i]);
       }
     }
   }
-#pragma unroll
-  for (int rr = 0; rr < kRowsPerWarp; rr++) {
-    float v = acc[rr];
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-    if (lane == 0 && rr < nr) job.y[r0 + rr] = v + (job.bias ? job.bias[r0 + rr] : 0.f);
+  finish_rows<32>(acc, r0, 0, lane, nr, job);
+}
+
+// One block = kWarps warps x kRowsPerWarp rows of one job (blocks[] = (job, first row)).
+__global__ void __launch_bounds__(kWarps * 32, 3)
+    k_gemv(const GemvJob* __restrict__ jobs, const int2* __restrict__ blocks, GemvJob inline_job,
+           const float* __restrict__ stage) {
+  const int2 bj = jobs ? blocks[blockIdx.x] : make_int2(0, blockIdx.x * kGemvRowsPerBlock);
+  const GemvJob job = jobs ? jobs[bj.x] : inline_job;
+  const float* xs = stage + (int64_t)job.x_slot * kStageStride;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int r0 = bj.y + warp * kRowsPerWarp;
+  if (r0 >= job.n_rows) return;
+  const int nr = min(kRowsPerWarp, job.n_rows - r0);
+  if (job.type == MB_GGML_Q4_K) {
+    if ((job.n_cols / 64) % 16 == 0)
+      rows_q4k<16>(job, xs, xs + kMaxLen, r0, nr, lane);
+    else
+      rows_q4k<32>(job, xs, xs + kMaxLen, r0, nr, lane);
+  } else if (job.type == MB_GGML_Q8_0) {
+    if ((job.n_cols / 32) % 32 == 0)
+      rows_q8<32>(job, xs, r0, nr, lane);
+    else
+      rows_q8<16>(job, xs, r0, nr, lane);
+  } else {
+    rows_plain(job, xs, r0, nr, lane);
   }
 }
 
 }  // namespace gemv
 
 cudaError_t launch_gemv_batch(const GemvJob* jobs_dev, int n_jobs, const int* block_job_dev, int n_blocks,
-                              const GemvInput* inputs, int n_inputs, int max_len, cudaStream_t st) {
+                              const GemvInput* inputs, int n_inputs, float* stage, cudaStream_t st) {
   (void)n_jobs;
-  if (max_len > gemv::kMaxLen || n_inputs > 4) return cudaErrorInvalidValue;
+  if (n_inputs < 1 || n_inputs > gemv::kMaxInputs || !stage) return cudaErrorInvalidValue;
   gemv::Inputs ins = {};
-  for (int i = 0; i < n_inputs; i++) ins.in[i] = inputs[i];
+  for (int i = 0; i < n_inputs; i++) {
+    if (inputs[i].len <= 0 || inputs[i].len > gemv::kMaxLen || inputs[i].len % 32) return cudaErrorInvalidValue;
+    ins.in[i] = inputs[i];
+  }
+  gemv::k_gemv_stage<<<n_inputs, 256, 0, st>>>(ins, stage);
   GemvJob dummy = {};
-  gemv::k_gemv<<<n_blocks, gemv::kWarps * 32, 0, st>>>(jobs_dev, (const int2*)block_job_dev, dummy, ins);
+  gemv::k_gemv<<<n_blocks, gemv::kWarps * 32, 0, st>>>(jobs_dev, (const int2*)block_job_dev, dummy, stage);
   return cudaGetLastError();
 }
+
+size_t gemv_stage_floats() { return (size_t)gemv::kMaxInputs * gemv::kStageStride; }
 
 // Single-weight GEMV without a device job table (mb_qgemv).
 cudaError_t launch_gemv_single(const mb_weight* w, const float* x, int apply_silu, const float* bias, float* y,
                                cudaStream_t st) {
-  if (w->n_cols > gemv::kMaxLen) return cudaErrorInvalidValue;
+  if (w->n_cols > gemv::kMaxLen || w->n_cols % 32) return cudaErrorInvalidValue;
+  float* stage = (float*)device_scratch(gemv_stage_floats() * sizeof(float));
+  if (!stage) return cudaErrorMemoryAllocation;
   GemvJob j = {};
   j.w = w->dev;
   j.type = w->type;
@@ -193,8 +275,9 @@ cudaError_t launch_gemv_single(const mb_weight* w, const float* x, int apply_sil
   ins.in[0].n_parts = 1;
   ins.in[0].apply_silu = apply_silu;
   ins.in[0].len = (int)w->n_cols;
+  gemv::k_gemv_stage<<<1, 256, 0, st>>>(ins, stage);
   const int blocks = (int)((w->n_rows + kGemvRowsPerBlock - 1) / kGemvRowsPerBlock);
-  gemv::k_gemv<<<blocks, gemv::kWarps * 32, 0, st>>>(nullptr, nullptr, j, ins);
+  gemv::k_gemv<<<blocks, gemv::kWarps * 32, 0, st>>>(nullptr, nullptr, j, stage);
   return cudaGetLastError();
 }
 

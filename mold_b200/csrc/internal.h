@@ -94,9 +94,12 @@ struct GemvInput {
   int len;
 };
 constexpr int kGemvRowsPerBlock = 32;  // rows of one job handled by one GEMV block
-// Runs a batch of GEMV jobs in one launch. jobs_dev / block_job_dev live in device memory.
+// Runs a batch of GEMV jobs: one launch stages the inputs (len % 32 == 0, <= 4096) into
+// `stage` (gemv_stage_floats() floats, owned by the caller), one launch runs every job.
+// jobs_dev / block_job_dev live in device memory.
 cudaError_t launch_gemv_batch(const GemvJob* jobs_dev, int n_jobs, const int* block_job_dev, int n_blocks,
-                              const GemvInput* inputs, int n_inputs, int max_len, cudaStream_t st);
+                              const GemvInput* inputs, int n_inputs, float* stage, cudaStream_t st);
+size_t gemv_stage_floats();
 
 cudaError_t launch_ln_modulate(const float* x, int64_t M, int64_t C, int64_t ldx, const float* shift,
                                const float* scale, void* y, int64_t ldy, cudaStream_t st);

@@ -78,6 +78,7 @@ struct mb_qwen {
   float* hid = nullptr;    // [h]
   float* tvec = nullptr;   // [h]  timestep embedding
   float* mods = nullptr;
+  float* gemv_stage = nullptr;
   std::vector<int64_t> mod_off;
   int64_t mod_off_final = 0;
   GemvJob* jobs_dev = nullptr;
@@ -262,7 +263,7 @@ mb_status finalize(mb_qwen* m) {
 
 mb_status gemv_table(const mb_qwen* m, int table, const GemvInput* in, cudaStream_t st) {
   return check_launch(launch_gemv_batch(m->jobs_dev, 0, m->blocks_dev + 2 * m->block0[table], m->n_blocks[table], in,
-                                        1, 4096, st),
+                                        1, m->gemv_stage, st),
                       "gemv batch");
 }
 
@@ -334,7 +335,9 @@ mb_status run_forward(mb_qwen* m, const float* img, int64_t img_stride, int64_t 
     GemvInput in = {};
     in.parts[0] = m->temb;
     in.n_parts = 1;
+    in.len = 256;
     TIMED("gemv timestep", gemv_table(m, 0, &in, st));
+    in.len = (int)h;
     in.parts[0] = m->hid;
     in.apply_silu = 1;
     TIMED("gemv timestep", gemv_table(m, 1, &in, st));
@@ -521,7 +524,7 @@ mb_status mb_qwen_create(const mb_qwen_config* cfg, int64_t max_txt, int64_t max
       (s = dalloc(&m->img_bf, max_batch * max_img * cfg->in_channels)) ||
       (s = dalloc(&m->pred, max_batch * max_img * cfg->in_channels)) || (s = dalloc(&m->scal, 4)) ||
       (s = dalloc(&m->counter, 1)) || (s = dalloc(&m->temb, 256)) || (s = dalloc(&m->hid, h)) ||
-      (s = dalloc(&m->tvec, h))) {
+      (s = dalloc(&m->tvec, h)) || (s = dalloc(&m->gemv_stage, gemv_stage_floats()))) {
     mb_qwen_destroy(m);
     return s;
   }
@@ -540,7 +543,7 @@ mb_status mb_qwen_destroy(mb_qwen* m) {
   }
   void* bufs[] = {m->x,       m->xm,    m->Y,   m->q,    m->k,    m->v,     m->pe,   m->ids,
                   m->kv_pos,  m->txt_bf, m->img_bf, m->pred, m->scal, m->counter, m->sched, m->temb,
-                  m->hid,     m->tvec,  m->mods, m->jobs_dev, m->blocks_dev};
+                  m->hid,     m->tvec,  m->mods, m->jobs_dev, m->blocks_dev, m->gemv_stage};
   for (void* b : bufs)
     if (b) cudaFree(b);
   delete m;
