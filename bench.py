@@ -564,8 +564,8 @@ def main():
                               "(profiles/k_qgemm_q4k_linear1_4608x21504x3072.md)"}
     step_flops = mb.flux.step_flops(cfg, L_TXT, L_IMG)
     # launches per replayed step: timestep embeddings (2), batched GEMVs (3), casts (2), stems (2),
-    # final LN + linear (2), Euler (1), prologue (1); 11 per double block, 5 per single block
-    n_launch = 13 + cfg.depth * 11 + cfg.depth_single_blocks * 5
+    # final LN + linear (2), Euler (1), prologue (1); 8 per double block, 5 per single block
+    n_launch = 13 + cfg.depth * 8 + cfg.depth_single_blocks * 5
     line = {
         "metric": "flux_dev_1024_denoise_steps_per_s", "value": steps_per_s, "unit": "steps/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
@@ -681,8 +681,8 @@ def main_qwen(args, world, rank, local, dev, peaks):
             "peak_source": peaks["source"] + " bf16_tflops (burst; kernel timed alone)"}
     step_flops = mb.qwen.step_flops(cfg, Q_TXT, L_IMG, batch=2)
     # per replayed step: temb, 3 GEMVs, RMSNorm, txt_in, 2 casts, img_in, final LN + linear,
-    # CFG-Euler, prologue (13); per block 4 LN, 4 grouped GEMMs, 4 QK-norm, 2 attention
-    n_launch = 13 + cfg.num_layers * 14
+    # CFG-Euler, prologue (13); per block 2 LN, 4 grouped GEMMs, 1 QK-norm, 2 attention
+    n_launch = 13 + cfg.num_layers * 9
     line = {
         "metric": METRIC["qwen"], "value": steps_per_s, "unit": "steps/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,

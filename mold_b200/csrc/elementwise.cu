@@ -21,16 +21,24 @@ MB_DEV float warp_sum(float v) {
 }
 
 // ------------------------------------------------------------------ K5
-// y = LN(x) * (1 + scale) + shift, LN without affine, eps 1e-6 (flux/offload.rs:286-295).
-// One warp per row; the row stays in registers (C <= 32*4*VEC).
+// y = LN(x) * (1 + scale) + shift, LN without affine, eps 1e-6 (flux/offload.rs:286-295,
+// qwen_image/quantized_transformer.rs:136-151). One warp per row, the row in registers
+// (C <= 128 * VEC); the rows of up to kMaxSegs segments (e.g. the text and image streams,
+// each with its own modulation vectors) run in one launch.
 template <int VEC>
-__global__ void k_ln_modulate(const float* __restrict__ x, int64_t M, int C, int64_t ldx,
-                              const float* __restrict__ shift, const float* __restrict__ scale,
+__global__ void k_ln_modulate(const float* __restrict__ x, int C, int64_t ldx, LnSegs segs,
                               __nv_bfloat16* __restrict__ y, int64_t ldy) {
   const int lane = threadIdx.x & 31;
   const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
   const int nvec = C / 128;  // float4 per lane actually used (<= VEC)
-  for (int64_t row = blockIdx.x * (int64_t)(blockDim.x >> 5) + (threadIdx.x >> 5); row < M; row += warps) {
+  int64_t total = 0;
+  for (int i = 0; i < segs.n; i++) total += segs.s[i].rows;
+  for (int64_t u = blockIdx.x * (int64_t)(blockDim.x >> 5) + (threadIdx.x >> 5); u < total; u += warps) {
+    int si = 0;
+    int64_t r = u;
+    while (si + 1 < segs.n && r >= segs.s[si].rows) r -= segs.s[si++].rows;
+    const LnSeg sg = segs.s[si];
+    const int64_t row = sg.row0 + r;
     const float* xr = x + row * ldx;
     float4 v[VEC];
     float s = 0.f;
@@ -57,31 +65,42 @@ __global__ void k_ln_modulate(const float* __restrict__ x, int64_t M, int C, int
     for (int i = 0; i < VEC; i++) {
       if (i < nvec) {
         const int c = (i * 32 + lane) * 4;
-        const float4 sc = *(const float4*)(scale + c), sh = *(const float4*)(shift + c);
+        const float4 sc = __ldg((const float4*)(sg.scale + c)), sh = __ldg((const float4*)(sg.shift + c));
         const float o0 = (v[i].x - mean) * rstd * (1.f + sc.x) + sh.x;
         const float o1 = (v[i].y - mean) * rstd * (1.f + sc.y) + sh.y;
         const float o2 = (v[i].z - mean) * rstd * (1.f + sc.z) + sh.z;
         const float o3 = (v[i].w - mean) * rstd * (1.f + sc.w) + sh.w;
-        uint2 u;
-        u.x = pack_bf16x2(o0, o1);
-        u.y = pack_bf16x2(o2, o3);
-        *(uint2*)(yr + c) = u;
+        uint2 w;
+        w.x = pack_bf16x2(o0, o1);
+        w.y = pack_bf16x2(o2, o3);
+        *(uint2*)(yr + c) = w;
       }
     }
   }
 }
 
-cudaError_t launch_ln_modulate(const float* x, int64_t M, int64_t C, int64_t ldx, const float* shift,
-                               const float* scale, void* y, int64_t ldy, cudaStream_t st) {
+cudaError_t launch_ln_modulate_segs(const float* x, int64_t C, int64_t ldx, const LnSegs& segs, void* y, int64_t ldy,
+                                    cudaStream_t st) {
+  int64_t M = 0;
+  for (int i = 0; i < segs.n; i++) M += segs.s[i].rows;
   if (M <= 0) return cudaSuccess;
+  if (segs.n < 1 || segs.n > kMaxSegs || C % 128 != 0 || C > 8192) return cudaErrorInvalidValue;
   const int threads = 256;
   const int g = grid_cap((M + 7) / 8);
   __nv_bfloat16* yb = (__nv_bfloat16*)y;
   if (C <= 3072)
-    k_ln_modulate<24><<<g, threads, 0, st>>>(x, M, (int)C, ldx, shift, scale, yb, ldy);
+    k_ln_modulate<24><<<g, threads, 0, st>>>(x, (int)C, ldx, segs, yb, ldy);
   else
-    k_ln_modulate<64><<<g, threads, 0, st>>>(x, M, (int)C, ldx, shift, scale, yb, ldy);
+    k_ln_modulate<64><<<g, threads, 0, st>>>(x, (int)C, ldx, segs, yb, ldy);
   return cudaGetLastError();
+}
+
+cudaError_t launch_ln_modulate(const float* x, int64_t M, int64_t C, int64_t ldx, const float* shift,
+                               const float* scale, void* y, int64_t ldy, cudaStream_t st) {
+  LnSegs s = {};
+  s.n = 1;
+  s.s[0] = {0, M, shift, scale};
+  return launch_ln_modulate_segs(x, C, ldx, s, y, ldy, st);
 }
 
 // ------------------------------------------------------------------ RoPE table
@@ -122,64 +141,108 @@ cudaError_t launch_rope_table(const float* ids, int64_t L, int n_axes, const int
 }
 
 // ------------------------------------------------------------------ K6
-// qkv row block [M, 3*H*128] bf16 -> RMSNorm(q), RMSNorm(k) (eps 1e-6, learned scale),
-// RoPE on interleaved pairs, v copied; outputs [H, L_total, 128] bf16 at rows row_offset+.
-// One warp per (row, head); lane holds 4 consecutive features (two rope pairs).
-__global__ void k_qk_norm_rope(const __nv_bfloat16* __restrict__ qkv, int64_t M, int64_t ld, int H,
-                               const float* __restrict__ qs, const float* __restrict__ ks,
-                               const float* __restrict__ pe, int64_t row_off, int64_t L_total,
+// qkv row block [rows, 3*H*128] bf16 -> RMSNorm(q), RMSNorm(k) (eps 1e-6, learned scale),
+// RoPE on interleaved pairs, v copied; outputs [H, L_total, 128] bf16 (flux/offload.rs:56-72,
+// 191-201; qwen_image/quantized_transformer.rs:716-753). One warp per (sequence row, group of
+// 8 heads): lane l holds features 4l..4l+3 (two rope pairs) of each head, so the row's RoPE
+// entries are loaded once per 8 heads, and all 8 heads' loads are issued first.
+// Rows of up to kMaxSegs segments (streams, batch items) run in one launch.
+__global__ void k_qk_norm_rope(const __nv_bfloat16* __restrict__ qkv, int64_t ld, int H,
+                               const float* __restrict__ pe, int64_t L_total, QkSegs segs,
                                __nv_bfloat16* __restrict__ q, __nv_bfloat16* __restrict__ k,
-                               __nv_bfloat16* __restrict__ v, const int* __restrict__ kv_pos) {
+                               __nv_bfloat16* __restrict__ v) {
   const int lane = threadIdx.x & 31;
-  const int64_t total = M * H;
   const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
-  const float4 qsc = *(const float4*)(qs + lane * 4);
-  const float4 ksc = *(const float4*)(ks + lane * 4);
+  int64_t total = 0;
+  for (int i = 0; i < segs.n; i++) total += segs.s[i].rows;
+  const int groups = (H + 7) / 8;
+  total *= groups;
   for (int64_t u = blockIdx.x * (int64_t)(blockDim.x >> 5) + (threadIdx.x >> 5); u < total; u += warps) {
-    const int64_t row = u / H;
-    const int h = (int)(u % H);
-    const __nv_bfloat16* src = qkv + row * ld + h * 128 + lane * 4;
-    const uint2 rq = *(const uint2*)(src);
-    const uint2 rk = *(const uint2*)(src + (int64_t)H * 128);
-    const uint2 rv = *(const uint2*)(src + (int64_t)2 * H * 128);
-    const int64_t prow = row_off + row;
+    int si = 0;
+    int64_t r = u / groups;
+    const int h0 = (int)(u % groups) * 8;
+    while (si + 1 < segs.n && r >= segs.s[si].rows) r -= segs.s[si++].rows;
+    const QkSeg sg = segs.s[si];
+    const int64_t prow = sg.pos0 + r;  // sequence position: RoPE row and q row
+    const int64_t kvrow = sg.kv_pos ? sg.kv_pos[prow] : prow;
+    const __nv_bfloat16* src = qkv + (sg.row0 + r) * ld + lane * 4;
     const float4* per = (const float4*)(pe + prow * 256);
-    const float4 p0 = per[lane * 2], p1 = per[lane * 2 + 1];
-    const int64_t dst = ((int64_t)h * L_total + prow) * 128 + lane * 4;
-    const int64_t dkv = kv_pos ? ((int64_t)h * L_total + kv_pos[prow]) * 128 + lane * 4 : dst;
+    const float4 p0 = __ldg(per + lane * 2), p1 = __ldg(per + lane * 2 + 1);
+    const float4 qsc = __ldg((const float4*)(sg.qs + lane * 4));
+    const float4 ksc = __ldg((const float4*)(sg.ks + lane * 4));
+    __nv_bfloat16* qb = q + sg.off;
+    __nv_bfloat16* kb = k + sg.off;
+    __nv_bfloat16* vb = v + sg.off;
+    {
+      const int nh = min(8, H - h0);
+      uint2 rq[8], rk[8], rv[8];
 #pragma unroll
-    for (int which = 0; which < 2; which++) {
-      const uint2 r = which ? rk : rq;
-      const float4 sc = which ? ksc : qsc;
-      float x0 = bf16_lo(r.x), x1 = bf16_hi(r.x), x2 = bf16_lo(r.y), x3 = bf16_hi(r.y);
-      const float ms = warp_sum((x0 * x0 + x1 * x1) + (x2 * x2 + x3 * x3)) * (1.f / 128.f);
-      const float rinv = 1.f / sqrtf(ms + 1e-6f);
-      x0 = x0 * rinv * sc.x;
-      x1 = x1 * rinv * sc.y;
-      x2 = x2 * rinv * sc.z;
-      x3 = x3 * rinv * sc.w;
-      const float y0 = p0.x * x0 + p0.y * x1, y1 = p0.z * x0 + p0.w * x1;
-      const float y2 = p1.x * x2 + p1.y * x3, y3 = p1.z * x2 + p1.w * x3;
-      uint2 o;
-      o.x = pack_bf16x2(y0, y1);
-      o.y = pack_bf16x2(y2, y3);
-      if (which)
-        *(uint2*)(k + dkv) = o;
-      else
-        *(uint2*)(q + dst) = o;
+      for (int j = 0; j < 8; j++) {
+        if (j < nh) {
+          const __nv_bfloat16* sp = src + (h0 + j) * 128;
+          rq[j] = *(const uint2*)(sp);
+          rk[j] = *(const uint2*)(sp + (int64_t)H * 128);
+          rv[j] = *(const uint2*)(sp + (int64_t)2 * H * 128);
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < 8; j++) {
+        if (j < nh) {
+          const int h = h0 + j;
+          const int64_t dq = ((int64_t)h * L_total + prow) * 128 + lane * 4;
+          const int64_t dkv = ((int64_t)h * L_total + kvrow) * 128 + lane * 4;
+#pragma unroll
+          for (int which = 0; which < 2; which++) {
+            const uint2 rr = which ? rk[j] : rq[j];
+            const float4 sc = which ? ksc : qsc;
+            float x0 = bf16_lo(rr.x), x1 = bf16_hi(rr.x), x2 = bf16_lo(rr.y), x3 = bf16_hi(rr.y);
+            const float ms = warp_sum((x0 * x0 + x1 * x1) + (x2 * x2 + x3 * x3)) * (1.f / 128.f);
+            const float rinv = 1.f / sqrtf(ms + 1e-6f);
+            x0 = x0 * rinv * sc.x;
+            x1 = x1 * rinv * sc.y;
+            x2 = x2 * rinv * sc.z;
+            x3 = x3 * rinv * sc.w;
+            const float y0 = p0.x * x0 + p0.y * x1, y1 = p0.z * x0 + p0.w * x1;
+            const float y2 = p1.x * x2 + p1.y * x3, y3 = p1.z * x2 + p1.w * x3;
+            uint2 o;
+            o.x = pack_bf16x2(y0, y1);
+            o.y = pack_bf16x2(y2, y3);
+            if (which)
+              *(uint2*)(kb + dkv) = o;
+            else
+              *(uint2*)(qb + dq) = o;
+          }
+          *(uint2*)(vb + dkv) = rv[j];
+        }
+      }
     }
-    *(uint2*)(v + dkv) = rv;
   }
+}
+
+cudaError_t launch_qk_norm_rope_segs(const void* qkv, int64_t ld_qkv, int H, const float* pe, int64_t L_total,
+                                     const QkSegs& segs, void* q, void* k, void* v, cudaStream_t st) {
+  int64_t M = 0;
+  for (int i = 0; i < segs.n; i++) M += segs.s[i].rows;
+  if (M <= 0) return cudaSuccess;
+  if (segs.n < 1 || segs.n > kMaxSegs) return cudaErrorInvalidValue;
+  k_qk_norm_rope<<<grid_cap((M * ((H + 7) / 8) + 7) / 8), 256, 0, st>>>((const __nv_bfloat16*)qkv, ld_qkv, H, pe, L_total, segs,
+                                                        (__nv_bfloat16*)q, (__nv_bfloat16*)k, (__nv_bfloat16*)v);
+  return cudaGetLastError();
 }
 
 cudaError_t launch_qk_norm_rope(const void* qkv, int64_t M, int64_t ld_qkv, int H, const float* q_scale,
                                 const float* k_scale, const float* pe, int64_t row_offset, int64_t L_total, void* q,
                                 void* k, void* v, cudaStream_t st, const int* kv_pos) {
-  if (M <= 0) return cudaSuccess;
-  k_qk_norm_rope<<<grid_cap((M * H + 7) / 8), 256, 0, st>>>(
-      (const __nv_bfloat16*)qkv, M, ld_qkv, H, q_scale, k_scale, pe, row_offset, L_total, (__nv_bfloat16*)q,
-      (__nv_bfloat16*)k, (__nv_bfloat16*)v, kv_pos);
-  return cudaGetLastError();
+  QkSegs s = {};
+  s.n = 1;
+  s.s[0].row0 = 0;
+  s.s[0].rows = M;
+  s.s[0].pos0 = row_offset;
+  s.s[0].off = 0;
+  s.s[0].kv_pos = kv_pos;
+  s.s[0].qs = q_scale;
+  s.s[0].ks = k_scale;
+  return launch_qk_norm_rope_segs(qkv, ld_qkv, H, pe, L_total, s, q, k, v, st);
 }
 
 // ------------------------------------------------------------------ K9

@@ -312,22 +312,31 @@ mb_status run_forward(mb_flux* m, const float* img, int64_t Li, const float* txt
     const float* md = m->mods + m->mod_off_double[i];
     const float* mos[2] = {md + 6 * h, md};  // txt_mod, img_mod
     const std::string S[2] = {"txt", "img"};
-    for (int s = 0; s < 2; s++)
-      TIMED("ln_modulate", check_launch(launch_ln_modulate(m->x + segs[s].row0 * h, segs[s].rows, h, h, mos[s],
-                                                           mos[s] + h, m->xm + segs[s].row0 * h, h, st),
-                                        "ln_mod1"));
+    {
+      LnSegs ls = {};
+      ls.n = 2;
+      for (int s = 0; s < 2; s++) ls.s[s] = {segs[s].row0, segs[s].rows, mos[s], mos[s] + h};
+      TIMED("ln_modulate", check_launch(launch_ln_modulate_segs(m->x, h, h, ls, m->xm, h, st), "ln_mod1"));
+    }
     {
       const void* xs[2] = {m->xm, m->xm + Lt * h};
       void* ys[2] = {m->Y, m->Y + Lt * ldY};
       const float* gates[2] = {nullptr, nullptr};
       MB_TRY(linear_pair(m, p, "_attn.qkv", segs, xs, h, ys, ldY, true, MB_EPI_NONE, gates, st));
     }
-    for (int s = 0; s < 2; s++)
-      TIMED("qk_norm_rope", check_launch(launch_qk_norm_rope(m->Y + segs[s].row0 * ldY, segs[s].rows, ldY, (int)H,
-                                                             B(m, p + S[s] + "_attn.norm.query_norm.scale"),
-                                                             B(m, p + S[s] + "_attn.norm.key_norm.scale"), m->pe,
-                                                             segs[s].row0, L, m->q, m->k, m->v, st),
-                                        "qk_norm_rope"));
+    {
+      QkSegs qs = {};
+      qs.n = 2;
+      for (int s = 0; s < 2; s++) {
+        qs.s[s].row0 = segs[s].row0;
+        qs.s[s].rows = segs[s].rows;
+        qs.s[s].pos0 = segs[s].row0;
+        qs.s[s].qs = B(m, p + S[s] + "_attn.norm.query_norm.scale");
+        qs.s[s].ks = B(m, p + S[s] + "_attn.norm.key_norm.scale");
+      }
+      TIMED("qk_norm_rope", check_launch(launch_qk_norm_rope_segs(m->Y, ldY, (int)H, m->pe, L, qs, m->q, m->k, m->v, st),
+                                         "qk_norm_rope"));
+    }
     TIMED("attention", check_launch(launch_attention(m->q, m->k, m->v, (int)H, L, L, L, m->Y + 2 * h, ldY, st), "attention"));
     {
       const void* xs[2] = {m->Y + 2 * h, m->Y + Lt * ldY + 2 * h};
@@ -335,10 +344,12 @@ mb_status run_forward(mb_flux* m, const float* img, int64_t Li, const float* txt
       const float* gates[2] = {mos[0] + 2 * h, mos[1] + 2 * h};
       MB_TRY(linear_pair(m, p, "_attn.proj", segs, xs, ldY, ys, h, false, MB_EPI_GATE_RESIDUAL, gates, st));
     }
-    for (int s = 0; s < 2; s++)
-      TIMED("ln_modulate", check_launch(launch_ln_modulate(m->x + segs[s].row0 * h, segs[s].rows, h, h, mos[s] + 3 * h,
-                                                           mos[s] + 4 * h, m->xm + segs[s].row0 * h, h, st),
-                                        "ln_mod2"));
+    {
+      LnSegs ls = {};
+      ls.n = 2;
+      for (int s = 0; s < 2; s++) ls.s[s] = {segs[s].row0, segs[s].rows, mos[s] + 3 * h, mos[s] + 4 * h};
+      TIMED("ln_modulate", check_launch(launch_ln_modulate_segs(m->x, h, h, ls, m->xm, h, st), "ln_mod2"));
+    }
     {
       const void* xs[2] = {m->xm, m->xm + Lt * h};
       void* ys[2] = {m->Y + 3 * h, m->Y + Lt * ldY + 3 * h};

@@ -103,6 +103,31 @@ size_t gemv_stage_floats();
 
 cudaError_t launch_ln_modulate(const float* x, int64_t M, int64_t C, int64_t ldx, const float* shift,
                                const float* scale, void* y, int64_t ldy, cudaStream_t st);
+// Row segments of one elementwise launch (the text / image streams, batch items).
+constexpr int kMaxSegs = 4;
+struct LnSeg {
+  int64_t row0, rows;        // rows of x and y
+  const float *shift, *scale;
+};
+struct LnSegs {
+  LnSeg s[kMaxSegs];
+  int n;
+};
+cudaError_t launch_ln_modulate_segs(const float* x, int64_t C, int64_t ldx, const LnSegs& segs, void* y, int64_t ldy,
+                                    cudaStream_t st);
+struct QkSeg {
+  int64_t row0, rows;   // rows of the qkv buffer
+  int64_t pos0;         // sequence position (RoPE row, q row) of the segment's first row
+  int64_t off;          // element offset of this sequence's [H, L_total, 128] q / k / v
+  const int* kv_pos;    // key order of this sequence (NULL = identity)
+  const float *qs, *ks; // RMSNorm scales [128]
+};
+struct QkSegs {
+  QkSeg s[kMaxSegs];
+  int n;
+};
+cudaError_t launch_qk_norm_rope_segs(const void* qkv, int64_t ld_qkv, int H, const float* pe, int64_t L_total,
+                                     const QkSegs& segs, void* q, void* k, void* v, cudaStream_t st);
 cudaError_t launch_rope_table(const float* ids, int64_t L, int n_axes, const int* axes_dim, int theta, float* pe,
                               cudaStream_t st);
 cudaError_t launch_qk_norm_rope(const void* qkv, int64_t M, int64_t ld_qkv, int H, const float* q_scale,

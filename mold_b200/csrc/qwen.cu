@@ -362,10 +362,12 @@ mb_status run_forward(mb_qwen* m, const float* img, int64_t img_stride, int64_t 
   for (int i = 0; i < c.num_layers; i++) {
     const std::string p = blk(i);
     const float* mos[2] = {m->mods + m->mod_off[i] + 6 * h, m->mods + m->mod_off[i]};  // txt_mod, img_mod
-    for (int s = 0; s < 2; s++)
-      TIMED("ln_modulate", check_launch(launch_ln_modulate(m->x + segs[s].row0 * h, segs[s].rows, h, h, mos[s],
-                                                           mos[s] + h, m->xm + segs[s].row0 * h, h, st),
-                                        "ln_mod1"));
+    {
+      LnSegs ls = {};
+      ls.n = 2;
+      for (int s = 0; s < 2; s++) ls.s[s] = {segs[s].row0, segs[s].rows, mos[s], mos[s] + h};
+      TIMED("ln_modulate", check_launch(launch_ln_modulate_segs(m->x, h, h, ls, m->xm, h, st), "ln_mod1"));
+    }
     {
       const mb_weight* w[2] = {m->qkv_w[0][i], m->qkv_w[1][i]};
       const float* bs[2] = {m->qkv_b[0][i], m->qkv_b[1][i]};
@@ -373,19 +375,22 @@ mb_status run_forward(mb_qwen* m, const float* img, int64_t img_stride, int64_t 
       void* ys[2] = {m->Y, m->Y + Rt * ldY};
       MB_TRY(gemm_pair(w, bs, segs, xs, h, ys, ldY, true, MB_EPI_NONE, nullptr, "qkv", st));
     }
-    for (int b = 0; b < B; b++) {
-      const int64_t o = b * qkv_stride;
-      const int* kp = m->kv_pos + (int64_t)b * L;
-      TIMED("qk_norm_rope", check_launch(launch_qk_norm_rope(m->Y + (int64_t)b * Lt * ldY, Lt, ldY, (int)H,
-                                                             Vt(m, p + "attn.norm_added_q.weight"),
-                                                             Vt(m, p + "attn.norm_added_k.weight"), m->pe, 0, L,
-                                                             m->q + o, m->k + o, m->v + o, st, kp),
-                                         "qk_norm_rope txt"));
-      TIMED("qk_norm_rope", check_launch(launch_qk_norm_rope(m->Y + (Rt + (int64_t)b * Li) * ldY, Li, ldY, (int)H,
-                                                             Vt(m, p + "attn.norm_q.weight"),
-                                                             Vt(m, p + "attn.norm_k.weight"), m->pe, Lt, L, m->q + o,
-                                                             m->k + o, m->v + o, st, kp),
-                                         "qk_norm_rope img"));
+    {
+      QkSegs qs = {};
+      for (int b = 0; b < B; b++) {
+        for (int s = 0; s < 2; s++) {  // text, image rows of sequence b
+          QkSeg& g = qs.s[qs.n++];
+          g.row0 = s == 0 ? (int64_t)b * Lt : Rt + (int64_t)b * Li;
+          g.rows = s == 0 ? Lt : Li;
+          g.pos0 = s == 0 ? 0 : Lt;
+          g.off = b * qkv_stride;
+          g.kv_pos = m->kv_pos + (int64_t)b * L;
+          g.qs = Vt(m, p + (s == 0 ? "attn.norm_added_q.weight" : "attn.norm_q.weight"));
+          g.ks = Vt(m, p + (s == 0 ? "attn.norm_added_k.weight" : "attn.norm_k.weight"));
+        }
+      }
+      TIMED("qk_norm_rope", check_launch(launch_qk_norm_rope_segs(m->Y, ldY, (int)H, m->pe, L, qs, m->q, m->k, m->v, st),
+                                         "qk_norm_rope"));
     }
     for (int b = 0; b < B; b++) {
       const int64_t o = b * qkv_stride;
@@ -402,10 +407,12 @@ mb_status run_forward(mb_qwen* m, const float* img, int64_t img_stride, int64_t 
       const float* gates[2] = {mos[0] + 2 * h, mos[1] + 2 * h};
       MB_TRY(gemm_pair(w, bs, segs, xs, ldY, ys, h, false, MB_EPI_GATE_RESIDUAL, gates, "attn out", st));
     }
-    for (int s = 0; s < 2; s++)
-      TIMED("ln_modulate", check_launch(launch_ln_modulate(m->x + segs[s].row0 * h, segs[s].rows, h, h, mos[s] + 3 * h,
-                                                           mos[s] + 4 * h, m->xm + segs[s].row0 * h, h, st),
-                                        "ln_mod2"));
+    {
+      LnSegs ls = {};
+      ls.n = 2;
+      for (int s = 0; s < 2; s++) ls.s[s] = {segs[s].row0, segs[s].rows, mos[s] + 3 * h, mos[s] + 4 * h};
+      TIMED("ln_modulate", check_launch(launch_ln_modulate_segs(m->x, h, h, ls, m->xm, h, st), "ln_mod2"));
+    }
     {
       const mb_weight* w[2] = {Wt(m, p + "txt_mlp.net.0.proj.weight"), Wt(m, p + "img_mlp.net.0.proj.weight")};
       const float* bs[2] = {bias_or_null(m, p + "txt_mlp.net.0.proj.bias"),
