@@ -78,12 +78,24 @@ struct Params {
   int n_tiles;
   int* status;
   int ablate;  // builds with -DMB_TRACE only: 1 decode, 2 X loads, 4 raw loads, 8 TMEM stores, 16 epilogue
+  unsigned long long* trace;  // builds with -DMB_TRACE only: summed wait cycles per role (see TW)
 };
 
 #ifdef MB_TRACE
 #define ABL(bit) ((p.ablate & (bit)) != 0)
+// Cycles lane 0 of a role spends in a wait, accumulated in tr_[slot] and summed over CTAs at
+// exit. Slots: 0 TMA x_empty, 1 TMA r_empty, 2 MMA acc_empty, 3 MMA x_full, 4 MMA a_full,
+// 5 decode r_full, 6 decode a_empty, 7 epilogue acc_full, 8 MMA role total.
+#define TW(slot, call)                          \
+  ([&]() {                                      \
+    const long long t0__ = clock64();           \
+    const bool r__ = (call);                    \
+    tr_[slot] += (unsigned long long)(clock64() - t0__); \
+    return r__;                                 \
+  }())
 #else
 #define ABL(bit) false
+#define TW(slot, call) (call)
 #endif
 
 // ---- packed f32x2 arithmetic (sm_100): two IEEE single-precision ops per instruction ----
@@ -209,6 +221,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_tiles = p.n_tiles;
+#ifdef MB_TRACE
+  unsigned long long tr_[9] = {0, 0, 0, 0, 0, 0, 0, 0, 0};
+  const long long t_start_ = clock64();
+#endif
   // problem of a global tile index and the tile's origin within it
 #define TILE_SETUP(tile)                                                   \
   const int pi_ = (p.nprob > 1 && (tile) >= p.pr[1].tile0) ? 1 : 0;      \
@@ -257,7 +273,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int m0 = (lt_ % P.tiles_m) * TM, n0 = (lt_ / P.tiles_m) * TN;
         for (int ks = 0; ks < nks && ok; ks++, it++) {
           const uint32_t sx = it % SX, px = (it / SX) & 1;
-          if (!(ok = mbar_wait(&x_empty[sx], px ^ 1, abort_flag, p.status, kDevTimeoutGemm))) break;
+          if (!(ok = TW(0, mbar_wait(&x_empty[sx], px ^ 1, abort_flag, p.status, kDevTimeoutGemm)))) break;
           if (ABL(2)) {
             mbar_arrive(&x_full[sx]);
           } else {
@@ -267,7 +283,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (ks % kSPC == 0) {  // one raw chunk (kSPC stages) per 128-row weight block
             const uint32_t sr = ic % kSR, pr = (ic / kSR) & 1;
             ic++;
-            if (!(ok = mbar_wait(&r_empty[sr], pr ^ 1, abort_flag, p.status, kDevTimeoutGemm))) break;
+            if (!(ok = TW(1, mbar_wait(&r_empty[sr], pr ^ 1, abort_flag, p.status, kDevTimeoutGemm)))) break;
             if (ABL(4)) {
               mbar_arrive(&r_full[sr]);
               continue;
@@ -292,13 +308,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool ok = true;
     for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x, tcount++) {
       TILE_SETUP(tile);
-      if (!(ok = mbar_wait(acc_empty, (tcount & 1) ^ 1, abort_flag, p.status, kDevTimeoutGemm))) break;
+      if (!(ok = TW(2, mbar_wait(acc_empty, (tcount & 1) ^ 1, abort_flag, p.status, kDevTimeoutGemm)))) break;
       tc_fence_after();
       for (int ks = 0; ks < nks; ks++, it++) {
         const uint32_t sx = it % SX, px = (it / SX) & 1;
         const uint32_t sa = it % SAT, pa = (it / SAT) & 1;
-        if (!(ok = mbar_wait(&x_full[sx], px, abort_flag, p.status, kDevTimeoutGemm))) break;
-        if (!(ok = mbar_wait(&a_full[sa], pa, abort_flag, p.status, kDevTimeoutGemm))) break;
+        if (!(ok = TW(3, mbar_wait(&x_full[sx], px, abort_flag, p.status, kDevTimeoutGemm)))) break;
+        if (!(ok = TW(4, mbar_wait(&a_full[sa], pa, abort_flag, p.status, kDevTimeoutGemm)))) break;
         tc_fence_after();
         if (lane == 0) {
           const uint32_t xaddr = smem_u32(xs + sx * kXStageBytes);
@@ -316,6 +332,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (lane == 0) umma_commit(acc_full);
       __syncwarp();
     }
+#ifdef MB_TRACE
+    tr_[8] = (unsigned long long)(clock64() - t_start_);
+#endif
   } else if (warp < 2 + kDW) {
     // ------------------------------------------------ dequant: raw GGML -> bf16 -> TMEM
     const int q = warp & 3;               // TMEM lane quarter
@@ -328,7 +347,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       TILE_SETUP(tile);
       for (int kc = 0; kc < nks / kSPC && ok; kc++, ic++) {
         const uint32_t sr = ic % kSR, pr = (ic / kSR) & 1;
-        if (!(ok = mbar_wait(&r_full[sr], pr, abort_flag, p.status, kDevTimeoutGemm))) break;
+        if (!(ok = TW(5, mbar_wait(&r_full[sr], pr, abort_flag, p.status, kDevTimeoutGemm)))) break;
         const uint8_t* R = rs + sr * kRawStage;
         // Q4_K: this thread's four sub-blocks (2j + hh, j = 0..3) of the super-block, decoded once.
         // High nibbles (hh = 1) are used in place (16 q) with the scale divided by 16: still exact.
@@ -395,7 +414,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             __syncwarp();
             if (lane == 0) mbar_arrive(&r_empty[sr]);
           }
-          if (!(ok = mbar_wait(&a_empty[sa], pa ^ 1, abort_flag, p.status, kDevTimeoutGemm))) break;
+          if (!(ok = TW(6, mbar_wait(&a_empty[sa], pa ^ 1, abort_flag, p.status, kDevTimeoutGemm)))) break;
           tc_fence_after();
           if (!ABL(8)) {
             tmem_st16(tmem + lane_addr + kTmemA + sa * 32 + hh * 16, o);
@@ -419,7 +438,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const GemmEpilogue& e = P.epi;
       const int m0 = (lt_ % P.tiles_m) * TM + ch * 128, n0 = (lt_ / P.tiles_m) * TN;
       const int n = n0 + q * 32 + lane;
-      if (!(ok = mbar_wait(acc_full, tcount & 1, abort_flag, p.status, kDevTimeoutGemm))) break;
+      if (!(ok = TW(7, mbar_wait(acc_full, tcount & 1, abort_flag, p.status, kDevTimeoutGemm)))) break;
       tc_fence_after();
       const bool nvalid = n < P.N;
       const float bias = (nvalid && e.bias) ? e.bias[n] : 0.f;
@@ -539,6 +558,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
 
+#ifdef MB_TRACE
+  if (p.trace && lane == 0 && (warp <= 2 || warp == 2 + kDW))
+    for (int i = 0; i < 9; i++)
+      if (tr_[i]) atomicAdd(p.trace + i, tr_[i]);
+#endif
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
@@ -548,6 +572,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 int g_gemm_ablate = 0;
+unsigned long long* g_gemm_trace = nullptr;
 
 template <int WT>
 bool make_maps(const mb_weight* w, const void* x, int64_t M, int64_t ldx, CUtensorMap* tx, CUtensorMap* tw) {
@@ -586,6 +611,7 @@ cudaError_t launch_t(int n, const GemmProblem* g, cudaStream_t st) {
   p.n_tiles = tiles;
   p.status = device_status_ptr();
   p.ablate = g_gemm_ablate;
+  p.trace = g_gemm_trace;
   const int grid = tiles < num_sms() ? tiles : num_sms();
   constexpr size_t smem = smem_bytes<WT>();
   static int attr_done[64];  // per template instance and device
@@ -604,6 +630,10 @@ cudaError_t launch_t(int n, const GemmProblem* g, cudaStream_t st) {
 
 #ifdef MB_TRACE
 extern "C" __attribute__((visibility("default"))) void mb_debug_set_gemm_ablate(int flags) { gemm::g_gemm_ablate = flags; }
+// Device buffer of 9 u64 counters (NULL = off) that k_qgemm adds its per-role wait cycles to.
+extern "C" __attribute__((visibility("default"))) void mb_debug_set_gemm_trace(unsigned long long* buf) {
+  gemm::g_gemm_trace = buf;
+}
 #endif
 
 cudaError_t launch_qgemm_group(int n, const GemmProblem* g, cudaStream_t st) {
