@@ -47,13 +47,24 @@ MB_DEV bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
+// try_wait with a suspend-time hint: the thread sleeps until the phase completes or ~hint_ns
+// pass, instead of re-polling (polling warps take issue slots from the warps doing work).
+MB_DEV bool mbar_try_wait_hint(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
 // Bounded wait. Returns false (and raises *abort and the device status) when the
 // phase did not complete within kSpinLimitCycles or another role already aborted.
 MB_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* status, int code) {
   if (mbar_try_wait(bar, parity)) return true;
   long long t0 = clock64();
   while (true) {
-    if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_try_wait_hint(bar, parity, 20000)) return true;
     if (*abort_flag) return false;
     if (clock64() - t0 > kSpinLimitCycles) {
       *abort_flag = 1;

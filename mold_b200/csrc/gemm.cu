@@ -39,29 +39,38 @@ namespace gemm {
 constexpr int TN = 128;  // weight rows per tile (MMA M, TMEM lanes)
 constexpr int TM = 256;  // activation rows per tile (MMA N): every decoded weight feeds 256 rows
 constexpr int BK = 64;   // K per stage
-constexpr int SAT = 8;   // TMEM A-stage ring depth (32 columns each)
+// The decoded-A ring in TMEM (32 columns per stage) has the same depth as the X ring in shared
+// memory: stage s uses slot s % SX of both, so one "full" and one "empty" barrier per slot cover
+// both operands (one barrier wait and one commit per stage in the MMA issuer).
 constexpr int kDW = 8;   // dequant warps (2..9)
 constexpr int kEW = 8;   // epilogue warps (10..17)
 constexpr int kThreads = (2 + kDW + kEW) * 32;
 constexpr uint32_t kXStageBytes = TM * BK * 2;  // 32 KB
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kTmemA = 256;  // first A-stage column (D uses [0, 256))
+constexpr int kMaxSX = 4;         // A ring [256, 384)
+// Epilogue staging [384, 512): each epilogue warp parks its 128 packed bf16 results (64 words per
+// lane) here, so the accumulator is freed without holding them in registers (the kernel's 18
+// warps leave 96 registers per thread; a register-resident copy spills).
+constexpr uint32_t kTmemStage = kTmemA + kMaxSX * 32;
 
 template <int WT>
 struct Cfg;
 template <>
 struct Cfg<MB_GGML_Q4_K> {
-  static constexpr int kRawRow = 144, kSPC = 4, kSR = 3, kSX = 5;  // whole super-blocks
+  static constexpr int kRawRow = 144, kSPC = 4, kSR = 3, kSX = 4;  // whole super-blocks
 };
 template <>
 struct Cfg<MB_GGML_Q8_0> {
-  static constexpr int kRawRow = 80, kSPC = 1, kSR = 6, kSX = 5;
+  static constexpr int kRawRow = 80, kSPC = 1, kSR = 6, kSX = 4;
 };
 template <>
 struct Cfg<MB_GGML_BF16> {
-  static constexpr int kRawRow = 128, kSPC = 1, kSR = 4, kSX = 5;
+  static constexpr int kRawRow = 128, kSPC = 1, kSR = 4, kSX = 4;
 };
 
+static_assert(Cfg<MB_GGML_Q4_K>::kSX <= kMaxSX && Cfg<MB_GGML_Q8_0>::kSX <= kMaxSX && Cfg<MB_GGML_BF16>::kSX <= kMaxSX,
+              "A ring must fit below the epilogue staging columns");
 template <int WT>
 constexpr size_t smem_bytes() {
   return 1024 + (size_t)Cfg<WT>::kSX * kXStageBytes + (size_t)Cfg<WT>::kSR * TN * Cfg<WT>::kRawRow + 512;
@@ -84,8 +93,8 @@ struct Params {
 #ifdef MB_TRACE
 #define ABL(bit) ((p.ablate & (bit)) != 0)
 // Cycles lane 0 of a role spends in a wait, accumulated in tr_[slot] and summed over CTAs at
-// exit. Slots: 0 TMA x_empty, 1 TMA r_empty, 2 MMA acc_empty, 3 MMA x_full, 4 MMA a_full,
-// 5 decode r_full, 6 decode a_empty, 7 epilogue acc_full, 8 MMA role total.
+// exit. Slots: 0 TMA empty, 1 TMA r_empty, 2 MMA acc_empty, 3 MMA full, 4 epilogue drain,
+// 5 decode r_full, 6 decode empty, 7 epilogue acc_full, 8 MMA role total.
 #define TW(slot, call)                          \
   ([&]() {                                      \
     const long long t0__ = clock64();           \
@@ -179,6 +188,13 @@ MB_DEV void q8_block(const uint32_t (&W)[12], uint32_t (&o)[16]) {
   }
 }
 
+MB_DEV void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
 MB_DEV void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
   asm volatile(
       "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
@@ -208,13 +224,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* xs = smem;                                    // SX x 32 KB, 1024-aligned
   uint8_t* rs = smem + SX * kXStageBytes;                // kSR raw stages
   uint64_t* bars = (uint64_t*)(rs + kSR * kRawStage);
-  uint64_t* x_full = bars;
-  uint64_t* x_empty = x_full + SX;
-  uint64_t* r_full = x_empty + SX;
+  uint64_t* full = bars;         // X landed (TMA tx) and A decoded (kDW arrivals)
+  uint64_t* empty = full + SX;    // the stage's MMAs completed (one commit)
+  uint64_t* r_full = empty + SX;
   uint64_t* r_empty = r_full + kSR;
-  uint64_t* a_full = r_empty + kSR;
-  uint64_t* a_empty = a_full + SAT;
-  uint64_t* acc_full = a_empty + SAT;
+  uint64_t* acc_full = r_empty + kSR;
   uint64_t* acc_empty = acc_full + 1;
   uint32_t* tmem_slot = (uint32_t*)(acc_empty + 1);
   volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
@@ -222,7 +236,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_tiles = p.n_tiles;
 #ifdef MB_TRACE
-  unsigned long long tr_[9] = {0, 0, 0, 0, 0, 0, 0, 0, 0};
+  unsigned long long tr_[12] = {0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0};
   const long long t_start_ = clock64();
 #endif
   // problem of a global tile index and the tile's origin within it
@@ -238,9 +252,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   (void)nks;
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < SX; i++) { mbar_init(&x_full[i], 1); mbar_init(&x_empty[i], 1); }
+    for (int i = 0; i < SX; i++) { mbar_init(&full[i], 1 + kDW); mbar_init(&empty[i], 1); }
     for (int i = 0; i < kSR; i++) { mbar_init(&r_full[i], 1); mbar_init(&r_empty[i], kDW); }
-    for (int i = 0; i < SAT; i++) { mbar_init(&a_full[i], kDW); mbar_init(&a_empty[i], 1); }
     mbar_init(acc_full, 1);
     mbar_init(acc_empty, kEW);
     *abort_flag = 0;
@@ -264,39 +277,48 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 0) {
-    // ------------------------------------------------ TMA producer
+    // ------------------------------------------------ TMA producers
+    // lane 0 streams the activation (X) stages, lane 1 the raw weight chunks; the weight stream
+    // runs ahead of X, bounded only by its own ring, so decode never waits behind the X ring.
     if (lane == 0) {
-      uint32_t it = 0, ic = 0;
+      uint32_t it = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x) {
         TILE_SETUP(tile);
-        const int m0 = (lt_ % P.tiles_m) * TM, n0 = (lt_ / P.tiles_m) * TN;
+        const int m0 = (lt_ % P.tiles_m) * TM;
         for (int ks = 0; ks < nks && ok; ks++, it++) {
           const uint32_t sx = it % SX, px = (it / SX) & 1;
-          if (!(ok = TW(0, mbar_wait(&x_empty[sx], px ^ 1, abort_flag, p.status, kDevTimeoutGemm)))) break;
+          if (!(ok = TW(0, mbar_wait(&empty[sx], px ^ 1, abort_flag, p.status, kDevTimeoutGemm)))) break;
           if (ABL(2)) {
-            mbar_arrive(&x_full[sx]);
+            mbar_arrive(&full[sx]);
           } else {
-            mbar_expect_tx(&x_full[sx], kXStageBytes);
-            tma_load_2d(xs + sx * kXStageBytes, tm_x, &x_full[sx], ks * BK, m0);
+            mbar_expect_tx(&full[sx], kXStageBytes);
+            tma_load_2d(xs + sx * kXStageBytes, tm_x, &full[sx], ks * BK, m0);
           }
-          if (ks % kSPC == 0) {  // one raw chunk (kSPC stages) per 128-row weight block
-            const uint32_t sr = ic % kSR, pr = (ic / kSR) & 1;
-            ic++;
-            if (!(ok = TW(1, mbar_wait(&r_empty[sr], pr ^ 1, abort_flag, p.status, kDevTimeoutGemm)))) break;
-            if (ABL(4)) {
-              mbar_arrive(&r_full[sr]);
-              continue;
-            }
-            mbar_expect_tx(&r_full[sr], kRawStage);
-            uint8_t* rdst = rs + sr * kRawStage;
-            if (WT == MB_GGML_Q4_K) {
-              tma_load_2d(rdst, tm_w, &r_full[sr], (ks >> 2) * 144, n0);
-            } else if (WT == MB_GGML_Q8_0) {
-              tma_load_2d(rdst, tm_w, &r_full[sr], (68 * ks) & ~15, n0);
-            } else {
-              tma_load_2d(rdst, tm_w, &r_full[sr], ks * 128, n0);
-            }
+        }
+      }
+    } else if (lane == 1) {
+      uint32_t ic = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x) {
+        TILE_SETUP(tile);
+        const int n0 = (lt_ / P.tiles_m) * TN;
+        for (int ks = 0; ks < nks && ok; ks += kSPC) {  // one raw chunk (kSPC stages) per 128-row block
+          const uint32_t sr = ic % kSR, pr = (ic / kSR) & 1;
+          ic++;
+          if (!(ok = TW(1, mbar_wait(&r_empty[sr], pr ^ 1, abort_flag, p.status, kDevTimeoutGemm)))) break;
+          if (ABL(4)) {
+            mbar_arrive(&r_full[sr]);
+            continue;
+          }
+          mbar_expect_tx(&r_full[sr], kRawStage);
+          uint8_t* rdst = rs + sr * kRawStage;
+          if (WT == MB_GGML_Q4_K) {
+            tma_load_2d(rdst, tm_w, &r_full[sr], (ks >> 2) * 144, n0);
+          } else if (WT == MB_GGML_Q8_0) {
+            tma_load_2d(rdst, tm_w, &r_full[sr], (68 * ks) & ~15, n0);
+          } else {
+            tma_load_2d(rdst, tm_w, &r_full[sr], ks * 128, n0);
           }
         }
       }
@@ -311,10 +333,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!(ok = TW(2, mbar_wait(acc_empty, (tcount & 1) ^ 1, abort_flag, p.status, kDevTimeoutGemm)))) break;
       tc_fence_after();
       for (int ks = 0; ks < nks; ks++, it++) {
-        const uint32_t sx = it % SX, px = (it / SX) & 1;
-        const uint32_t sa = it % SAT, pa = (it / SAT) & 1;
-        if (!(ok = TW(3, mbar_wait(&x_full[sx], px, abort_flag, p.status, kDevTimeoutGemm)))) break;
-        if (!(ok = TW(4, mbar_wait(&a_full[sa], pa, abort_flag, p.status, kDevTimeoutGemm)))) break;
+        const uint32_t sx = it % SX, px = (it / SX) & 1, sa = sx;
+        if (!(ok = TW(3, mbar_wait(&full[sx], px, abort_flag, p.status, kDevTimeoutGemm)))) break;
         tc_fence_after();
         if (lane == 0) {
           const uint32_t xaddr = smem_u32(xs + sx * kXStageBytes);
@@ -323,8 +343,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint64_t bdesc = sw128_desc(xaddr + kk * 32, 16, 1024);
             umma_ts(tmem, tmem + kTmemA + sa * 32 + kk * 8, bdesc, idesc, (ks | kk) != 0);
           }
-          umma_commit(&x_empty[sx]);
-          umma_commit(&a_empty[sa]);
+          umma_commit(&empty[sx]);
         }
         __syncwarp();
       }
@@ -367,7 +386,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int j = 0; j < kSPC; j++, it++) {
           const int ks = kc * kSPC + j;
-          const uint32_t sa = it % SAT, pa = (it / SAT) & 1;
+          const uint32_t sa = it % SX, pa = (it / SX) & 1;
           uint32_t o[16];
           if (ABL(1)) {
 #pragma unroll
@@ -414,7 +433,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             __syncwarp();
             if (lane == 0) mbar_arrive(&r_empty[sr]);
           }
-          if (!(ok = TW(6, mbar_wait(&a_empty[sa], pa ^ 1, abort_flag, p.status, kDevTimeoutGemm)))) break;
+          if (!(ok = TW(6, mbar_wait(&empty[sa], pa ^ 1, abort_flag, p.status, kDevTimeoutGemm)))) break;
           tc_fence_after();
           if (!ABL(8)) {
             tmem_st16(tmem + lane_addr + kTmemA + sa * 32 + hh * 16, o);
@@ -422,7 +441,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive(&a_full[sa]);
+          if (lane == 0) mbar_arrive(&full[sa]);
         }
       }
     }
@@ -438,26 +457,39 @@ __global__ void __launch_bounds__(kThreads, 1)
       const GemmEpilogue& e = P.epi;
       const int m0 = (lt_ % P.tiles_m) * TM + ch * 128, n0 = (lt_ / P.tiles_m) * TN;
       const int n = n0 + q * 32 + lane;
-      if (!(ok = TW(7, mbar_wait(acc_full, tcount & 1, abort_flag, p.status, kDevTimeoutGemm)))) break;
-      tc_fence_after();
+      // per-feature epilogue operands are loaded before the accumulator wait (off the drain path)
       const bool nvalid = n < P.N;
       const float bias = (nvalid && e.bias) ? e.bias[n] : 0.f;
       const float gate = (nvalid && e.kind == MB_EPI_GATE_RESIDUAL) ? e.gate[n] : 0.f;
+      if (!(ok = TW(7, mbar_wait(acc_full, tcount & 1, abort_flag, p.status, kDevTimeoutGemm)))) break;
+      tc_fence_after();
+#ifdef MB_TRACE
+      const long long t_drain_ = clock64();
+#define DRAIN_DONE() (tr_[4] += (unsigned long long)(clock64() - t_drain_))
+#else
+#define DRAIN_DONE() ((void)0)
+#endif
       const bool do_gelu = e.kind == MB_EPI_GELU_TANH && n >= e.gelu_from;
       const bool fast_bf16 = e.out_bf16 && e.kind != MB_EPI_GATE_RESIDUAL && (P.N & 1) == 0;
       if (ABL(16)) {
         __syncwarp();
         if (lane == 0) mbar_arrive(acc_empty);
+        DRAIN_DONE();
       } else if (fast_bf16) {
-        // bf16 output: pull the warp's 128 accumulator columns into registers as packed bf16
-        // pairs (rows m, m+1 of feature n), free the accumulator, then store 32-bit words:
-        // lanes 2j / 2j+1 exchange halves so each writes features (n, n+1) of one row.
-        uint32_t pk[64];
-#pragma unroll
+        // bf16 output: pack the warp's 128 accumulator columns to bf16 pairs (rows m, m+1 of
+        // feature n), park them in the TMEM staging columns, free the accumulator, then read them
+        // back 16 words at a time and store 32-bit words: lanes 2j / 2j+1 exchange halves so each
+        // writes features (n, n+1) of one row.
+        const uint32_t stage = tmem + lane_addr + kTmemStage + ch * 64;
+#pragma unroll 1
         for (int c = 0; c < 4; c++) {
           uint32_t v[32];
           tmem_ld32(tmem + lane_addr + ch * 128 + c * 32, v);
           tmem_wait_ld();
+#ifdef MB_TRACE
+          if (c == 0) tr_[9] += (unsigned long long)(clock64() - t_drain_);
+#endif
+          uint32_t o[16];
 #pragma unroll
           for (int j = 0; j < 16; j++) {
             float a0 = __uint_as_float(v[2 * j]) + bias, a1 = __uint_as_float(v[2 * j + 1]) + bias;
@@ -465,19 +497,28 @@ __global__ void __launch_bounds__(kThreads, 1)
               a0 = gelu_tanh(a0);
               a1 = gelu_tanh(a1);
             }
-            pk[c * 16 + j] = pack_bf16x2(a0, a1);
+            o[j] = pack_bf16x2(a0, a1);
           }
+          tmem_st16(stage + c * 16, o);
         }
+        tmem_wait_st();
+#ifdef MB_TRACE
+        tr_[10] += (unsigned long long)(clock64() - t_drain_);
+#endif
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(acc_empty);
+        DRAIN_DONE();
         const bool odd = lane & 1;
         const int ncol = n - (odd ? 1 : 0);  // even feature of the pair this lane writes
-#pragma unroll
+#pragma unroll 1
         for (int c = 0; c < 4; c++) {
+          uint32_t pk[16];
+          tmem_ld16(stage + c * 16, pk);
+          tmem_wait_ld();
 #pragma unroll
           for (int j = 0; j < 16; j++) {
-            const uint32_t r = pk[c * 16 + j];
+            const uint32_t r = pk[j];
             const uint32_t r2 = __shfl_xor_sync(0xffffffffu, r, 1);
             // even lane: (own lo, partner lo) = row m ; odd lane: (partner hi, own hi) = row m + 1
             const uint32_t wv = odd ? __byte_perm(r2, r, 0x7632) : __byte_perm(r, r2, 0x5410);
@@ -487,38 +528,48 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       } else if (e.kind == MB_EPI_GATE_RESIDUAL) {
-        // f32 residual output: u = gate * (acc + bias) is pulled out of TMEM as packed bf16
-        // pairs (rows m, m+1), the accumulator is freed, then y = residual + u in f32.
-        uint32_t pk[64];
-#pragma unroll
+        // f32 residual output: u = gate * (acc + bias) is parked in the TMEM staging columns as
+        // packed bf16 pairs (rows m, m+1), the accumulator is freed, then y = residual + u in f32.
+        const uint32_t stage = tmem + lane_addr + kTmemStage + ch * 64;
+#pragma unroll 1
         for (int c = 0; c < 4; c++) {
           uint32_t v[32];
           tmem_ld32(tmem + lane_addr + ch * 128 + c * 32, v);
           tmem_wait_ld();
+          uint32_t o[16];
 #pragma unroll
           for (int j = 0; j < 16; j++)
-            pk[c * 16 + j] = pack_bf16x2(gate * (__uint_as_float(v[2 * j]) + bias),
-                                         gate * (__uint_as_float(v[2 * j + 1]) + bias));
+            o[j] = pack_bf16x2(gate * (__uint_as_float(v[2 * j]) + bias), gate * (__uint_as_float(v[2 * j + 1]) + bias));
+          tmem_st16(stage + c * 16, o);
         }
+        tmem_wait_st();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(acc_empty);
-        if (nvalid) {
-          // y usually aliases res: issue a batch of 16 residual loads before any store so
-          // their latencies overlap (the compiler cannot reorder loads past aliasing stores).
+        DRAIN_DONE();
+        // y usually aliases res: issue a batch of 16 residual loads before any store so their
+        // latencies overlap (the compiler cannot reorder loads past aliasing stores). The TMEM
+        // reads stay warp-uniform; only the global accesses depend on the lane's feature.
+#pragma unroll 1
+        for (int c = 0; c < 4; c++) {
+          uint32_t pk[16];
+          tmem_ld16(stage + c * 16, pk);
+          tmem_wait_ld();
+          if (nvalid) {
 #pragma unroll
-          for (int c = 0; c < 8; c++) {
-            float rv[16];
+            for (int hb = 0; hb < 2; hb++) {
+              float rv[16];
 #pragma unroll
-            for (int i = 0; i < 16; i++) {
-              const int m = m0 + c * 16 + i;
-              rv[i] = m < P.M ? e.res[(int64_t)m * e.ldr + n] : 0.f;
-            }
+              for (int i = 0; i < 16; i++) {
+                const int m = m0 + c * 32 + hb * 16 + i;
+                rv[i] = m < P.M ? e.res[(int64_t)m * e.ldr + n] : 0.f;
+              }
 #pragma unroll
-            for (int i = 0; i < 16; i++) {
-              const int m = m0 + c * 16 + i;
-              const uint32_t r = pk[c * 8 + (i >> 1)];
-              if (m < P.M) ((float*)e.y)[(int64_t)m * e.ldy + n] = rv[i] + ((i & 1) ? bf16_hi(r) : bf16_lo(r));
+              for (int i = 0; i < 16; i++) {
+                const int m = m0 + c * 32 + hb * 16 + i;
+                const uint32_t r = pk[hb * 8 + (i >> 1)];
+                if (m < P.M) ((float*)e.y)[(int64_t)m * e.ldy + n] = rv[i] + ((i & 1) ? bf16_hi(r) : bf16_lo(r));
+              }
             }
           }
         }
@@ -532,6 +583,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(acc_empty);
+        DRAIN_DONE();
           }
           const int mb = m0 + c * 32;
           if (nvalid) {
@@ -559,8 +611,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 
 #ifdef MB_TRACE
-  if (p.trace && lane == 0 && (warp <= 2 || warp == 2 + kDW))
-    for (int i = 0; i < 9; i++)
+  if (p.trace && (lane == 0 || (warp == 0 && lane == 1)) && (warp <= 2 || warp == 2 + kDW))
+    for (int i = 0; i < 12; i++)
       if (tr_[i]) atomicAdd(p.trace + i, tr_[i]);
 #endif
   tc_fence_before();
