@@ -9,8 +9,9 @@
 //   warp 1      MMA issuer. Per KV block j the tensor core runs, in order,
 //                 PV_0(j), S_0(j+1) = Q_0 K_{j+1}^T, PV_1(j), S_1(j+1)
 //               so while one tile's softmax works, the tensor core serves the other.
-//   warps 4-7   softmax of tile 0, warps 8-11 softmax of tile 1: one thread per query
-//               row (= TMEM lane). Row max, exp2, row sum; P (bf16) is written back into
+//   warps 4-11  softmax of tile 0, warps 12-19 softmax of tile 1: two threads per query
+//               row (= TMEM lane), 64 key columns each, exchanging the row max through
+//               shared memory. Row max, exp2, row sum; P (bf16) of each half is written back into
 //               TMEM over the S columns it was computed from and consumed directly as the
 //               A operand of O += P V (O in TMEM). O is rescaled lazily, only when the row
 //               max grows by more than 2^8, which leaves the final O / l unchanged.
@@ -25,15 +26,20 @@ namespace mb {
 namespace attn {
 
 constexpr int BQ = 128, BKV = 128, D = 128, NT = 2;
-constexpr int kThreads = 384;
+constexpr int kThreads = 640;  // warp 0 TMA, warp 1 MMA, warps 4-11 softmax tile 0, 12-19 tile 1
 constexpr uint32_t kTile = 128 * 128 * 2;  // 32 KB: one 128x128 bf16 tile (two 64-wide swizzle atoms)
 constexpr uint32_t kHalf = kTile / 2;      // 16 KB: one 64-wide atom column
-constexpr size_t kSmem = 1024 + 6 * (size_t)kTile + 256;
+constexpr size_t kSmem = 1024 + 6 * (size_t)kTile + 256 + 6 * 1024;  // + row-max / row-sum exchange
 constexpr float kScaleLog2 = 0.12751743082459868f;  // log2(e) / sqrt(128)
 constexpr float kRescaleThreshold = 8.f;
-constexpr int kPolyPerChunk = 6;  // of every 32 exponentials, this many use the FMA-pipe polynomial
+#ifndef MB_ATTN_POLY
+#define MB_ATTN_POLY 6
+#endif
+constexpr int kPolyPerChunk = MB_ATTN_POLY;  // of every 32 exponentials, this many use the FMA-pipe polynomial
 
 struct Params {
+  unsigned long long* trace;  // builds with -DMB_TRACE only: summed wait cycles per role (see AW)
+  int ablate;                 // builds with -DMB_TRACE only: 1 no S loads, 2 no P stores, 4 no exp
   int H, Lq, Lk, n_valid, n_kv;
   __nv_bfloat16* out;   // rows [0, split)
   __nv_bfloat16* out2;  // rows [split, Lq), from its row 0
@@ -122,6 +128,25 @@ MB_DEV void umma_ts_a(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t
       : "memory");
 }
 
+#ifdef MB_TRACE
+#define AABL(bit) ((p.ablate & (bit)) != 0)
+#else
+#define AABL(bit) false
+#endif
+#ifdef MB_TRACE
+// Slots: 0 TMA kv_empty, 1 MMA v_full, 2 MMA p_full[0], 3 MMA k_full, 4 MMA p_full[1], 5 softmax(t0)
+// s_full, 6 softmax(t0) total, 7 MMA total, 8 softmax(t1) s_full.
+#define AW(slot, call)                                     \
+  ([&]() {                                                 \
+    const long long t0__ = clock64();                      \
+    const bool r__ = (call);                               \
+    tr_[slot] += (unsigned long long)(clock64() - t0__);   \
+    return r__;                                            \
+  }())
+#else
+#define AW(slot, call) (call)
+#endif
+
 __global__ void __launch_bounds__(kThreads, 1)
     k_attention(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                 const __grid_constant__ CUtensorMap tv, const Params p) {
@@ -138,12 +163,18 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* s_full = bars + 7;    // [2] per tile
   uint64_t* p_full = bars + 9;    // [2] per tile
   uint64_t* o_full = bars + 11;   // [2] per tile
-  uint32_t* tmem_slot = (uint32_t*)(bars + 13);
+  uint64_t* pair_bar = bars + 13;  // [8] per (tile, lane quarter): the two softmax warps of a row
+  uint32_t* tmem_slot = (uint32_t*)(bars + 21);
   volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
+  float* xch = (float*)(smem + 6 * kTile + 256);  // [2 parity][2 tiles][128 rows][2 halves] maxima, then [2][128][2] sums
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int h = blockIdx.y, q0 = blockIdx.x * (NT * BQ);
   const int n_kv = p.n_kv;
+#ifdef MB_TRACE
+  unsigned long long tr_[9] = {0, 0, 0, 0, 0, 0, 0, 0, 0};
+  const long long t_start_ = clock64();
+#endif
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -152,9 +183,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&v_full[i], 1);
       mbar_init(&kv_empty[i], 1);
       mbar_init(&s_full[i], 1);
-      mbar_init(&p_full[i], 4);
+      mbar_init(&p_full[i], 8);
       mbar_init(&o_full[i], 1);
     }
+    for (int i = 0; i < 8; i++) mbar_init(&pair_bar[i], 2);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -180,7 +212,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int j = 0; j < n_kv; j++) {
         const int s = j & 1;
         const uint32_t ph = (j >> 1) & 1;
-        if (!mbar_wait(&kv_empty[s], ph ^ 1, abort_flag, p.status, kDevTimeoutAttn)) break;
+        if (!AW(0, mbar_wait(&kv_empty[s], ph ^ 1, abort_flag, p.status, kDevTimeoutAttn))) break;
         mbar_expect_tx(&k_full[s], kTile);
         tma_load_3d(sK + s * kTile, &tk, &k_full[s], 0, j * BKV, h);
         tma_load_3d(sK + s * kTile + kHalf, &tk, &k_full[s], 64, j * BKV, h);
@@ -216,7 +248,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int kk = 0; kk < BKV / 16; kk++) {
           // V [keys, d]: MN-major; 64-wide d chunks kHalf apart (LBO), 8-key groups 1024 B apart (SBO).
           const uint64_t bdesc = sw128_desc(va + kk * 16 * 128, kHalf, 1024);
-          umma_ts_a(tmem + 256 + t * 128, tmem + t * 128 + kk * 8, bdesc, idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
+          // P of keys 0..63 sits in S columns [0, 32), of keys 64..127 in [64, 96) (each softmax half
+          // writes P into its own S columns)
+          const uint32_t pcol = kk < 4 ? kk * 8 : 64 + (kk - 4) * 8;
+          umma_ts_a(tmem + 256 + t * 128, tmem + t * 128 + pcol, bdesc, idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
         }
       }
       __syncwarp();
@@ -230,17 +265,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int j = 0; j < n_kv && ok; j++) {
       const uint32_t ph = (j >> 1) & 1;
-      if (!(ok = mbar_wait(&v_full[j & 1], ph, abort_flag, p.status, kDevTimeoutAttn))) break;
+      if (!(ok = AW(1, mbar_wait(&v_full[j & 1], ph, abort_flag, p.status, kDevTimeoutAttn)))) break;
       const bool more = j + 1 < n_kv;
-      if (!(ok = mbar_wait(&p_full[0], j & 1, abort_flag, p.status, kDevTimeoutAttn))) break;
+      if (!(ok = AW(2, mbar_wait(&p_full[0], j & 1, abort_flag, p.status, kDevTimeoutAttn)))) break;
       tc_fence_after();
       issue_pv(0, j);
       if (more) {
-        if (!(ok = mbar_wait(&k_full[(j + 1) & 1], ((j + 1) >> 1) & 1, abort_flag, p.status, kDevTimeoutAttn))) break;
+        if (!(ok = AW(3, mbar_wait(&k_full[(j + 1) & 1], ((j + 1) >> 1) & 1, abort_flag, p.status, kDevTimeoutAttn))))
+          break;
         tc_fence_after();
         issue_s(0, j + 1);
       }
-      if (!(ok = mbar_wait(&p_full[1], j & 1, abort_flag, p.status, kDevTimeoutAttn))) break;
+      if (!(ok = AW(4, mbar_wait(&p_full[1], j & 1, abort_flag, p.status, kDevTimeoutAttn)))) break;
       tc_fence_after();
       issue_pv(1, j);
       if (lane == 0) umma_commit(&kv_empty[j & 1]);
@@ -252,32 +288,55 @@ __global__ void __launch_bounds__(kThreads, 1)
       umma_commit(&o_full[1]);
     }
     __syncwarp();
+#ifdef MB_TRACE
+    tr_[7] = (unsigned long long)(clock64() - t_start_);
+#endif
   } else if (warp >= 4) {
-    // ---------------------------------------------------------------- softmax (one tile per warpgroup)
-    const int t = (warp - 4) >> 2;
+    // ---------------------------------------------------------------- softmax
+    // 8 warps per tile: the two warps of a lane quarter split each query row's 128 key columns
+    // (half 0: columns 0..63, half 1: 64..127). They share the row max of every KV block through
+    // shared memory (pair barrier), keep partial row sums, and each rescales / normalises its
+    // half of the row's 128 O columns.
+    const int t = (warp - 4) >> 3;
+    const int half = ((warp - 4) >> 2) & 1;
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;
     const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
     const uint32_t tS = tmem + t * 128 + lane_addr, tO = tmem + 256 + t * 128 + lane_addr;
+    uint64_t* pbar = &pair_bar[t * 4 + quarter];
     float m_run = -INFINITY, l_run = 0.f;
     bool ok = true;
     for (int j = 0; j < n_kv; j++) {
-      if (!(ok = mbar_wait(&s_full[t], j & 1, abort_flag, p.status, kDevTimeoutAttn))) break;
+      if (!(ok = AW(t ? 8 : 5, mbar_wait(&s_full[t], j & 1, abort_flag, p.status, kDevTimeoutAttn)))) break;
       tc_fence_after();
-      const int valid = p.n_valid - j * BKV;  // keys >= valid are masked in this block
-      // the whole S row in registers: one TMEM round trip per block
-      uint32_t v[128];
-#pragma unroll
-      for (int c = 0; c < 4; c++) tmem_ld32(tS + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&v[32 * c]));
-      tmem_wait_ld();
-      if (valid < BKV) {
-#pragma unroll
-        for (int i = 0; i < 128; i++)
-          if (i >= valid) v[i] = __float_as_uint(-INFINITY);
-      }
+      const int valid = p.n_valid - j * BKV - half * 64;  // keys >= valid are masked in this half
+      // pass 1: row max of this half (32 columns at a time; S is read again for the exponentials)
       float mx = -INFINITY;
+#pragma unroll 1
+      for (int c = 0; c < 2; c++) {
+        uint32_t v[32];
+        if (AABL(1)) {
 #pragma unroll
-      for (int i = 0; i < 128; i += 2) mx = max3(mx, __uint_as_float(v[i]), __uint_as_float(v[i + 1]));
+          for (int i = 0; i < 32; i++) v[i] = __float_as_uint((float)(i + c));
+        } else {
+          tmem_ld32(tS + half * 64 + c * 32, v);
+          tmem_wait_ld();
+        }
+        if (valid < 64) {
+#pragma unroll
+          for (int i = 0; i < 32; i++)
+            if (c * 32 + i >= valid) v[i] = __float_as_uint(-INFINITY);
+        }
+#pragma unroll
+        for (int i = 0; i < 32; i += 2) mx = max3(mx, __uint_as_float(v[i]), __uint_as_float(v[i + 1]));
+      }
+      // row max over both halves
+      float* xm = xch + ((j & 1) * 2 + t) * 256;
+      xm[r * 2 + half] = mx;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(pbar);
+      if (!(ok = mbar_wait(pbar, j & 1, abort_flag, p.status, kDevTimeoutAttn))) break;
+      mx = fmaxf(mx, xm[r * 2 + (half ^ 1)]);
       const float m_new = fmaxf(m_run, mx * kScaleLog2);
       if (j == 0) {
         m_run = m_new;
@@ -287,13 +346,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (__any_sync(0xffffffffu, need)) {
           const float alpha = need ? ex2_approx(m_run - m_new) : 1.f;
 #pragma unroll 1
-          for (int c = 0; c < 4; c++) {
+          for (int c = 0; c < 2; c++) {
             uint32_t o[32];
-            tmem_ld32(tO + c * 32, o);
+            tmem_ld32(tO + half * 64 + c * 32, o);
             tmem_wait_ld();
 #pragma unroll
             for (int i = 0; i < 32; i++) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-            tmem_st32(tO + c * 32, o);
+            tmem_st32(tO + half * 64 + c * 32, o);
           }
           tmem_wait_st();
           l_run *= alpha;
@@ -302,15 +361,31 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       const uint64_t sc2 = pk2(kScaleLog2, kScaleLog2), nm2 = pk2(-m_run, -m_run);
       uint64_t sum2 = pk2(0.f, 0.f);
+      // pass 2: exponentials, 32 columns at a time; P chunk c (16 words) lands over S columns
+      // [32h + 16c, 32h + 16c + 16), which belong to chunk c of this half that is already read
+#pragma unroll 1
+      for (int c = 0; c < 2; c++) {
+        uint32_t v[32];
+        if (AABL(1)) {
 #pragma unroll
-      for (int c = 0; c < 4; c++) {
+          for (int i = 0; i < 32; i++) v[i] = __float_as_uint((float)(i - c));
+        } else {
+          tmem_ld32(tS + half * 64 + c * 32, v);
+          tmem_wait_ld();
+        }
+        if (valid < 64) {
+#pragma unroll
+          for (int i = 0; i < 32; i++)
+            if (c * 32 + i >= valid) v[i] = __float_as_uint(-INFINITY);
+        }
         uint32_t pk[16];
 #pragma unroll
         for (int i = 0; i < 16; i++) {
-          const uint64_t x2 = fma2(pk2(__uint_as_float(v[32 * c + 2 * i]), __uint_as_float(v[32 * c + 2 * i + 1])),
-                                   sc2, nm2);
+          const uint64_t x2 = fma2(pk2(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1])), sc2, nm2);
           float e0, e1;
-          if (2 * i < kPolyPerChunk) {
+          if (AABL(4)) {
+            up2(x2, e0, e1);
+          } else if (2 * i < kPolyPerChunk) {
             exp2_poly2(x2, e0, e1);
           } else {
             float x0, x1;
@@ -321,8 +396,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           sum2 = add2(sum2, pk2(e0, e1));
           pk[i] = pack_bf16x2(e0, e1);
         }
-        // P columns 16c..16c+15 overwrite S columns already held in registers
-        tmem_st16a(tS + c * 16, pk);
+        // P words 16c .. 16c+15 of this half (keys 64h + 32c ..) go to S columns 64h + 16c ..,
+        // which this thread has already read (chunk 0 covers columns 64h .. 64h+31)
+        if (!AABL(2)) tmem_st16a(tS + half * 64 + c * 16, pk);
       }
       float sa, sb;
       up2(sum2, sa, sb);
@@ -333,17 +409,26 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_full[t]);
     }
+    // row sum over both halves (pair barrier phase n_kv)
+    if (ok) {
+      float* xs = xch + 4 * 256 + t * 256;
+      xs[r * 2 + half] = l_run;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(pbar);
+      ok = mbar_wait(pbar, n_kv & 1, abort_flag, p.status, kDevTimeoutAttn);
+      if (ok) l_run += xs[r * 2 + (half ^ 1)];
+    }
     if (ok) ok = mbar_wait(&o_full[t], 0, abort_flag, p.status, kDevTimeoutAttn);
     if (ok) {
       tc_fence_after();
       const int qrow = q0 + t * BQ + r;
       const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
-      __nv_bfloat16* orow =
-          (qrow < p.split ? p.out + (int64_t)qrow * p.ldo : p.out2 + (int64_t)(qrow - p.split) * p.ldo) + (int64_t)h * D;
+      __nv_bfloat16* orow = (qrow < p.split ? p.out + (int64_t)qrow * p.ldo : p.out2 + (int64_t)(qrow - p.split) * p.ldo) +
+                            (int64_t)h * D + half * 64;
 #pragma unroll 1
-      for (int c = 0; c < 4; c++) {
+      for (int c = 0; c < 2; c++) {
         uint32_t o[32];
-        tmem_ld32(tO + c * 32, o);
+        tmem_ld32(tO + half * 64 + c * 32, o);
         tmem_wait_ld();
         if (qrow < p.Lq) {
 #pragma unroll
@@ -358,8 +443,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
+#ifdef MB_TRACE
+    if (t == 0) tr_[6] = (unsigned long long)(clock64() - t_start_);
+#endif
   }
 
+#ifdef MB_TRACE
+  if (p.trace && lane == 0 && (warp <= 1 || warp == 4 || warp == 12))
+    for (int i = 0; i < 9; i++)
+      if (tr_[i]) atomicAdd(p.trace + i, tr_[i]);
+#endif
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
@@ -369,6 +462,15 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 }  // namespace attn
+
+#ifdef MB_TRACE
+unsigned long long* g_attn_trace = nullptr;
+int g_attn_ablate = 0;
+extern "C" __attribute__((visibility("default"))) void mb_debug_set_attn_ablate(int f) { g_attn_ablate = f; }
+extern "C" __attribute__((visibility("default"))) void mb_debug_set_attn_trace(unsigned long long* buf) {
+  g_attn_trace = buf;
+}
+#endif
 
 cudaError_t launch_attention(const void* q, const void* k, const void* v, int H, int64_t Lq, int64_t Lk,
                              int64_t n_valid, void* out, int64_t ldo, cudaStream_t st, int64_t split_row,
@@ -394,6 +496,13 @@ cudaError_t launch_attention(const void* q, const void* k, const void* v, int H,
   p.split = (split_row < 0 || split_row > Lq) ? (int)Lq : (int)split_row;
   p.ldo = ldo;
   p.status = device_status_ptr();
+#ifdef MB_TRACE
+  p.trace = g_attn_trace;
+  p.ablate = g_attn_ablate;
+#else
+  p.trace = nullptr;
+  p.ablate = 0;
+#endif
   static int attr_done[64];
   int dev = 0;
   cudaGetDevice(&dev);
