@@ -563,9 +563,9 @@ def main():
             "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, one launch of the same shape "
                               "(profiles/k_qgemm_q4k_linear1_4608x21504x3072.md)"}
     step_flops = mb.flux.step_flops(cfg, L_TXT, L_IMG)
-    # launches per replayed step: timestep embeddings (2), batched GEMVs (3), casts (2), stems (2),
-    # final LN + linear (2), Euler (1), prologue (1); 8 per double block, 5 per single block
-    n_launch = 13 + cfg.depth * 8 + cfg.depth_single_blocks * 5
+    # launches per replayed step: timestep embeddings (2), batched GEMVs (3 x stage + run), casts (2),
+    # stems (2), final LN + linear (2), Euler (1), prologue (1); 8 per double block, 5 per single block
+    n_launch = 16 + cfg.depth * 8 + cfg.depth_single_blocks * 5
     line = {
         "metric": "flux_dev_1024_denoise_steps_per_s", "value": steps_per_s, "unit": "steps/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
@@ -576,8 +576,8 @@ def main():
                    "parallelism": f"replicas x{world} (one image per GPU, no collective)",
                    "l2": "inputs larger than L2 (6.7 GB of weights streamed per step)"},
         "images_per_s": steps_per_s / N_SCHEDULE,
-        "step_tflops": step_flops / 1e12, "step_frac_of_peak": step_flops * (steps_per_s / world) / 1e12 /
-        peaks["bf16_tflops_sustained"],
+        "step_tflops": step_flops / 1e12,
+        "step_frac_of_sustained": step_flops * (steps_per_s / world) / 1e12 / peaks["bf16_tflops_sustained"],
         "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": n_launch * args.steps,
         "clocks": clk.summary(), "kernels": kern, "finite": finite,
     }
@@ -680,9 +680,9 @@ def main_qwen(args, world, rank, local, dev, peaks):
             "kernel": "k_qgemm<%s> img_mlp.net.0.proj M=8192 N=12288 K=3072" % args.quant.upper(),
             "peak_source": peaks["source"] + " bf16_tflops (burst; kernel timed alone)"}
     step_flops = mb.qwen.step_flops(cfg, Q_TXT, L_IMG, batch=2)
-    # per replayed step: temb, 3 GEMVs, RMSNorm, txt_in, 2 casts, img_in, final LN + linear,
-    # CFG-Euler, prologue (13); per block 2 LN, 4 grouped GEMMs, 1 QK-norm, 2 attention
-    n_launch = 13 + cfg.num_layers * 9
+    # per replayed step: temb, 3 GEMVs (stage + run each), RMSNorm, txt_in, 2 casts, img_in, final
+    # LN + linear, CFG-Euler, prologue (16); per block 2 LN, 4 grouped GEMMs, 1 QK-norm, 2 attention
+    n_launch = 16 + cfg.num_layers * 9
     line = {
         "metric": METRIC["qwen"], "value": steps_per_s, "unit": "steps/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
@@ -694,7 +694,7 @@ def main_qwen(args, world, rank, local, dev, peaks):
                    "l2": "inputs larger than L2 (11.5 GB of weights streamed per step)"},
         "images_per_s": world / (ms_max / args.steps * Q_STEPS / 1e3),
         "step_tflops": step_flops / 1e12,
-        "step_frac_of_peak": step_flops * steps_per_s / world / 1e12 / peaks["bf16_tflops"],
+        "step_frac_of_sustained": step_flops * steps_per_s / world / 1e12 / peaks["bf16_tflops_sustained"],
         "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": n_launch * args.steps,
         "clocks": clk.summary(), "kernels": kern, "finite": finite,
     }
