@@ -19,7 +19,9 @@
  *  - One thread per device, as in mold's per-GPU worker threads
  *    (crates/mold-server/src/gpu_worker.rs:18-39); calls for different devices
  *    may run concurrently from different threads.
- *  - GGML type ids are GGUF's: F32=0, F16=1, Q8_0=8, Q4_K=12, BF16=30.
+ *  - GGML type ids are GGUF's: F32=0, F16=1, Q4_0=2, Q4_1=3, Q5_0=6, Q5_1=7, Q8_0=8,
+ *    Q4_K=12, Q5_K=13, Q6_K=14, BF16=30. Q6_K rows are re-laid on upload (each 210-byte
+ *    super-block padded to 224 bytes) so every 256-value chunk starts 16-byte aligned.
  *  - Element types of activations: MB_DT_F32 or MB_DT_BF16.
  */
 #ifndef MOLD_B200_H
@@ -48,7 +50,19 @@ typedef enum {
   MB_ERR_NOT_READY = 6    /* model missing tensors / not initialised */
 } mb_status;
 
-enum { MB_GGML_F32 = 0, MB_GGML_F16 = 1, MB_GGML_Q8_0 = 8, MB_GGML_Q4_K = 12, MB_GGML_BF16 = 30 };
+enum {
+  MB_GGML_F32 = 0,
+  MB_GGML_F16 = 1,
+  MB_GGML_Q4_0 = 2,
+  MB_GGML_Q4_1 = 3,
+  MB_GGML_Q5_0 = 6,
+  MB_GGML_Q5_1 = 7,
+  MB_GGML_Q8_0 = 8,
+  MB_GGML_Q4_K = 12,
+  MB_GGML_Q5_K = 13,
+  MB_GGML_Q6_K = 14,
+  MB_GGML_BF16 = 30
+};
 enum { MB_DT_F32 = 0, MB_DT_BF16 = 1 };
 
 /* Epilogues fused into the quantized linear. */

@@ -11,7 +11,8 @@ All arithmetic runs in libmold_b200.so behind the C ABI (include/mold_b200.h);
 this package only moves pointers. PyTorch provides device memory and streams.
 """
 from ._lib import (  # noqa: F401
-    GGML_F32, GGML_F16, GGML_Q8_0, GGML_Q4_K, GGML_BF16, DT_F32, DT_BF16,
+    GGML_F32, GGML_F16, GGML_Q8_0, GGML_Q4_K, GGML_BF16, GGML_Q4_0, GGML_Q4_1, GGML_Q5_0, GGML_Q5_1, GGML_Q5_K,
+    GGML_Q6_K, DT_F32, DT_BF16,
     EPI_NONE, EPI_GELU_TANH, EPI_GATE_RESIDUAL, MoldError, lib, LIB_PATH, SIGNATURES,
 )
 from .ops import (  # noqa: F401

@@ -11,6 +11,7 @@ LIB_PATH = os.environ.get("MOLD_B200_LIB") or os.path.join(_HERE, "libmold_b200.
 
 MB_OK, MB_ERR_INVALID, MB_ERR_UNSUPPORTED, MB_ERR_CUDA, MB_ERR_TIMEOUT, MB_ERR_NOMEM, MB_ERR_NOT_READY = range(7)
 GGML_F32, GGML_F16, GGML_Q8_0, GGML_Q4_K, GGML_BF16 = 0, 1, 8, 12, 30
+GGML_Q4_0, GGML_Q4_1, GGML_Q5_0, GGML_Q5_1, GGML_Q5_K, GGML_Q6_K = 2, 3, 6, 7, 13, 14
 DT_F32, DT_BF16 = 0, 1
 EPI_NONE, EPI_GELU_TANH, EPI_GATE_RESIDUAL = 0, 1, 2
 

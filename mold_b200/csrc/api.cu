@@ -54,7 +54,9 @@ int num_sms() {
 }
 
 bool ggml_type_supported(int t) {
-  return t == MB_GGML_F32 || t == MB_GGML_F16 || t == MB_GGML_BF16 || t == MB_GGML_Q8_0 || t == MB_GGML_Q4_K;
+  return t == MB_GGML_F32 || t == MB_GGML_F16 || t == MB_GGML_BF16 || t == MB_GGML_Q8_0 || t == MB_GGML_Q4_K ||
+         t == MB_GGML_Q4_0 || t == MB_GGML_Q4_1 || t == MB_GGML_Q5_0 || t == MB_GGML_Q5_1 || t == MB_GGML_Q5_K ||
+         t == MB_GGML_Q6_K;
 }
 
 int64_t row_bytes_of(int t, int64_t n_cols) {
@@ -64,8 +66,19 @@ int64_t row_bytes_of(int t, int64_t n_cols) {
     case MB_GGML_BF16: return n_cols * 2;
     case MB_GGML_Q8_0: return n_cols % 32 ? -1 : n_cols / 32 * 34;
     case MB_GGML_Q4_K: return n_cols % 256 ? -1 : n_cols / 256 * 144;
+    case MB_GGML_Q4_0: return n_cols % 32 ? -1 : n_cols / 32 * 18;
+    case MB_GGML_Q4_1: return n_cols % 32 ? -1 : n_cols / 32 * 20;
+    case MB_GGML_Q5_0: return n_cols % 32 ? -1 : n_cols / 32 * 22;
+    case MB_GGML_Q5_1: return n_cols % 32 ? -1 : n_cols / 32 * 24;
+    case MB_GGML_Q5_K: return n_cols % 256 ? -1 : n_cols / 256 * 176;
+    case MB_GGML_Q6_K: return n_cols % 256 ? -1 : n_cols / 256 * 210;
     default: return -1;
   }
+}
+
+int64_t device_row_bytes_of(int t, int64_t n_cols) {
+  if (t == MB_GGML_Q6_K) return n_cols % 256 ? -1 : n_cols / 256 * 224;
+  return row_bytes_of(t, n_cols);
 }
 
 // ---------------------------------------------------------------- TMA encode
@@ -187,13 +200,26 @@ mb_status mb_weight_create(int ggml_type, int64_t n_rows, int64_t n_cols, const 
   w->type = ggml_type;
   w->n_rows = n_rows;
   w->n_cols = n_cols;
-  w->row_bytes = rb;
+  w->row_bytes = device_row_bytes_of(ggml_type, n_cols);
   cudaGetDevice(&w->device);
-  if (cudaMalloc(&w->dev, nbytes) != cudaSuccess) {
+  const size_t dev_bytes = (size_t)w->row_bytes * (size_t)n_rows;
+  if (cudaMalloc(&w->dev, dev_bytes) != cudaSuccess) {
     delete w;
-    return set_error(MB_ERR_NOMEM, "cudaMalloc of " + std::to_string(nbytes) + " bytes for a weight failed");
+    return set_error(MB_ERR_NOMEM, "cudaMalloc of " + std::to_string(dev_bytes) + " bytes for a weight failed");
   }
-  cudaError_t e = cudaMemcpy(w->dev, data, nbytes, data_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice);
+  cudaError_t e = cudaSuccess;
+  if (ggml_type == MB_GGML_Q6_K) {
+    // re-lay 210-byte super-blocks into 224-byte ones (16-byte aligned chunks)
+    void* tmp = nullptr;
+    e = cudaMalloc(&tmp, nbytes);
+    if (e == cudaSuccess)
+      e = cudaMemcpy(tmp, data, nbytes, data_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = launch_relayout_q6k(tmp, w->dev, (int64_t)(nbytes / 210), 0);
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    if (tmp) cudaFree(tmp);
+  } else {
+    e = cudaMemcpy(w->dev, data, nbytes, data_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice);
+  }
   if (e != cudaSuccess) {
     cudaFree(w->dev);
     delete w;
@@ -236,8 +262,8 @@ mb_status mb_qlinear(const mb_weight* w, const void* x, int x_dtype, int64_t M, 
                      const float* residual, int64_t ldr, void* stream) {
   MB_CHECK(w && x && y, MB_ERR_INVALID, "weight, x or y is NULL");
   MB_CHECK(M >= 0, MB_ERR_INVALID, "M must be >= 0");
-  MB_CHECK(w->type == MB_GGML_Q4_K || w->type == MB_GGML_Q8_0 || w->type == MB_GGML_BF16, MB_ERR_UNSUPPORTED,
-           "mb_qlinear supports Q4_K, Q8_0 and BF16 weights (got ggml type " + std::to_string(w->type) + ")");
+  MB_CHECK(gemm_type_supported(w->type), MB_ERR_UNSUPPORTED,
+           "mb_qlinear supports BF16 and the quantized types Q4_0, Q4_1, Q5_0, Q5_1, Q8_0, Q4_K, Q5_K, Q6_K (got ggml type " + std::to_string(w->type) + ")");
   const int64_t K = w->n_cols, N = w->n_rows;
   MB_CHECK(K % 64 == 0, MB_ERR_INVALID, "K must be a multiple of 64");
   MB_CHECK(w->type == MB_GGML_BF16 || K % 256 == 0, MB_ERR_INVALID, "quantized K must be a multiple of 256");

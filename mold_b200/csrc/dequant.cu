@@ -2,14 +2,64 @@
 // and the f32 -> bf16 activation cast used by mb_qlinear's f32-input path.
 //
 // HBM-bound. One thread decodes one 64-value Q4_K group (16-byte header + 32
-// bytes of nibbles) or one 32-value Q8_0 block; stores are 16-byte vectors.
+// bytes of nibbles), one 32-value Q8_0 block, or one 32-value unit of the other
+// chunked types (ggml_decode.cuh); stores are 16-byte vectors.
 // Decode order follows the GGML formula with one rounding per operation
 // (multiply, then subtract), so the f32 output is bit-identical to the CPU
 // decode; the bf16 output is its round-to-nearest-even.
 #include "common.cuh"
+#include "ggml_decode.cuh"
 #include "internal.h"
 
 namespace mb {
+
+// Any chunked type (decode_unit): one thread per 32-value unit. Unit u of a row is unit u % 8 of
+// 256-value chunk u / 8 (for the 32-value block types that is simply block u, so rows only need
+// a multiple of 32 values).
+template <int T, bool BF16>
+__global__ void k_dequant_units(const uint8_t* __restrict__ raw, int64_t n_rows, int64_t n_units, int64_t row_bytes,
+                                void* __restrict__ out) {
+  const int64_t total = n_rows * n_units;
+  for (int64_t v = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; v < total; v += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t row = v / n_units, u = v % n_units;
+    float y[32];
+    decode_unit<T>(raw + row * row_bytes + (u >> 3) * kDeviceChunk(T), (int)(u & 7), y);
+    const int64_t obase = v * 32;
+#pragma unroll
+    for (int c = 0; c < 4; c++) {
+      if (BF16) {
+        uint4 w;
+        w.x = pack_bf16x2(y[8 * c + 0], y[8 * c + 1]);
+        w.y = pack_bf16x2(y[8 * c + 2], y[8 * c + 3]);
+        w.z = pack_bf16x2(y[8 * c + 4], y[8 * c + 5]);
+        w.w = pack_bf16x2(y[8 * c + 6], y[8 * c + 7]);
+        *(uint4*)((__nv_bfloat16*)out + obase + 8 * c) = w;
+      } else {
+        float4* o = (float4*)((float*)out + obase + 8 * c);
+        o[0] = make_float4(y[8 * c + 0], y[8 * c + 1], y[8 * c + 2], y[8 * c + 3]);
+        o[1] = make_float4(y[8 * c + 4], y[8 * c + 5], y[8 * c + 6], y[8 * c + 7]);
+      }
+    }
+  }
+}
+
+// Q6_K super-blocks 210 B (GGUF) -> 224 B (device layout, zero padding), one thread per 16 bytes.
+__global__ void k_relayout_q6k(const uint8_t* __restrict__ in, uint8_t* __restrict__ out, int64_t n_sb) {
+  const int64_t total = n_sb * 14;
+  for (int64_t v = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; v < total; v += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t sb = v / 14;
+    const int part = (int)(v % 14);
+    uint8_t b[16];
+#pragma unroll
+    for (int i = 0; i < 16; i++) {
+      const int o = part * 16 + i;
+      b[i] = o < 210 ? in[sb * 210 + o] : 0;
+    }
+    uint4 w;
+    memcpy(&w, b, 16);
+    *(uint4*)(out + sb * 224 + part * 16) = w;
+  }
+}
 
 MB_DEV float h2f_bits(uint32_t v) { return __half2float(__ushort_as_half((unsigned short)(v & 0xFFFFu))); }
 
@@ -126,6 +176,21 @@ cudaError_t launch_dequant(int type, const void* raw, int64_t n_rows, int64_t n_
       else k_dequant_q8_0<false><<<g, T, 0, st>>>(r, n_rows, nb, row_bytes, out);
       break;
     }
+#define MB_UNITS_CASE(TT)                                                                          \
+    case TT: {                                                                                     \
+      const int64_t nu = n_cols / 32;                                                              \
+      const int g = grid_for(n_rows * nu, T);                                                      \
+      if (out_bf16) k_dequant_units<TT, true><<<g, T, 0, st>>>(r, n_rows, nu, row_bytes, out);     \
+      else k_dequant_units<TT, false><<<g, T, 0, st>>>(r, n_rows, nu, row_bytes, out);             \
+      break;                                                                                       \
+    }
+    MB_UNITS_CASE(MB_GGML_Q4_0)
+    MB_UNITS_CASE(MB_GGML_Q4_1)
+    MB_UNITS_CASE(MB_GGML_Q5_0)
+    MB_UNITS_CASE(MB_GGML_Q5_1)
+    MB_UNITS_CASE(MB_GGML_Q5_K)
+    MB_UNITS_CASE(MB_GGML_Q6_K)
+#undef MB_UNITS_CASE
     case MB_GGML_F32:
       if (out_bf16) k_convert<MB_GGML_F32, true><<<grid_for(n, T), T, 0, st>>>(raw, n, out);
       else k_convert<MB_GGML_F32, false><<<grid_for(n, T), T, 0, st>>>(raw, n, out);
@@ -140,6 +205,12 @@ cudaError_t launch_dequant(int type, const void* raw, int64_t n_rows, int64_t n_
       break;
     default: return cudaErrorInvalidValue;
   }
+  return cudaGetLastError();
+}
+
+cudaError_t launch_relayout_q6k(const void* in, void* out, int64_t n_superblocks, cudaStream_t st) {
+  if (n_superblocks <= 0) return cudaSuccess;
+  k_relayout_q6k<<<grid_for(n_superblocks * 14, 256), 256, 0, st>>>((const uint8_t*)in, (uint8_t*)out, n_superblocks);
   return cudaGetLastError();
 }
 

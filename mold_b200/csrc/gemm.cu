@@ -30,6 +30,7 @@
 // to bf16 RNE. d1*q is formed as fma(d1, 2^23+q, -d1*2^23), which is the same
 // single rounding of the exact product.
 #include "common.cuh"
+#include "ggml_decode.cuh"
 #include "internal.h"
 
 namespace mb {
@@ -54,8 +55,12 @@ constexpr int kMaxSX = 4;         // A ring [256, 384)
 // warps leave 96 registers per thread; a register-resident copy spills).
 constexpr uint32_t kTmemStage = kTmemA + kMaxSX * 32;
 
+// Other quantized types: one 256-value chunk per row and raw stage (kDeviceChunk bytes, a
+// multiple of 16), decoded per 32-value unit by decode_unit<WT>.
 template <int WT>
-struct Cfg;
+struct Cfg {
+  static constexpr int kRawRow = kDeviceChunk(WT), kSPC = 4, kSR = 3, kSX = 4;
+};
 template <>
 struct Cfg<MB_GGML_Q4_K> {
   static constexpr int kRawRow = 144, kSPC = 4, kSR = 3, kSX = 4;  // whole super-blocks
@@ -69,8 +74,10 @@ struct Cfg<MB_GGML_BF16> {
   static constexpr int kRawRow = 128, kSPC = 1, kSR = 4, kSX = 4;
 };
 
-static_assert(Cfg<MB_GGML_Q4_K>::kSX <= kMaxSX && Cfg<MB_GGML_Q8_0>::kSX <= kMaxSX && Cfg<MB_GGML_BF16>::kSX <= kMaxSX,
+static_assert(Cfg<MB_GGML_Q4_K>::kSX <= kMaxSX && Cfg<MB_GGML_Q8_0>::kSX <= kMaxSX && Cfg<MB_GGML_BF16>::kSX <= kMaxSX &&
+                  Cfg<MB_GGML_Q6_K>::kSX <= kMaxSX,
               "A ring must fit below the epilogue staging columns");
+static_assert(1024 + 4 * 32768 + 3 * 128 * 224 + 512 <= 232448, "largest raw ring must fit in shared memory");
 template <int WT>
 constexpr size_t smem_bytes() {
   return 1024 + (size_t)Cfg<WT>::kSX * kXStageBytes + (size_t)Cfg<WT>::kSR * TN * Cfg<WT>::kRawRow + 512;
@@ -313,12 +320,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           mbar_expect_tx(&r_full[sr], kRawStage);
           uint8_t* rdst = rs + sr * kRawStage;
-          if (WT == MB_GGML_Q4_K) {
-            tma_load_2d(rdst, tm_w, &r_full[sr], (ks >> 2) * 144, n0);
-          } else if (WT == MB_GGML_Q8_0) {
+          if (WT == MB_GGML_Q8_0) {
             tma_load_2d(rdst, tm_w, &r_full[sr], (68 * ks) & ~15, n0);
-          } else {
+          } else if (WT == MB_GGML_BF16) {
             tma_load_2d(rdst, tm_w, &r_full[sr], ks * 128, n0);
+          } else {  // one whole 256-value chunk (ks is a multiple of kSPC = 4)
+            tma_load_2d(rdst, tm_w, &r_full[sr], (ks >> 2) * Cfg<WT>::kRawRow, n0);
           }
         }
       }
@@ -419,13 +426,18 @@ __global__ void __launch_bounds__(kThreads, 1)
               case 10: q8_block<10>(W, o); break;
               default: q8_block<14>(W, o); break;
             }
-          } else {
+          } else if (WT == MB_GGML_BF16) {
             const uint4* src = (const uint4*)(R + r * 128 + hh * 64);
 #pragma unroll
             for (int i = 0; i < 4; i++) {
               const uint4 v = src[i];
               o[4 * i] = v.x; o[4 * i + 1] = v.y; o[4 * i + 2] = v.z; o[4 * i + 3] = v.w;
             }
+          } else {
+            float y[32];
+            decode_unit<WT>(R + r * Cfg<WT>::kRawRow, 2 * j + hh, y);
+#pragma unroll
+            for (int i = 0; i < 16; i++) o[i] = pack_bf16x2(y[2 * i], y[2 * i + 1]);
           }
           if (j == kSPC - 1) {
             // generic-proxy reads of this raw chunk are ordered before the TMA that will refill it
@@ -632,7 +644,7 @@ bool make_maps(const mb_weight* w, const void* x, int64_t M, int64_t ldx, CUtens
                     TM, CU_TENSOR_MAP_SWIZZLE_128B))
     return false;
   const uint64_t rb = (uint64_t)w->row_bytes, nr = (uint64_t)w->n_rows;
-  const uint32_t box = WT == MB_GGML_Q4_K ? 144 : (WT == MB_GGML_Q8_0 ? 80 : 128);
+  const uint32_t box = (uint32_t)Cfg<WT>::kRawRow;
   return make_tmap_2d(tw, w->dev, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, rb, nr, rb, box, TN, CU_TENSOR_MAP_SWIZZLE_NONE);
 }
 
@@ -696,6 +708,12 @@ cudaError_t launch_qgemm_group(int n, const GemmProblem* g, cudaStream_t st) {
     case MB_GGML_Q4_K: return gemm::launch_t<MB_GGML_Q4_K>(n, g, st);
     case MB_GGML_Q8_0: return gemm::launch_t<MB_GGML_Q8_0>(n, g, st);
     case MB_GGML_BF16: return gemm::launch_t<MB_GGML_BF16>(n, g, st);
+    case MB_GGML_Q4_0: return gemm::launch_t<MB_GGML_Q4_0>(n, g, st);
+    case MB_GGML_Q4_1: return gemm::launch_t<MB_GGML_Q4_1>(n, g, st);
+    case MB_GGML_Q5_0: return gemm::launch_t<MB_GGML_Q5_0>(n, g, st);
+    case MB_GGML_Q5_1: return gemm::launch_t<MB_GGML_Q5_1>(n, g, st);
+    case MB_GGML_Q5_K: return gemm::launch_t<MB_GGML_Q5_K>(n, g, st);
+    case MB_GGML_Q6_K: return gemm::launch_t<MB_GGML_Q6_K>(n, g, st);
     default: return cudaErrorInvalidValue;
   }
 }

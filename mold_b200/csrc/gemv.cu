@@ -7,6 +7,7 @@
 // once, with no shared memory or barrier between the loads; the staged x values a lane
 // needs stay in its registers across the rows it serves.
 #include "common.cuh"
+#include "ggml_decode.cuh"
 #include "internal.h"
 
 namespace mb {
@@ -187,6 +188,44 @@ MB_DEV void rows_q8(const GemvJob& job, const float* __restrict__ xs, int r0, in
   finish_rows<LPR>(acc, r0, sub, sl, nr, job);
 }
 
+// Other chunked types: unit = 32 values decoded by decode_unit<T> straight from global memory.
+// Rows run one at a time (one accumulator, reduced and stored per row) to keep registers low.
+template <int T, int LPR>
+MB_DEV void rows_units(const GemvJob& job, const float* __restrict__ xs, int r0, int nr, int lane) {
+  constexpr int NSUB = 32 / LPR, RPL = kRowsPerWarp / NSUB;
+  const int sub = lane / LPR, sl = lane % LPR;
+  const int U = job.n_cols / 32;
+#pragma unroll 1
+  for (int i = 0; i < RPL; i++) {
+    const int rr = sub + i * NSUB;
+    const uint8_t* row = (const uint8_t*)job.w + (int64_t)(r0 + min(rr, nr - 1)) * job.row_bytes;
+    float acc = 0.f;
+    for (int u = sl; u < U; u += LPR) {
+      float y[32];
+      decode_unit<T>(row + (int64_t)(u >> 3) * kDeviceChunk(T), u & 7, y);
+#pragma unroll
+      for (int k4 = 0; k4 < 8; k4++) {
+        const float4 t = __ldg((const float4*)(xs + u * 32) + k4);
+        acc = fmaf(y[4 * k4], t.x, acc);
+        acc = fmaf(y[4 * k4 + 1], t.y, acc);
+        acc = fmaf(y[4 * k4 + 2], t.z, acc);
+        acc = fmaf(y[4 * k4 + 3], t.w, acc);
+      }
+    }
+#pragma unroll
+    for (int o = LPR / 2; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if (sl == 0 && rr < nr) job.y[r0 + rr] = acc + (job.bias ? job.bias[r0 + rr] : 0.f);
+  }
+}
+
+template <int T>
+MB_DEV void rows_units_any(const GemvJob& job, const float* __restrict__ xs, int r0, int nr, int lane) {
+  if ((job.n_cols / 32) % 32 == 0)
+    rows_units<T, 32>(job, xs, r0, nr, lane);
+  else
+    rows_units<T, 16>(job, xs, r0, nr, lane);
+}
+
 // F32 / F16 / BF16 rows: the whole warp serves one row at a time.
 MB_DEV void rows_plain(const GemvJob& job, const float* __restrict__ xs, int r0, int nr, int lane) {
   const uint8_t* wbase = (const uint8_t*)job.w + (int64_t)r0 * job.row_bytes;
@@ -231,6 +270,18 @@ __global__ void __launch_bounds__(kWarps * 32, 3)
       rows_q8<32>(job, xs, r0, nr, lane);
     else
       rows_q8<16>(job, xs, r0, nr, lane);
+  } else if (job.type == MB_GGML_Q4_0) {
+    rows_units_any<MB_GGML_Q4_0>(job, xs, r0, nr, lane);
+  } else if (job.type == MB_GGML_Q4_1) {
+    rows_units_any<MB_GGML_Q4_1>(job, xs, r0, nr, lane);
+  } else if (job.type == MB_GGML_Q5_0) {
+    rows_units_any<MB_GGML_Q5_0>(job, xs, r0, nr, lane);
+  } else if (job.type == MB_GGML_Q5_1) {
+    rows_units_any<MB_GGML_Q5_1>(job, xs, r0, nr, lane);
+  } else if (job.type == MB_GGML_Q5_K) {
+    rows_units_any<MB_GGML_Q5_K>(job, xs, r0, nr, lane);
+  } else if (job.type == MB_GGML_Q6_K) {
+    rows_units_any<MB_GGML_Q6_K>(job, xs, r0, nr, lane);
   } else {
     rows_plain(job, xs, r0, nr, lane);
   }

@@ -12,7 +12,7 @@ struct mb_weight {
   int type;        // GGML type id
   int64_t n_rows;  // output features
   int64_t n_cols;  // input features (blocks run along this axis)
-  int64_t row_bytes;
+  int64_t row_bytes;  // bytes per row on the device (Q6_K: 224 per 256 values, others as in GGUF)
   void* dev;       // device copy of the raw GGML bytes
   int device;
 };
@@ -35,8 +35,14 @@ mb_status cuda_error(cudaError_t e, const char* what);
 int num_sms();
 int* device_status_ptr();
 bool device_status_ready();  // true once mb_init allocated the status word on the current device  // per-device status word (allocated on first use)
-int64_t row_bytes_of(int ggml_type, int64_t n_cols);  // -1 if unsupported / not divisible
+int64_t row_bytes_of(int ggml_type, int64_t n_cols);         // GGUF bytes per row; -1 if unsupported / not divisible
+int64_t device_row_bytes_of(int ggml_type, int64_t n_cols);  // bytes per row as stored on the device
 bool ggml_type_supported(int ggml_type);
+// Weight types the tensor-core GEMM reads (quantized ones need n_cols % 256 == 0; BF16: % 64).
+inline bool gemm_type_supported(int t) {
+  return t == MB_GGML_BF16 || t == MB_GGML_Q8_0 || t == MB_GGML_Q4_K || t == MB_GGML_Q4_0 || t == MB_GGML_Q4_1 ||
+         t == MB_GGML_Q5_0 || t == MB_GGML_Q5_1 || t == MB_GGML_Q5_K || t == MB_GGML_Q6_K;
+}
 
 // ---- TMA descriptors ----
 bool make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, int elem_bytes, uint64_t inner,
@@ -74,6 +80,7 @@ struct GemmProblem {
 cudaError_t launch_qgemm_group(int n, const GemmProblem* g, cudaStream_t st);
 cudaError_t launch_dequant(int type, const void* raw, int64_t n_rows, int64_t n_cols, int64_t row_bytes, void* out,
                            int out_bf16, cudaStream_t st);
+cudaError_t launch_relayout_q6k(const void* in, void* out, int64_t n_superblocks, cudaStream_t st);
 cudaError_t launch_cast_f32_bf16(const float* x, int64_t M, int64_t K, int64_t ldx, void* y, int64_t ldy,
                                  cudaStream_t st);
 

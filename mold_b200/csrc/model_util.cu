@@ -66,7 +66,7 @@ mb_status upload_matrix(int ggml_type, int64_t n_rows, int64_t n_cols, const voi
   mb_weight* w = nullptr;
   MB_TRY(mb_weight_create(ggml_type, n_rows, n_cols, data, nbytes, on_device, &w));
   const bool gemm_ready =
-      (w->type == MB_GGML_Q4_K || w->type == MB_GGML_Q8_0) ? n_cols % 256 == 0 : w->type == MB_GGML_BF16;
+      w->type == MB_GGML_BF16 ? n_cols % 64 == 0 : (gemm_type_supported(w->type) && n_cols % 256 == 0);
   if (gemm && !gemm_ready) {
     // e.g. img_in [3072, 64]: rows shorter than the GEMM's quantized K step.
     mb_weight* wb = new mb_weight(*w);

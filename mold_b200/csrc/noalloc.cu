@@ -55,9 +55,9 @@ extern "C" mb_status mb_qlinear_f32_static(const mb_weight* w, const float* x, i
                                            void* stream) {
   MB_CHECK(w && x && y, MB_ERR_INVALID, "weight, x or y is NULL");
   MB_CHECK(M >= 0, MB_ERR_INVALID, "M must be >= 0");
-  MB_CHECK(w->type == MB_GGML_Q4_K || w->type == MB_GGML_Q8_0 || w->type == MB_GGML_BF16, MB_ERR_UNSUPPORTED,
-           "mb_qlinear_f32_static supports Q4_K, Q8_0 and BF16 weights (got ggml type " + std::to_string(w->type) +
-               ")");
+  MB_CHECK(gemm_type_supported(w->type), MB_ERR_UNSUPPORTED,
+           "mb_qlinear_f32_static supports BF16 and the quantized types Q4_0, Q4_1, Q5_0, Q5_1, Q8_0, Q4_K, Q5_K, "
+           "Q6_K (got ggml type " + std::to_string(w->type) + ")");
   const int64_t K = w->n_cols, N = w->n_rows;
   MB_CHECK((size_t)M * (size_t)K <= kStaticElems, MB_ERR_INVALID,
            "mb_qlinear_f32_static: M * K = " + std::to_string(M * K) + " exceeds the fixed staging buffer of " +

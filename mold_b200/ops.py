@@ -9,9 +9,12 @@ import numpy as np
 import torch
 
 from ._lib import (DT_BF16, DT_F32, EPI_GATE_RESIDUAL, EPI_GELU_TANH, EPI_NONE, GGML_BF16, GGML_F16, GGML_F32,
-                   GGML_Q4_K, GGML_Q8_0, check, lib)
+                   GGML_Q4_0, GGML_Q4_1, GGML_Q4_K, GGML_Q5_0, GGML_Q5_1, GGML_Q5_K, GGML_Q6_K, GGML_Q8_0, check, lib)
 
-_BLOCK = {GGML_F32: (1, 4), GGML_F16: (1, 2), GGML_BF16: (1, 2), GGML_Q8_0: (32, 34), GGML_Q4_K: (256, 144)}
+# (values, bytes) per GGUF block
+_BLOCK = {GGML_F32: (1, 4), GGML_F16: (1, 2), GGML_BF16: (1, 2), GGML_Q8_0: (32, 34), GGML_Q4_K: (256, 144),
+          GGML_Q4_0: (32, 18), GGML_Q4_1: (32, 20), GGML_Q5_0: (32, 22), GGML_Q5_1: (32, 24), GGML_Q5_K: (256, 176),
+          GGML_Q6_K: (256, 210)}
 _inited = set()
 
 

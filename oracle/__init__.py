@@ -16,6 +16,7 @@ Pinning status:
     math is **parity unpinned** beyond that restatement.
 """
 from .codec import (  # noqa: F401
-    GGML_F32, GGML_F16, GGML_Q8_0, GGML_Q4_K, GGML_BF16,
+    GGML_F32, GGML_F16, GGML_Q8_0, GGML_Q4_K, GGML_BF16, GGML_Q4_0, GGML_Q4_1, GGML_Q5_0, GGML_Q5_1, GGML_Q5_K,
+    GGML_Q6_K,
     block_bytes, block_elems, dequantize, quantize, randn, round_bf16, lib_path,
 )

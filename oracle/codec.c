@@ -19,8 +19,22 @@
  *     Pinned: bit-exact against the `gguf` 0.19.0 Python package
  *     (gguf/quants.py Q8_0.quantize_blocks/dequantize_blocks, Q4_K.dequantize_blocks);
  *     fixtures in tests/golden/ with the script that produced them.
+ *       Q4_0 : 18 bytes / 32 values  = f16 d, u8 qs[16];                x = d*(q-8)
+ *       Q4_1 : 20 bytes / 32 values  = f16 d, f16 m, u8 qs[16];         x = d*q + m
+ *       Q5_0 : 22 bytes / 32 values  = f16 d, u32 qh, u8 qs[16];        x = d*(q5-16)
+ *       Q5_1 : 24 bytes / 32 values  = f16 d, f16 m, u32 qh, u8 qs[16]; x = d*q5 + m
+ *              (value j < 16: low nibble of qs[j], high bit = bit j of qh; value j + 16:
+ *              high nibble of qs[j], high bit = bit j + 16 of qh)
+ *       Q5_K : 176 bytes / 256 values = f16 d, f16 dmin, u8 scales[12] (as Q4_K),
+ *              u8 qh[32], u8 qs[128]; x = (d*sc)*q5 - (dmin*m)
+ *       Q6_K : 210 bytes / 256 values = u8 ql[128], u8 qh[64], int8 scales[16], f16 d;
+ *              x = (d*sc)*(q6-32)
+ *     Every product above is exact in f32 (at most 24 significant bits), so each value is
+ *     one rounding of the exact result and does not depend on the evaluation order.
  *   - A Q8_0 quantizer equal to ggml's reference quantizer (amax/127, round half
  *     away from zero), pinned against gguf-py's Q8_0.quantize_blocks.
+ *   - Simple quantizers of this project's own for Q4_0/Q4_1/Q5_0/Q5_1/Q5_K/Q6_K (any
+ *     valid block exercises the same decode; only the decode must be bit-exact).
  *   - A Q4_K quantizer of this project's own (per-sub-block min/max, 6-bit
  *     scales relative to the super-block maxima). Any valid Q4_K block
  *     exercises the same decode; only the decode is required to be bit-exact.
@@ -228,7 +242,248 @@ static void dequant_q4_k(const uint8_t* in, int64_t nb, float* out) {
   }
 }
 
-/* ggml type ids (GGMLQuantizationType): F32=0, F16=1, Q8_0=8, Q4_K=12, BF16=30 */
+/* ---------- Q4_0 / Q4_1 / Q5_0 / Q5_1 (32-value blocks) ---------- */
+static void dequant_q4_01(const uint8_t* in, int64_t nb, float* out, int has_m) {
+  const int bytes = has_m ? 20 : 18;
+#pragma omp parallel for schedule(static)
+  for (int64_t b = 0; b < nb; b++) {
+    const uint8_t* ib = in + b * bytes;
+    uint16_t dh, mh = 0;
+    memcpy(&dh, ib, 2);
+    if (has_m) memcpy(&mh, ib + 2, 2);
+    const float d = h2f(dh), m = h2f(mh);
+    const uint8_t* qs = ib + (has_m ? 4 : 2);
+    float* y = out + b * 32;
+    for (int j = 0; j < 16; j++) {
+      const int q0 = qs[j] & 0xF, q1 = qs[j] >> 4;
+      if (has_m) {
+        y[j] = (float)q0 * d + m;
+        y[j + 16] = (float)q1 * d + m;
+      } else {
+        y[j] = (float)(q0 - 8) * d;
+        y[j + 16] = (float)(q1 - 8) * d;
+      }
+    }
+  }
+}
+
+static void dequant_q5_01(const uint8_t* in, int64_t nb, float* out, int has_m) {
+  const int bytes = has_m ? 24 : 22;
+#pragma omp parallel for schedule(static)
+  for (int64_t b = 0; b < nb; b++) {
+    const uint8_t* ib = in + b * bytes;
+    uint16_t dh, mh = 0;
+    uint32_t qh;
+    memcpy(&dh, ib, 2);
+    if (has_m) memcpy(&mh, ib + 2, 2);
+    memcpy(&qh, ib + (has_m ? 4 : 2), 4);
+    const float d = h2f(dh), m = h2f(mh);
+    const uint8_t* qs = ib + (has_m ? 8 : 6);
+    float* y = out + b * 32;
+    for (int j = 0; j < 16; j++) {
+      const int q0 = (qs[j] & 0xF) | (((qh >> j) & 1) << 4);
+      const int q1 = (qs[j] >> 4) | (((qh >> (j + 16)) & 1) << 4);
+      if (has_m) {
+        y[j] = (float)q0 * d + m;
+        y[j + 16] = (float)q1 * d + m;
+      } else {
+        y[j] = (float)(q0 - 16) * d;
+        y[j + 16] = (float)(q1 - 16) * d;
+      }
+    }
+  }
+}
+
+/* per-block min/max (affine types) or signed absmax (symmetric types) quantizer */
+void or_quantize_q4q5(const float* x, int64_t n, uint8_t* out, int bits, int has_m) {
+  const int bytes = bits == 4 ? (has_m ? 20 : 18) : (has_m ? 24 : 22);
+  const int qmax = (1 << bits) - 1;
+  int64_t nb = n / 32;
+#pragma omp parallel for schedule(static)
+  for (int64_t b = 0; b < nb; b++) {
+    const float* xb = x + b * 32;
+    uint8_t* ob = out + b * bytes;
+    float d, m = 0.f;
+    int q[32];
+    if (has_m) {
+      float mn = INFINITY, mx = -INFINITY;
+      for (int j = 0; j < 32; j++) { mn = fminf(mn, xb[j]); mx = fmaxf(mx, xb[j]); }
+      d = (mx - mn) / (float)qmax;
+      m = mn;
+      uint16_t dh = f2h(d), mh = f2h(m);
+      d = h2f(dh);
+      m = h2f(mh);
+      memcpy(ob, &dh, 2);
+      memcpy(ob + 2, &mh, 2);
+      for (int j = 0; j < 32; j++) q[j] = d > 0.f ? clampi((int)lrintf((xb[j] - m) / d), 0, qmax) : 0;
+    } else {
+      float amax = 0.f, vmax = 0.f;
+      for (int j = 0; j < 32; j++)
+        if (fabsf(xb[j]) > amax) { amax = fabsf(xb[j]); vmax = xb[j]; }
+      const int half = 1 << (bits - 1);
+      d = vmax / (float)(-half);
+      uint16_t dh = f2h(d);
+      d = h2f(dh);
+      memcpy(ob, &dh, 2);
+      for (int j = 0; j < 32; j++) q[j] = d != 0.f ? clampi((int)lrintf(xb[j] / d) + half, 0, qmax) : half;
+    }
+    uint8_t* qs = ob + (has_m ? 4 : 2);
+    if (bits == 5) {
+      uint32_t qh = 0;
+      for (int j = 0; j < 32; j++) qh |= (uint32_t)((q[j] >> 4) & 1) << j;
+      memcpy(qs, &qh, 4);
+      qs += 4;
+    }
+    for (int j = 0; j < 16; j++) qs[j] = (uint8_t)((q[j] & 0xF) | ((q[j + 16] & 0xF) << 4));
+  }
+}
+
+/* ---------- Q5_K ---------- */
+static void dequant_q5_k(const uint8_t* in, int64_t nb, float* out) {
+#pragma omp parallel for schedule(static)
+  for (int64_t b = 0; b < nb; b++) {
+    const uint8_t* ib = in + b * 176;
+    uint16_t dh, mh;
+    memcpy(&dh, ib, 2);
+    memcpy(&mh, ib + 2, 2);
+    const float d = h2f(dh), dmin = h2f(mh);
+    const uint8_t* s = ib + 4;
+    const uint8_t* qh = ib + 16;
+    const uint8_t* qs = ib + 48;
+    float* y = out + b * QK_K;
+    for (int g = 0; g < 4; g++) {
+      for (int h = 0; h < 2; h++) {
+        int sc, m;
+        q4k_scale_min(2 * g + h, s, &sc, &m);
+        const float d1 = d * (float)sc, m1 = dmin * (float)m;
+        for (int l = 0; l < 32; l++) {
+          const int q = (h ? (qs[32 * g + l] >> 4) : (qs[32 * g + l] & 0xF)) | (((qh[l] >> (2 * g + h)) & 1) << 4);
+          volatile float p = d1 * (float)q; /* exact; no FMA contraction */
+          y[64 * g + 32 * h + l] = p - m1;
+        }
+      }
+    }
+  }
+}
+
+void or_quantize_q5_k(const float* x, int64_t n, uint8_t* out) {
+  int64_t nb = n / QK_K;
+#pragma omp parallel for schedule(static)
+  for (int64_t b = 0; b < nb; b++) {
+    const float* xb = x + b * QK_K;
+    uint8_t* ob = out + b * 176;
+    float scale[8], mins[8], max_scale = 0.f, max_min = 0.f;
+    for (int j = 0; j < 8; j++) {
+      float mn = 0.f, mx = -INFINITY;
+      for (int l = 0; l < 32; l++) { mn = fminf(mn, xb[32 * j + l]); mx = fmaxf(mx, xb[32 * j + l]); }
+      if (mx < mn) mx = mn;
+      scale[j] = (mx - mn) / 31.f;
+      mins[j] = -mn;
+      max_scale = fmaxf(max_scale, scale[j]);
+      max_min = fmaxf(max_min, mins[j]);
+    }
+    uint16_t dh = f2h(max_scale / 63.f), mh = f2h(max_min / 63.f);
+    const float d = h2f(dh), dmin = h2f(mh);
+    int sc[8], m[8];
+    for (int j = 0; j < 8; j++) {
+      sc[j] = d > 0.f ? clampi((int)lrintf(scale[j] / d), 0, 63) : 0;
+      m[j] = dmin > 0.f ? clampi((int)lrintf(mins[j] / dmin), 0, 63) : 0;
+    }
+    memcpy(ob, &dh, 2);
+    memcpy(ob + 2, &mh, 2);
+    uint8_t* s = ob + 4;
+    for (int j = 0; j < 4; j++) {
+      s[j] = (uint8_t)((sc[j] & 63) | ((sc[j + 4] >> 4) << 6));
+      s[j + 4] = (uint8_t)((m[j] & 63) | ((m[j + 4] >> 4) << 6));
+      s[j + 8] = (uint8_t)((sc[j + 4] & 0xF) | ((m[j + 4] & 0xF) << 4));
+    }
+    uint8_t* qh = ob + 16;
+    uint8_t* qs = ob + 48;
+    memset(qh, 0, 32);
+    for (int g = 0; g < 4; g++) {
+      for (int l = 0; l < 32; l++) {
+        int q2[2];
+        for (int h = 0; h < 2; h++) {
+          const int j = 2 * g + h;
+          const float dl = d * (float)sc[j], ml = dmin * (float)m[j];
+          q2[h] = dl > 0.f ? clampi((int)lrintf((xb[32 * j + l] + ml) / dl), 0, 31) : 0;
+          qh[l] |= (uint8_t)(((q2[h] >> 4) & 1) << (2 * g + h));
+        }
+        qs[32 * g + l] = (uint8_t)((q2[0] & 0xF) | ((q2[1] & 0xF) << 4));
+      }
+    }
+  }
+}
+
+/* ---------- Q6_K ---------- */
+static void dequant_q6_k(const uint8_t* in, int64_t nb, float* out) {
+#pragma omp parallel for schedule(static)
+  for (int64_t b = 0; b < nb; b++) {
+    const uint8_t* ib = in + b * 210;
+    const uint8_t* ql = ib;
+    const uint8_t* qh = ib + 128;
+    const int8_t* sc = (const int8_t*)(ib + 192);
+    uint16_t dh;
+    memcpy(&dh, ib + 208, 2);
+    const float d = h2f(dh);
+    float* y = out + b * QK_K;
+    for (int n2 = 0; n2 < 2; n2++) {
+      for (int l = 0; l < 32; l++) {
+        const int is = l / 16;
+        const int q1 = (int)((ql[64 * n2 + l] & 0xF) | (((qh[32 * n2 + l] >> 0) & 3) << 4)) - 32;
+        const int q2 = (int)((ql[64 * n2 + l + 32] & 0xF) | (((qh[32 * n2 + l] >> 2) & 3) << 4)) - 32;
+        const int q3 = (int)((ql[64 * n2 + l] >> 4) | (((qh[32 * n2 + l] >> 4) & 3) << 4)) - 32;
+        const int q4 = (int)((ql[64 * n2 + l + 32] >> 4) | (((qh[32 * n2 + l] >> 6) & 3) << 4)) - 32;
+        y[128 * n2 + l] = d * (float)sc[8 * n2 + is + 0] * (float)q1;
+        y[128 * n2 + l + 32] = d * (float)sc[8 * n2 + is + 2] * (float)q2;
+        y[128 * n2 + l + 64] = d * (float)sc[8 * n2 + is + 4] * (float)q3;
+        y[128 * n2 + l + 96] = d * (float)sc[8 * n2 + is + 6] * (float)q4;
+      }
+    }
+  }
+}
+
+void or_quantize_q6_k(const float* x, int64_t n, uint8_t* out) {
+  int64_t nb = n / QK_K;
+#pragma omp parallel for schedule(static)
+  for (int64_t b = 0; b < nb; b++) {
+    const float* xb = x + b * QK_K;
+    uint8_t* ob = out + b * 210;
+    float sv[16], amax_all = 0.f;
+    for (int j = 0; j < 16; j++) {
+      float am = 0.f, vm = 0.f;
+      for (int l = 0; l < 16; l++)
+        if (fabsf(xb[16 * j + l]) > am) { am = fabsf(xb[16 * j + l]); vm = xb[16 * j + l]; }
+      sv[j] = vm / -32.f;
+      if (fabsf(sv[j]) > amax_all) amax_all = fabsf(sv[j]);
+    }
+    uint16_t dh = f2h(amax_all / 127.f);
+    const float d = h2f(dh);
+    int8_t* sc = (int8_t*)(ob + 192);
+    int q[QK_K];
+    for (int j = 0; j < 16; j++) {
+      sc[j] = (int8_t)(d > 0.f ? clampi((int)lrintf(sv[j] / d), -127, 127) : 0);
+      const float ds = d * (float)sc[j];
+      for (int l = 0; l < 16; l++) q[16 * j + l] = ds != 0.f ? clampi((int)lrintf(xb[16 * j + l] / ds) + 32, 0, 63) : 32;
+    }
+    uint8_t* ql = ob;
+    uint8_t* qh = ob + 128;
+    memset(ql, 0, 128);
+    memset(qh, 0, 64);
+    for (int n2 = 0; n2 < 2; n2++)
+      for (int l = 0; l < 32; l++) {
+        const int* qq = q + 128 * n2;
+        ql[64 * n2 + l] = (uint8_t)((qq[l] & 0xF) | ((qq[l + 64] & 0xF) << 4));
+        ql[64 * n2 + l + 32] = (uint8_t)((qq[l + 32] & 0xF) | ((qq[l + 96] & 0xF) << 4));
+        qh[32 * n2 + l] = (uint8_t)(((qq[l] >> 4) & 3) | (((qq[l + 32] >> 4) & 3) << 2) | (((qq[l + 64] >> 4) & 3) << 4) |
+                                    (((qq[l + 96] >> 4) & 3) << 6));
+      }
+    memcpy(ob + 208, &dh, 2);
+  }
+}
+
+/* ggml type ids (GGMLQuantizationType): F32=0, F16=1, Q4_0=2, Q4_1=3, Q5_0=6, Q5_1=7, Q8_0=8,
+ * Q4_K=12, Q5_K=13, Q6_K=14, BF16=30 */
 int or_dequantize(int ggml_type, const uint8_t* in, int64_t n, float* out) {
   switch (ggml_type) {
     case 0: memcpy(out, in, (size_t)n * 4); return 0;
@@ -246,6 +501,24 @@ int or_dequantize(int ggml_type, const uint8_t* in, int64_t n, float* out) {
     case 12:
       if (n % QK_K) return -1;
       dequant_q4_k(in, n / QK_K, out);
+      return 0;
+    case 2:
+    case 3:
+      if (n % 32) return -1;
+      dequant_q4_01(in, n / 32, out, ggml_type == 3);
+      return 0;
+    case 6:
+    case 7:
+      if (n % 32) return -1;
+      dequant_q5_01(in, n / 32, out, ggml_type == 7);
+      return 0;
+    case 13:
+      if (n % QK_K) return -1;
+      dequant_q5_k(in, n / QK_K, out);
+      return 0;
+    case 14:
+      if (n % QK_K) return -1;
+      dequant_q6_k(in, n / QK_K, out);
       return 0;
     default: return -2;
   }

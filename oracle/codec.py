@@ -6,7 +6,10 @@ import subprocess
 import numpy as np
 
 GGML_F32, GGML_F16, GGML_Q8_0, GGML_Q4_K, GGML_BF16 = 0, 1, 8, 12, 30
-_BLOCK = {GGML_F32: (1, 4), GGML_F16: (1, 2), GGML_BF16: (1, 2), GGML_Q8_0: (32, 34), GGML_Q4_K: (256, 144)}
+GGML_Q4_0, GGML_Q4_1, GGML_Q5_0, GGML_Q5_1, GGML_Q5_K, GGML_Q6_K = 2, 3, 6, 7, 13, 14
+_BLOCK = {GGML_F32: (1, 4), GGML_F16: (1, 2), GGML_BF16: (1, 2), GGML_Q8_0: (32, 34), GGML_Q4_K: (256, 144),
+          GGML_Q4_0: (32, 18), GGML_Q4_1: (32, 20), GGML_Q5_0: (32, 22), GGML_Q5_1: (32, 24),
+          GGML_Q5_K: (256, 176), GGML_Q6_K: (256, 210)}
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
 lib_path = os.path.join(_HERE, "liboracle.so")
@@ -25,6 +28,9 @@ def _load():
         _lib.or_dequantize.restype = ctypes.c_int
         _lib.or_quantize_q8_0.argtypes = [P, I64, P]
         _lib.or_quantize_q4_k.argtypes = [P, I64, P]
+        _lib.or_quantize_q4q5.argtypes = [P, I64, P, ctypes.c_int, ctypes.c_int]
+        _lib.or_quantize_q5_k.argtypes = [P, I64, P]
+        _lib.or_quantize_q6_k.argtypes = [P, I64, P]
         _lib.or_randn.argtypes = [ctypes.c_uint64, I64, ctypes.c_float, P]
         _lib.or_round_bf16.argtypes = [P, I64, P]
     return _lib
@@ -78,6 +84,13 @@ def quantize(x, t):
         _load().or_quantize_q8_0(x.ctypes.data, x.size, out.ctypes.data)
     elif t == GGML_Q4_K:
         _load().or_quantize_q4_k(x.ctypes.data, x.size, out.ctypes.data)
+    elif t in (GGML_Q4_0, GGML_Q4_1, GGML_Q5_0, GGML_Q5_1):
+        bits = 4 if t in (GGML_Q4_0, GGML_Q4_1) else 5
+        _load().or_quantize_q4q5(x.ctypes.data, x.size, out.ctypes.data, bits, int(t in (GGML_Q4_1, GGML_Q5_1)))
+    elif t == GGML_Q5_K:
+        _load().or_quantize_q5_k(x.ctypes.data, x.size, out.ctypes.data)
+    elif t == GGML_Q6_K:
+        _load().or_quantize_q6_k(x.ctypes.data, x.size, out.ctypes.data)
     else:
         raise ValueError(f"no quantizer for ggml type {t}")
     return out

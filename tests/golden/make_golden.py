@@ -14,6 +14,9 @@ Fixtures (codec_golden.npz):
                so every 6-bit scale/min packing pattern occurs) + 32 blocks from
                the oracle's own quantizer
   q4k_deq      gguf-py Q4_K.dequantize_blocks of q4k_blocks
+  <t>_blocks / <t>_deq for t in q4_0, q4_1, q5_0, q5_1, q5_k, q6_k: 64 blocks of random bytes
+               (finite, moderate f16 scale fields) + 16 blocks from the oracle's own quantizer,
+               and gguf-py's dequantize_blocks of them
 """
 import os
 import sys
@@ -45,9 +48,23 @@ def main():
     q4k_blocks = np.concatenate([rand_blocks, own], axis=0)
     q4k_deq = quants.dequantize(q4k_blocks.reshape(-1), gguf.GGMLQuantizationType.Q4_K).reshape(96, 256)
 
+    extra = {}
+    # (ggml id, gguf name, block bytes, block values, byte offsets of f16 scale fields)
+    for tid, name, bb, be, f16_at in ((oracle.GGML_Q4_0, "Q4_0", 18, 32, (0,)), (oracle.GGML_Q4_1, "Q4_1", 20, 32, (0, 2)),
+                                      (oracle.GGML_Q5_0, "Q5_0", 22, 32, (0,)), (oracle.GGML_Q5_1, "Q5_1", 24, 32, (0, 2)),
+                                      (oracle.GGML_Q5_K, "Q5_K", 176, 256, (0, 2)), (oracle.GGML_Q6_K, "Q6_K", 210, 256, (208,))):
+        rb = rng.integers(0, 256, size=(64, bb), dtype=np.uint8)
+        for off in f16_at:
+            rb[:, off:off + 2] = rng.uniform(-0.01, 0.01, size=(64, 1)).astype(np.float16).view(np.uint8).reshape(64, 2)
+        own = oracle.quantize(oracle.randn(9 + tid, (16, be), 0.02), tid).reshape(16, bb)
+        blocks = np.concatenate([rb, own], axis=0)
+        deq = quants.dequantize(blocks.reshape(-1), getattr(gguf.GGMLQuantizationType, name)).reshape(80, be)
+        extra[name.lower() + "_blocks"] = blocks
+        extra[name.lower() + "_deq"] = deq.astype(np.float32)
+
     out = os.path.join(os.path.dirname(os.path.abspath(__file__)), "codec_golden.npz")
     np.savez_compressed(out, q8_in=q8_in, q8_blocks=q8_blocks, q8_deq=q8_deq,
-                        q4k_blocks=q4k_blocks, q4k_deq=q4k_deq)
+                        q4k_blocks=q4k_blocks, q4k_deq=q4k_deq, **extra)
     print("wrote", out)
 
 

@@ -46,8 +46,8 @@ def test_invalid_arguments_report_status():
     lib = mold_b200.lib()
     out = ctypes.c_void_p()
     data = np.zeros(144, np.uint8)
-    # unsupported ggml type (Q5_K = 13)
-    rc = lib.mb_weight_create(13, 1, 256, data.ctypes.data_as(ctypes.c_void_p), 144, 0, ctypes.byref(out))
+    # unsupported ggml type (Q2_K = 10)
+    rc = lib.mb_weight_create(10, 1, 256, data.ctypes.data_as(ctypes.c_void_p), 144, 0, ctypes.byref(out))
     assert rc == _lib.MB_ERR_UNSUPPORTED
     assert b"unsupported ggml type" in lib.mb_last_error()
     # n_cols not a multiple of the Q4_K block

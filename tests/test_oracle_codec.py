@@ -79,3 +79,21 @@ def test_bf16_rounding_rne():
     r = oracle.round_bf16(x)
     assert r[0] == 1.0 and r[1] == 1.0  # tie to even
     assert r[2] == np.float32(1.0078125)
+
+
+NEW_TYPES = [("q4_0", oracle.GGML_Q4_0, 32), ("q4_1", oracle.GGML_Q4_1, 32), ("q5_0", oracle.GGML_Q5_0, 32),
+             ("q5_1", oracle.GGML_Q5_1, 32), ("q5_k", oracle.GGML_Q5_K, 256), ("q6_k", oracle.GGML_Q6_K, 256)]
+
+
+@pytest.mark.parametrize("name,t,be", NEW_TYPES)
+def test_dequant_bit_exact_random_blocks(gold, name, t, be):
+    blocks = gold[name + "_blocks"]
+    d = oracle.dequantize(blocks, t, (blocks.shape[0], be))
+    assert np.array_equal(d.view(np.uint32), gold[name + "_deq"].view(np.uint32))
+
+
+@pytest.mark.parametrize("name,t,be", NEW_TYPES)
+def test_quantizer_roundtrip_error(name, t, be):
+    x = oracle.randn(21, (8, 1024), 0.02)
+    err = np.linalg.norm(oracle.dequantize(oracle.quantize(x, t), t, x.shape) - x) / np.linalg.norm(x)
+    assert err < (0.1 if name.startswith("q4") else 0.05), err
