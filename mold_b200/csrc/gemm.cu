@@ -180,6 +180,79 @@ MB_DEV void dq8(uint32_t q, uint64_t d, uint32_t& o0, uint32_t& o1) {
   o1 = bf16x2_of(fmul2(fsub2(f2(f2v, f3), kBias), d));
 }
 
+// ---- packed decoders for the GEMM's per-thread 32-value units (o[16] = 16 bf16 pairs) ----
+// 2^23 + b for the four bytes of `b` (each 0..255) as floats.
+MB_DEV void magic4(uint32_t b, float& f0, float& f1, float& f2v, float& f3) {
+  f0 = __int_as_float(__byte_perm(b, 0x4B000000u, 0x7440));
+  f1 = __int_as_float(__byte_perm(b, 0x4B000000u, 0x7441));
+  f2v = __int_as_float(__byte_perm(b, 0x4B000000u, 0x7442));
+  f3 = __int_as_float(__byte_perm(b, 0x4B000000u, 0x7443));
+}
+
+// Q6_K unit u of a 224-byte chunk: x = (d sc) (q6 - 32); q6 - 32 = (2^23 + q6) - (2^23 + 32) exactly,
+// then one rounding of the product.
+MB_DEV void dq_unit_q6k(const uint8_t* c, int u, uint32_t (&o)[16]) {
+  const int n = u >> 2, g = u & 3;
+  const uint4* ql = (const uint4*)(c + 64 * n + 32 * (g & 1));
+  const uint4* qh = (const uint4*)(c + 128 + 32 * n);
+  const int8_t* sc = (const int8_t*)(c + 192 + 8 * n + 2 * g);
+  const float d = h16(*(const uint16_t*)(c + 208));
+  const float ds0 = d * (float)sc[0], ds1 = d * (float)sc[1];
+  const int nsh = (g >> 1) * 4, hsh = 2 * g;
+  const uint64_t off = f2(8388640.f, 8388640.f);  // 2^23 + 32
+#pragma unroll
+  for (int v = 0; v < 2; v++) {
+    const uint4 L = ql[v], Hh = qh[v];
+    const uint32_t lw[4] = {L.x, L.y, L.z, L.w}, hw[4] = {Hh.x, Hh.y, Hh.z, Hh.w};
+    const uint64_t D = v ? f2(ds1, ds1) : f2(ds0, ds0);
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+      const uint32_t q = ((lw[i] >> nsh) & 0x0F0F0F0Fu) | (((hw[i] >> hsh) & 0x03030303u) << 4);
+      float a0, a1, a2, a3;
+      magic4(q, a0, a1, a2, a3);
+      o[8 * v + 2 * i] = bf16x2_of(fmul2(fsub2(f2(a0, a1), off), D));
+      o[8 * v + 2 * i + 1] = bf16x2_of(fmul2(fsub2(f2(a2, a3), off), D));
+    }
+  }
+}
+
+// Q5_K unit u of a 176-byte chunk: x = d1 q5 - m1 with d1 q5 = fma(d1, 2^23 + q5, -d1 2^23) exact.
+MB_DEV void dq_unit_q5k(const uint8_t* c, int u, uint32_t (&o)[16]) {
+  const uint4 h = *(const uint4*)c;
+  const float d = h16(h.x), dmin = h16(h.x >> 16);
+  int sc, m;
+  q4k_scale_min(u, h.y, h.z, h.w, sc, m);
+  const float d1 = d * (float)sc, m1 = dmin * (float)m;
+  const uint64_t D1 = f2(d1, d1), C1 = f2(-(d1 * 8388608.f), -(d1 * 8388608.f)), M1 = f2(m1, m1);
+  const uint4* qh = (const uint4*)(c + 16);
+  const uint4* qs = (const uint4*)(c + 48 + 32 * (u >> 1));
+  const int sh = (u & 1) * 4;
+#pragma unroll
+  for (int v = 0; v < 2; v++) {
+    const uint4 Q = qs[v], Hh = qh[v];
+    const uint32_t qw[4] = {Q.x, Q.y, Q.z, Q.w}, hw[4] = {Hh.x, Hh.y, Hh.z, Hh.w};
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+      const uint32_t q = ((qw[i] >> sh) & 0x0F0F0F0Fu) | (((hw[i] >> u) & 0x01010101u) << 4);
+      dq4(q, D1, C1, M1, o[8 * v + 2 * i], o[8 * v + 2 * i + 1]);
+    }
+  }
+}
+
+// Q4_1 unit u (block u of a 160-byte chunk): x = d q + m with d q exact.
+MB_DEV void dq_unit_q41(const uint8_t* c, int u, uint32_t (&o)[16]) {
+  const uint32_t* a = (const uint32_t*)(c + u * 20);
+  const float d = h16(a[0]), m = h16(a[0] >> 16);
+  const uint64_t D = f2(d, d), C = f2(-(d * 8388608.f), -(d * 8388608.f)), Mm = f2(-m, -m);
+#pragma unroll
+  for (int i = 0; i < 4; i++) {
+    const uint32_t w = a[1 + i];
+    // values 4i..4i+3 (low nibbles) and 16 + 4i.. (high nibbles); dq4 computes d q - (-m)
+    dq4(w & 0x0F0F0F0Fu, D, C, Mm, o[2 * i], o[2 * i + 1]);
+    dq4((w >> 4) & 0x0F0F0F0Fu, D, C, Mm, o[8 + 2 * i], o[8 + 2 * i + 1]);
+  }
+}
+
 // Q8_0 block at byte offset P (compile-time) of a 48-byte window W[12].
 template <int P>
 MB_DEV void q8_block(const uint32_t (&W)[12], uint32_t (&o)[16]) {
@@ -433,6 +506,12 @@ __global__ void __launch_bounds__(kThreads, 1)
               const uint4 v = src[i];
               o[4 * i] = v.x; o[4 * i + 1] = v.y; o[4 * i + 2] = v.z; o[4 * i + 3] = v.w;
             }
+          } else if (WT == MB_GGML_Q6_K) {
+            dq_unit_q6k(R + r * Cfg<WT>::kRawRow, 2 * j + hh, o);
+          } else if (WT == MB_GGML_Q5_K) {
+            dq_unit_q5k(R + r * Cfg<WT>::kRawRow, 2 * j + hh, o);
+          } else if (WT == MB_GGML_Q4_1) {
+            dq_unit_q41(R + r * Cfg<WT>::kRawRow, 2 * j + hh, o);
           } else {
             float y[32];
             decode_unit<WT>(R + r * Cfg<WT>::kRawRow, 2 * j + hh, y);
