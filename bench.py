@@ -45,7 +45,8 @@ def parse():
     ap.add_argument("--steps", type=int, default=28)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--quant", default="q4_k", choices=["q4_k", "q8_0"])
+    ap.add_argument("--quant", default="q4_k", choices=["q4_k", "q8_0", "q4_1", "q6_k"],
+                    help="GGUF type of the synthetic weights (the headline is q4_k)")
     ap.add_argument("--model", default="flux", choices=["flux", "qwen"],
                     help="flux: the headline FLUX.1-dev line; qwen: Qwen-Image 1024x1024 with CFG (config 5)")
     ap.add_argument("--no-e2e", action="store_true")
@@ -158,6 +159,53 @@ def q8_0_quantize_torch(x):
     return torch.cat([d.half().view(torch.uint8).reshape(N, K // 32, 2), q.view(torch.uint8)], -1).reshape(N, -1)
 
 
+def q4_1_quantize_torch(x):
+    """f32 [N, K] -> Q4_1 bytes [N, K/32*20]: per 32-value block d = (max - min)/15, m = min (f16)."""
+    import torch
+    N, K = x.shape
+    xb = x.reshape(N, K // 32, 32)
+    mn, mx = xb.amin(-1), xb.amax(-1)
+    d = ((mx - mn) / 15.0).half()
+    m = mn.half()
+    df, mf = d.float().unsqueeze(-1), m.float().unsqueeze(-1)
+    q = torch.where(df > 0, torch.clamp(torch.round((xb - mf) / df.clamp_min(1e-30)), 0, 15), torch.zeros_like(xb))
+    q = q.to(torch.uint8)
+    qs = q[..., :16] | (q[..., 16:] << 4)
+    head = torch.cat([d.view(torch.uint8).reshape(N, K // 32, 2), m.view(torch.uint8).reshape(N, K // 32, 2)], -1)
+    return torch.cat([head, qs], -1).reshape(N, -1).contiguous()
+
+
+def q6_k_quantize_torch(x):
+    """f32 [N, K] -> Q6_K bytes [N, K/256*210]: signed absmax scale per 16 values, int8 scales
+    relative to the super-block's largest (f16 d), 6-bit quants."""
+    import torch
+    N, K = x.shape
+    nb = K // 256
+    xs = x.reshape(N, nb, 16, 16)
+    idx = xs.abs().argmax(-1, keepdim=True)
+    sv = torch.gather(xs, -1, idx).squeeze(-1) / -32.0
+    d = (sv.abs().amax(-1) / 127.0).half()
+    df = d.float().unsqueeze(-1)
+    sc = torch.where(df > 0, torch.clamp(torch.round(sv / df.clamp_min(1e-30)), -127, 127), torch.zeros_like(sv))
+    ds = (df * sc).unsqueeze(-1)
+    q = torch.where(ds != 0, torch.clamp(torch.round(xs / torch.where(ds != 0, ds, torch.ones_like(ds))) + 32, 0, 63),
+                    torch.full_like(xs, 32.0)).to(torch.int32).reshape(N, nb, 2, 4, 32)  # (n2, quarter g, l)
+    ql0 = (q[:, :, :, 0] & 0xF) | ((q[:, :, :, 2] & 0xF) << 4)
+    ql1 = (q[:, :, :, 1] & 0xF) | ((q[:, :, :, 3] & 0xF) << 4)
+    ql = torch.stack([ql0, ql1], 3).reshape(N, nb, 128)
+    qh = (((q[:, :, :, 0] >> 4) & 3) | (((q[:, :, :, 1] >> 4) & 3) << 2) | (((q[:, :, :, 2] >> 4) & 3) << 4) |
+          (((q[:, :, :, 3] >> 4) & 3) << 6)).reshape(N, nb, 64)
+    out = torch.cat([ql.to(torch.uint8), qh.to(torch.uint8), sc.to(torch.int8).view(torch.uint8),
+                     d.view(torch.uint8).reshape(N, nb, 2)], -1)
+    return out.reshape(N, nb * 210).contiguous()
+
+
+def quantizer(quant):
+    """(ggml type id, torch quantizer, values per block) of a --quant choice."""
+    return {"q4_k": (12, q4k_quantize_torch, 256), "q8_0": (8, q8_0_quantize_torch, 32),
+            "q4_1": (3, q4_1_quantize_torch, 32), "q6_k": (14, q6_k_quantize_torch, 256)}[quant]
+
+
 def build_flux(quant, device, seed=0):
     import torch
     import mold_b200 as mb
@@ -165,13 +213,13 @@ def build_flux(quant, device, seed=0):
     model = mb.FluxTransformer(cfg, max_txt=L_TXT, max_img=L_IMG, device=device)
     g = torch.Generator(device=f"cuda:{device}")
     keep = {}
-    gtype = mb.GGML_Q4_K if quant == "q4_k" else mb.GGML_Q8_0
+    gtype, qfn, _ = quantizer(quant)
     for i, (name, shape) in enumerate(mb.flux.tensor_specs(cfg)):
         g.manual_seed(seed * 1000003 + i)
         if len(shape) == 2:
             x = torch.randn(shape, generator=g, device=f"cuda:{device}") * 0.02
             if shape[1] % 256 == 0:
-                raw = q4k_quantize_torch(x) if gtype == mb.GGML_Q4_K else q8_0_quantize_torch(x)
+                raw = qfn(x)
                 model.set_tensor(name, (raw, gtype, shape))
             else:  # rows shorter than a super-block (img_in [3072, 64]) stay BF16 as in GGUF files
                 raw = x.bfloat16().view(torch.uint8).reshape(shape[0], -1).contiguous()
@@ -200,13 +248,13 @@ def build_qwen(quant, device, seed=0):
     model = mb.QwenTransformer(cfg, max_txt=Q_TXT, max_img=L_IMG, max_batch=2, device=device)
     g = torch.Generator(device=f"cuda:{device}")
     keep = {}
-    gtype = mb.GGML_Q4_K if quant == "q4_k" else mb.GGML_Q8_0
+    gtype, qfn, _ = quantizer(quant)
     for i, (name, shape) in enumerate(mb.qwen.tensor_specs(cfg)):
         g.manual_seed(seed * 1000003 + i)
         x = torch.randn(shape, generator=g, device=f"cuda:{device}") * 0.02
         if len(shape) == 2:
             if shape[1] % 256 == 0:
-                raw = q4k_quantize_torch(x) if gtype == mb.GGML_Q4_K else q8_0_quantize_torch(x)
+                raw = qfn(x)
                 model.set_tensor(name, (raw, gtype, shape))
             else:
                 raw = x.bfloat16().view(torch.uint8).reshape(shape[0], -1).contiguous()
@@ -235,7 +283,7 @@ class CpuSample:
         import oracle
         self.F = F
         self.cfg = F.FluxConfig(depth=0, depth_single_blocks=1)
-        qt = oracle.GGML_Q4_K if quant == "q4_k" else oracle.GGML_Q8_0
+        qt = quantizer(quant)[0]
         self.W = F.synth_weights(self.cfg, seed=0, qtype=qt, only=lambda n: n.startswith("single_blocks.0."))
         L = l_txt + l_img
         side = int(round(l_img ** 0.5))
@@ -274,7 +322,7 @@ class QwenCpuSample:
         import oracle
         self.Q = Q
         self.cfg = Q.QwenConfig(num_layers=1)
-        qt = oracle.GGML_Q4_K if quant == "q4_k" else oracle.GGML_Q8_0
+        qt = quantizer(quant)[0]
         self.W = Q.synth_weights(self.cfg, seed=0, qtype=qt, only=lambda n: n.startswith("transformer_blocks.0."))
         side = int(round(l_img ** 0.5))
         self.img = oracle.randn(1, (l_img, 3072))
@@ -456,8 +504,8 @@ def main():
         # the dominant kernels alone, on one linear1-shaped weight (small enough for an ncu capture)
         g = torch.Generator(device=dev).manual_seed(7)
         x = torch.randn((3 * 3072 + 12288, 3072), generator=g, device=dev) * 0.02
-        raw = q4k_quantize_torch(x) if args.quant == "q4_k" else q8_0_quantize_torch(x)
-        gtype = mb.GGML_Q4_K if args.quant == "q4_k" else mb.GGML_Q8_0
+        gtype, qfn, _ = quantizer(args.quant)
+        raw = qfn(x)
         k = time_kernels({"linear1": (raw, gtype, tuple(x.shape))}, local, peaks, reps=5)
         if rank == 0:
             print(json.dumps({"kernels": k}), flush=True)
