@@ -471,7 +471,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (ABL(1)) {
 #pragma unroll
             for (int i = 0; i < 16; i++) o[i] = 0x3c003c00u ^ (uint32_t)(ks + i);
-          } else if (WT == MB_GGML_Q4_K) {
+          } else if constexpr (WT == MB_GGML_Q4_K) {
             const uint4* qp = (const uint4*)(R + r * 144 + 16 + 32 * j);
             const uint4 qa = qp[0], qb = qp[1];
             const float d1 = d1v[j], m1 = m1v[j];
@@ -481,7 +481,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t w[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
 #pragma unroll
             for (int i = 0; i < 8; i++) dq4(w[i] & mask, D1, C1, M1, o[2 * i], o[2 * i + 1]);
-          } else if (WT == MB_GGML_Q8_0) {
+          } else if constexpr (WT == MB_GGML_Q8_0) {
             const int off = (68 * ks) & 15;  // window offset of block 0 (0,4,8,12)
             const int base16 = hh ? 32 : 0;  // 16-aligned start of the 48-byte window
             const uint4* src = (const uint4*)(R + r * 80 + base16);
@@ -499,18 +499,18 @@ __global__ void __launch_bounds__(kThreads, 1)
               case 10: q8_block<10>(W, o); break;
               default: q8_block<14>(W, o); break;
             }
-          } else if (WT == MB_GGML_BF16) {
+          } else if constexpr (WT == MB_GGML_BF16) {
             const uint4* src = (const uint4*)(R + r * 128 + hh * 64);
 #pragma unroll
             for (int i = 0; i < 4; i++) {
               const uint4 v = src[i];
               o[4 * i] = v.x; o[4 * i + 1] = v.y; o[4 * i + 2] = v.z; o[4 * i + 3] = v.w;
             }
-          } else if (WT == MB_GGML_Q6_K) {
+          } else if constexpr (WT == MB_GGML_Q6_K) {
             dq_unit_q6k(R + r * Cfg<WT>::kRawRow, 2 * j + hh, o);
-          } else if (WT == MB_GGML_Q5_K) {
+          } else if constexpr (WT == MB_GGML_Q5_K) {
             dq_unit_q5k(R + r * Cfg<WT>::kRawRow, 2 * j + hh, o);
-          } else if (WT == MB_GGML_Q4_1) {
+          } else if constexpr (WT == MB_GGML_Q4_1) {
             dq_unit_q41(R + r * Cfg<WT>::kRawRow, 2 * j + hh, o);
           } else {
             float y[32];
