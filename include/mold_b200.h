@@ -312,6 +312,23 @@ MB_API mb_status mb_qwen_denoise(mb_qwen* m, float* img, int64_t h_tokens, int64
                                  const uint8_t* txt_mask, int64_t L_txt, int batch, const double* sigmas, int n_sigmas,
                                  float guidance, void* stream);
 
+/* ------------------------------------------------------------------ GGUF files */
+
+/* List the tensors of a GGUF (v2/v3) file without touching a GPU: one line per tensor,
+ * "name<TAB>ggml type<TAB>dim ... (outermost first)", newline separated, into buf (truncated
+ * at buflen - 1). Replaces candle's gguf_file::Content::read as used at flux/pipeline.rs:285-296. */
+MB_API mb_status mb_gguf_inspect(const char* path, char* buf, size_t buflen, int64_t* n_tensors);
+
+/* Load every tensor of a FLUX GGUF file into m (names as in the file; tensors the model does
+ * not read are skipped). With embeddings_path, the embedding tensors the file lacks (img_in,
+ * time_in, vector_in, guidance_in — city96 fine-tune files) are taken from that FLUX GGUF
+ * (flux/pipeline.rs:254-330). The file is memory-mapped; each tensor is copied to the device
+ * once. Replaces VarBuilder::from_gguf (flux/pipeline.rs:976) for the transformer. */
+MB_API mb_status mb_flux_load_gguf(mb_flux* m, const char* path, const char* embeddings_path, int* n_loaded);
+
+/* Load every tensor of a Qwen-Image GGUF file into m (qwen_image/pipeline.rs:258-275). */
+MB_API mb_status mb_qwen_load_gguf(mb_qwen* m, const char* path, int* n_loaded);
+
 #ifdef __cplusplus
 }
 #endif

@@ -17,7 +17,7 @@ from ._lib import (  # noqa: F401
 )
 from .ops import (  # noqa: F401
     QTensor, QMatMul, init, dequantize, qlinear, qgemv, ln_modulate, rope_table, qk_norm_rope, attention,
-    euler_step, device_status, key_order, rms_norm, cfg_euler_step,
+    euler_step, device_status, key_order, rms_norm, cfg_euler_step, gguf_inspect,
 )
 from .flux import FluxConfig, FluxTransformer  # noqa: F401
 from .qwen import QwenConfig, QwenTransformer  # noqa: F401

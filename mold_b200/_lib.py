@@ -53,6 +53,9 @@ SIGNATURES = {
     "mb_qwen_missing": (I32, [P, P, SZ]),
     "mb_qwen_forward": (I32, [P, P, I64, I64, P, P, I64, I32, F32, P, P]),
     "mb_qwen_denoise": (I32, [P, P, I64, I64, P, P, I64, I32, P, I32, F32, P]),
+    "mb_gguf_inspect": (I32, [ctypes.c_char_p, P, SZ, P]),
+    "mb_flux_load_gguf": (I32, [P, ctypes.c_char_p, ctypes.c_char_p, P]),
+    "mb_qwen_load_gguf": (I32, [P, ctypes.c_char_p, P]),
 }
 
 

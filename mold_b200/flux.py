@@ -130,6 +130,15 @@ class FluxTransformer:
             self.set_tensor(name, qt)
         return self
 
+    def load_gguf(self, path, embeddings_path=None):
+        """Load a FLUX GGUF file (VarBuilder::from_gguf, flux/pipeline.rs:976); embeddings_path
+        supplies img_in / time_in / vector_in / guidance_in when the file lacks them (city96)."""
+        n = ctypes.c_int(0)
+        check(lib().mb_flux_load_gguf(self._h, str(path).encode(),
+                                      None if embeddings_path is None else str(embeddings_path).encode(),
+                                      ctypes.byref(n)))
+        return n.value
+
     def missing(self):
         buf = ctypes.create_string_buffer(1 << 16)
         check(lib().mb_flux_missing(self._h, buf, len(buf)))

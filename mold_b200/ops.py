@@ -232,3 +232,16 @@ def device_status():
     s = ctypes.c_int(0)
     check(lib().mb_device_status(ctypes.byref(s)))
     return s.value
+
+
+def gguf_inspect(path):
+    """[(name, ggml_type, shape outermost-first)] of a GGUF file's tensors (no GPU needed)."""
+    buf = ctypes.create_string_buffer(1 << 22)
+    n = ctypes.c_int64(0)
+    check(lib().mb_gguf_inspect(str(path).encode(), buf, len(buf), ctypes.byref(n)))
+    out = []
+    for line in buf.value.decode().split("\n"):
+        if line:
+            f = line.split("\t")
+            out.append((f[0], int(f[1]), tuple(int(x) for x in f[2:])))
+    return out

@@ -115,6 +115,12 @@ class QwenTransformer:
             self.set_tensor(name, qt)
         return self
 
+    def load_gguf(self, path):
+        """Load a Qwen-Image GGUF file (qwen_image/pipeline.rs:258-275)."""
+        n = ctypes.c_int(0)
+        check(lib().mb_qwen_load_gguf(self._h, str(path).encode(), ctypes.byref(n)))
+        return n.value
+
     def missing(self):
         buf = ctypes.create_string_buffer(1 << 16)
         check(lib().mb_qwen_missing(self._h, buf, len(buf)))
