@@ -105,6 +105,9 @@ MB_API mb_status mb_weight_create(int ggml_type, int64_t n_rows, int64_t n_cols,
 MB_API mb_status mb_weight_destroy(mb_weight* w);
 /* Raw device pointer of the weight bytes and their GGML type. */
 MB_API mb_status mb_weight_info(const mb_weight* w, int* ggml_type, int64_t* n_rows, int64_t* n_cols, const void** dev_ptr);
+/* Copy the weight's bytes back to host memory in GGUF layout (n_rows x GGUF row bytes; Q6_K's
+ * device padding removed). Synchronous. */
+MB_API mb_status mb_weight_download(const mb_weight* w, void* host, size_t nbytes);
 
 /* ------------------------------------------------------------------ kernels */
 
@@ -328,6 +331,26 @@ MB_API mb_status mb_flux_load_gguf(mb_flux* m, const char* path, const char* emb
 
 /* Load every tensor of a Qwen-Image GGUF file into m (qwen_image/pipeline.rs:258-275). */
 MB_API mb_status mb_qwen_load_gguf(mb_qwen* m, const char* path, int* n_loaded);
+
+/* ------------------------------------------------------------------ LoRA merge */
+
+/* Merge a LoRA delta into rows [row_offset, row_offset + rows) of a weight, in place and in the
+ * weight's own GGML type (flux/lora.rs:661-868, `gguf_lora_var_builder`: dequantize, add
+ * scale * (B A) to the row slice, re-quantize to the original type). A is device f32
+ * [rank, n_cols] (lora_A), B is device f32 [rows, rank] (lora_B); scale is the effective scale
+ * (user scale * alpha / rank when the adapter has an alpha). Per value
+ *   w' = quantize(w + fl(fl(sum_k B[r,k] A[k,c]) * scale)), the sum by fmaf in ascending k.
+ * Q8_0, Q4_0, Q4_1, Q5_0, Q5_1 and BF16 / F16 re-quantize with ggml's reference quantizers
+ * (idempotent on their own output, so rows outside the slice need no pass); Q4_K, Q5_K and
+ * Q6_K with one-pass quantizers of this library. Asynchronous on `stream`. */
+MB_API mb_status mb_weight_lora_merge(mb_weight* w, int64_t row_offset, int64_t rows, const float* A, const float* B,
+                                      int rank, float scale, void* stream);
+
+/* mb_weight_lora_merge on the FLUX model's tensor `name` (GGUF name, e.g.
+ * "double_blocks.0.img_attn.qkv.weight"). Allowed before or after the first forward: the model
+ * reads the merged bytes from then on (no forward may be running on another stream). */
+MB_API mb_status mb_flux_lora_merge(mb_flux* m, const char* name, int64_t row_offset, int64_t rows, const float* A,
+                                    const float* B, int rank, float scale, void* stream);
 
 #ifdef __cplusplus
 }

@@ -28,6 +28,7 @@ SIGNATURES = {
     "mb_weight_create": (I32, [I32, I64, I64, P, SZ, I32, P]),
     "mb_weight_destroy": (I32, [P]),
     "mb_weight_info": (I32, [P, P, P, P, P]),
+    "mb_weight_download": (I32, [P, P, SZ]),
     "mb_dequant": (I32, [P, P, I32, P]),
     "mb_qlinear": (I32, [P, P, I32, I64, I64, P, I32, I64, P, I32, I64, P, P, I64, P]),
     "mb_qgemv": (I32, [P, P, I32, P, P, P]),
@@ -56,6 +57,8 @@ SIGNATURES = {
     "mb_gguf_inspect": (I32, [ctypes.c_char_p, P, SZ, P]),
     "mb_flux_load_gguf": (I32, [P, ctypes.c_char_p, ctypes.c_char_p, P]),
     "mb_qwen_load_gguf": (I32, [P, ctypes.c_char_p, P]),
+    "mb_weight_lora_merge": (I32, [P, I64, I64, P, P, I32, F32, P]),
+    "mb_flux_lora_merge": (I32, [P, ctypes.c_char_p, I64, I64, P, P, I32, F32, P]),
 }
 
 

@@ -12,7 +12,7 @@ import sys
 HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 OUT = os.path.join(HERE, "libmold_b200.so")
-SOURCES = ["api.cu", "dequant.cu", "gemm.cu", "gemv.cu", "attention.cu", "elementwise.cu", "flux.cu", "noalloc.cu", "model_util.cu", "qwen.cu", "gguf.cu"]
+SOURCES = ["api.cu", "dequant.cu", "gemm.cu", "gemv.cu", "attention.cu", "elementwise.cu", "flux.cu", "noalloc.cu", "model_util.cu", "qwen.cu", "gguf.cu", "lora.cu"]
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC",
          "-Xcompiler", "-fvisibility=hidden", "--expt-relaxed-constexpr", "-ccbin", "/usr/bin/g++"]

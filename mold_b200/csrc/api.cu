@@ -249,6 +249,23 @@ mb_status mb_weight_info(const mb_weight* w, int* ggml_type, int64_t* n_rows, in
   return MB_OK;
 }
 
+mb_status mb_weight_download(const mb_weight* w, void* host, size_t nbytes) {
+  MB_CHECK(w && host, MB_ERR_INVALID, "weight or host buffer is NULL");
+  const int64_t rb = row_bytes_of(w->type, w->n_cols);
+  MB_CHECK(nbytes == (size_t)(rb * w->n_rows), MB_ERR_INVALID,
+           "host buffer holds " + std::to_string(nbytes) + " bytes, the weight " + std::to_string(rb * w->n_rows));
+  if (w->row_bytes == rb) {
+    MB_CUDA(cudaMemcpy(host, w->dev, nbytes, cudaMemcpyDeviceToHost));
+    return MB_OK;
+  }
+  // Q6_K: 224-byte device super-blocks back to GGUF's 210
+  std::vector<uint8_t> dev((size_t)(w->row_bytes * w->n_rows));
+  MB_CUDA(cudaMemcpy(dev.data(), w->dev, dev.size(), cudaMemcpyDeviceToHost));
+  const int64_t nsb = w->n_rows * (w->n_cols / 256);
+  for (int64_t i = 0; i < nsb; i++) memcpy((uint8_t*)host + i * 210, dev.data() + i * 224, 210);
+  return MB_OK;
+}
+
 mb_status mb_dequant(const mb_weight* w, void* out, int out_dtype, void* stream) {
   MB_CHECK(w && out, MB_ERR_INVALID, "weight or out is NULL");
   MB_CHECK(out_dtype == MB_DT_F32 || out_dtype == MB_DT_BF16, MB_ERR_INVALID, "out_dtype must be F32 or BF16");

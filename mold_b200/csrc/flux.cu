@@ -483,6 +483,14 @@ mb_status mb_flux_set_tensor(mb_flux* m, const char* name, int ggml_type, int64_
   return MB_OK;
 }
 
+mb_status mb_flux_lora_merge(mb_flux* m, const char* name, int64_t row_offset, int64_t rows, const float* A,
+                             const float* B, int rank, float scale, void* stream) {
+  MB_CHECK(m && name, MB_ERR_INVALID, "NULL argument");
+  auto it = m->mats.find(name);
+  MB_CHECK(it != m->mats.end(), MB_ERR_INVALID, std::string("no FLUX weight matrix '") + name + "' is loaded");
+  return mb_weight_lora_merge(it->second, row_offset, rows, A, B, rank, scale, stream);
+}
+
 mb_status mb_flux_missing(const mb_flux* m, char* buf, size_t buflen) {
   MB_CHECK(m && buf && buflen > 0, MB_ERR_INVALID, "NULL argument");
   std::string s;

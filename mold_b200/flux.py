@@ -12,7 +12,7 @@ from dataclasses import dataclass
 import torch
 
 from ._lib import FluxConfigC, check, lib
-from .ops import QTensor, _ptr, _stream, init
+from .ops import QTensor, _lora_operands, _ptr, _stream, init
 
 
 @dataclass
@@ -138,6 +138,13 @@ class FluxTransformer:
                                       None if embeddings_path is None else str(embeddings_path).encode(),
                                       ctypes.byref(n)))
         return n.value
+
+    def lora_merge(self, name, A, B, scale, row_offset=0):
+        """Merge scale * (B @ A) into rows [row_offset, row_offset + B.shape[0]) of tensor `name`
+        in its own GGML type (mb_flux_lora_merge). A [rank, in], B [rows, rank] (CUDA)."""
+        A, B = _lora_operands(A, B)
+        check(lib().mb_flux_lora_merge(self._h, name.encode(), int(row_offset), B.shape[0], _ptr(A), _ptr(B),
+                                       A.shape[0], float(scale), _stream()))
 
     def missing(self):
         buf = ctypes.create_string_buffer(1 << 16)

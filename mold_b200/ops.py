@@ -107,6 +107,29 @@ class QMatMul:
 
     __call__ = forward
 
+    def download(self):
+        """The weight's bytes in GGUF layout (host uint8 [n_rows * row bytes])."""
+        out = np.empty(self.n_rows * row_bytes(self.ggml_type, self.n_cols), dtype=np.uint8)
+        check(lib().mb_weight_download(self._h, out.ctypes.data_as(ctypes.c_void_p), out.size))
+        return out
+
+    def lora_merge(self, A, B, scale, row_offset=0):
+        """In place: rows [row_offset, row_offset + B.shape[0]) += scale * (B @ A), re-quantized to
+        the weight's own type (mb_weight_lora_merge). A [rank, n_cols], B [rows, rank] (CUDA)."""
+        A, B = _lora_operands(A, B)
+        check(lib().mb_weight_lora_merge(self._h, int(row_offset), B.shape[0], _ptr(A), _ptr(B), A.shape[0],
+                                         float(scale), _stream()))
+
+
+def _lora_operands(A, B):
+    A = A.contiguous().float()
+    B = B.contiguous().float()
+    if A.dim() != 2 or B.dim() != 2 or B.shape[1] != A.shape[0]:
+        raise ValueError(f"LoRA shapes A {tuple(A.shape)} and B {tuple(B.shape)} do not chain")
+    if not (A.is_cuda and B.is_cuda):
+        raise ValueError("LoRA A and B must be CUDA tensors")
+    return A, B
+
 
 def qlinear(w: QMatMul, x, bias=None, epilogue=EPI_NONE, gelu_from=0, gate=None, residual=None, out=None,
             out_dtype=None):

@@ -33,8 +33,9 @@
  *     one rounding of the exact result and does not depend on the evaluation order.
  *   - A Q8_0 quantizer equal to ggml's reference quantizer (amax/127, round half
  *     away from zero), pinned against gguf-py's Q8_0.quantize_blocks.
- *   - Simple quantizers of this project's own for Q4_0/Q4_1/Q5_0/Q5_1/Q5_K/Q6_K (any
- *     valid block exercises the same decode; only the decode must be bit-exact).
+ *   - ggml's reference quantizers for Q4_0/Q4_1/Q5_0/Q5_1 (pinned against gguf-py), and
+ *     quantizers of this project's own for Q5_K/Q6_K (any valid block exercises the same
+ *     decode; the decode is what must be bit-exact).
  *   - A Q4_K quantizer of this project's own (per-sub-block min/max, 6-bit
  *     scales relative to the super-block maxima). Any valid Q4_K block
  *     exercises the same decode; only the decode is required to be bit-exact.
@@ -43,6 +44,7 @@
  */
 #include <math.h>
 #include <stdint.h>
+#include <stdlib.h>
 #include <string.h>
 
 #define QK8_0 32
@@ -294,7 +296,14 @@ static void dequant_q5_01(const uint8_t* in, int64_t nb, float* out, int has_m) 
   }
 }
 
-/* per-block min/max (affine types) or signed absmax (symmetric types) quantizer */
+/* ggml's reference quantizers for the 32-value block types (quantize_row_q4_0_ref and
+ * siblings in ggml-quants.c; restated from gguf-py's bit-exact numpy port, gguf/quants.py
+ * Q4_0..Q5_1.quantize_blocks, which the tests pin this against):
+ *   symmetric (Q4_0 / Q5_0): max = the value of largest |x| (first one), d = max / -8 or -16,
+ *     id = 1 / d (0 if d == 0), q = min(qmax, trunc(x id + 8.5 or 16.5))
+ *   affine (Q4_1 / Q5_1): d = (max - min) / 15 or 31, id = 1 / d (0 if d == 0),
+ *     q = min(qmax, trunc((x - min) id + 0.5)); the block stores f16(d) and f16(min)
+ * q is computed with the unrounded f32 d. */
 void or_quantize_q4q5(const float* x, int64_t n, uint8_t* out, int bits, int has_m) {
   const int bytes = bits == 4 ? (has_m ? 20 : 18) : (has_m ? 24 : 22);
   const int qmax = (1 << bits) - 1;
@@ -303,29 +312,32 @@ void or_quantize_q4q5(const float* x, int64_t n, uint8_t* out, int bits, int has
   for (int64_t b = 0; b < nb; b++) {
     const float* xb = x + b * 32;
     uint8_t* ob = out + b * bytes;
-    float d, m = 0.f;
     int q[32];
     if (has_m) {
       float mn = INFINITY, mx = -INFINITY;
       for (int j = 0; j < 32; j++) { mn = fminf(mn, xb[j]); mx = fmaxf(mx, xb[j]); }
-      d = (mx - mn) / (float)qmax;
-      m = mn;
-      uint16_t dh = f2h(d), mh = f2h(m);
-      d = h2f(dh);
-      m = h2f(mh);
+      const float d = (mx - mn) / (float)qmax;
+      const float id = d != 0.f ? 1.0f / d : 0.f;
+      uint16_t dh = f2h(d), mh = f2h(mn);
       memcpy(ob, &dh, 2);
       memcpy(ob + 2, &mh, 2);
-      for (int j = 0; j < 32; j++) q[j] = d > 0.f ? clampi((int)lrintf((xb[j] - m) / d), 0, qmax) : 0;
+      for (int j = 0; j < 32; j++) {
+        const float v = (xb[j] - mn) * id;
+        q[j] = clampi((int)(v + 0.5f), 0, qmax);
+      }
     } else {
       float amax = 0.f, vmax = 0.f;
       for (int j = 0; j < 32; j++)
         if (fabsf(xb[j]) > amax) { amax = fabsf(xb[j]); vmax = xb[j]; }
       const int half = 1 << (bits - 1);
-      d = vmax / (float)(-half);
+      const float d = vmax / (float)(-half);
+      const float id = d != 0.f ? 1.0f / d : 0.f;
       uint16_t dh = f2h(d);
-      d = h2f(dh);
       memcpy(ob, &dh, 2);
-      for (int j = 0; j < 32; j++) q[j] = d != 0.f ? clampi((int)lrintf(xb[j] / d) + half, 0, qmax) : half;
+      for (int j = 0; j < 32; j++) {
+        const float v = xb[j] * id;
+        q[j] = clampi((int)(v + ((float)half + 0.5f)), 0, qmax);
+      }
     }
     uint8_t* qs = ob + (has_m ? 4 : 2);
     if (bits == 5) {
@@ -522,6 +534,66 @@ int or_dequantize(int ggml_type, const uint8_t* in, int64_t n, float* out) {
       return 0;
     default: return -2;
   }
+}
+
+/* ---------- LoRA merge (flux/lora.rs:651-868) ----------
+ * Rows [row0, row0 + nrows) of a weight (raw GGUF bytes, n_cols values per row) become
+ * quantize(dequant(w) + fl(fl(sum_k B[r,k] A[k,c]) * scale)), the dot product accumulated with
+ * fmaf in ascending k; other rows are copied. A is [rank, n_cols], B is [nrows, rank] (f32).
+ * The quantizers are the ones above (Q8_0: ggml's reference algorithm). */
+int or_lora_merge(int type, const uint8_t* raw, int64_t n_rows, int64_t n_cols, int64_t row0, int64_t nrows,
+                  const float* A, const float* B, int rank, float scale, uint8_t* out) {
+  int64_t rb;
+  switch (type) {
+    case 0: rb = n_cols * 4; break;
+    case 1: case 30: rb = n_cols * 2; break;
+    case 8: rb = n_cols / 32 * 34; break;
+    case 12: rb = n_cols / 256 * 144; break;
+    case 2: rb = n_cols / 32 * 18; break;
+    case 3: rb = n_cols / 32 * 20; break;
+    case 6: rb = n_cols / 32 * 22; break;
+    case 7: rb = n_cols / 32 * 24; break;
+    case 13: rb = n_cols / 256 * 176; break;
+    case 14: rb = n_cols / 256 * 210; break;
+    default: return -2;
+  }
+  if (row0 < 0 || nrows < 0 || row0 + nrows > n_rows) return -1;
+  memcpy(out, raw, (size_t)(n_rows * rb));
+#pragma omp parallel for schedule(static)
+  for (int64_t r = 0; r < nrows; r++) {
+    float* t = (float*)malloc((size_t)n_cols * sizeof(float));
+    or_dequantize(type, raw + (row0 + r) * rb, n_cols, t);
+    for (int64_t c = 0; c < n_cols; c++) {
+      float acc = 0.f;
+      for (int k = 0; k < rank; k++) acc = fmaf(B[r * rank + k], A[(int64_t)k * n_cols + c], acc);
+      volatile float d = acc * scale;
+      t[c] = t[c] + d;
+    }
+    uint8_t* o = out + (row0 + r) * rb;
+    switch (type) {
+      case 0: memcpy(o, t, (size_t)n_cols * 4); break;
+      case 1: or_f32_to_f16(t, n_cols, (uint16_t*)o); break;
+      case 30:
+        for (int64_t c = 0; c < n_cols; c++) {
+          float q;
+          or_round_bf16(&t[c], 1, &q);
+          uint32_t bits;
+          memcpy(&bits, &q, 4);
+          ((uint16_t*)o)[c] = (uint16_t)(bits >> 16);
+        }
+        break;
+      case 8: or_quantize_q8_0(t, n_cols, o); break;
+      case 12: or_quantize_q4_k(t, n_cols, o); break;
+      case 2: or_quantize_q4q5(t, n_cols, o, 4, 0); break;
+      case 3: or_quantize_q4q5(t, n_cols, o, 4, 1); break;
+      case 6: or_quantize_q4q5(t, n_cols, o, 5, 0); break;
+      case 7: or_quantize_q4q5(t, n_cols, o, 5, 1); break;
+      case 13: or_quantize_q5_k(t, n_cols, o); break;
+      case 14: or_quantize_q6_k(t, n_cols, o); break;
+    }
+    free(t);
+  }
+  return 0;
 }
 
 /* ---------- shared seeded generator ----------

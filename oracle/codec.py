@@ -31,6 +31,8 @@ def _load():
         _lib.or_quantize_q4q5.argtypes = [P, I64, P, ctypes.c_int, ctypes.c_int]
         _lib.or_quantize_q5_k.argtypes = [P, I64, P]
         _lib.or_quantize_q6_k.argtypes = [P, I64, P]
+        _lib.or_lora_merge.argtypes = [ctypes.c_int, P, I64, I64, I64, I64, P, P, ctypes.c_int, ctypes.c_float, P]
+        _lib.or_lora_merge.restype = ctypes.c_int
         _lib.or_randn.argtypes = [ctypes.c_uint64, I64, ctypes.c_float, P]
         _lib.or_round_bf16.argtypes = [P, I64, P]
     return _lib
@@ -105,3 +107,19 @@ def dequantize(raw, t, shape):
     if rc != 0:
         raise ValueError(f"dequantize failed rc={rc} type={t}")
     return out.reshape(shape)
+
+
+def lora_merge(raw, t, shape, row0, nrows, A, B, scale):
+    """Raw GGUF bytes of a [rows, cols] weight with rows [row0, row0 + nrows) replaced by
+    quantize(dequant + fl(fl(B @ A) * scale)) (dot products by fmaf in ascending k)."""
+    raw = np.ascontiguousarray(raw, dtype=np.uint8)
+    A = np.ascontiguousarray(A, dtype=np.float32)
+    B = np.ascontiguousarray(B, dtype=np.float32)
+    rows, cols = shape
+    assert A.shape == (B.shape[1], cols) and B.shape[0] == nrows
+    out = np.empty_like(raw)
+    rc = _load().or_lora_merge(t, raw.ctypes.data, rows, cols, row0, nrows, A.ctypes.data, B.ctypes.data, B.shape[1],
+                               float(scale), out.ctypes.data)
+    if rc != 0:
+        raise ValueError(f"lora_merge failed rc={rc}")
+    return out

@@ -17,6 +17,12 @@ Fixtures (codec_golden.npz):
   <t>_blocks / <t>_deq for t in q4_0, q4_1, q5_0, q5_1, q5_k, q6_k: 64 blocks of random bytes
                (finite, moderate f16 scale fields) + 16 blocks from the oracle's own quantizer,
                and gguf-py's dequantize_blocks of them
+  <t>_qin / <t>_qblocks for t in q4_0, q4_1, q5_0, q5_1: f32 [16, 256] seeded input (one zero
+               block) and gguf-py's quantize of it (ggml's reference quantizers)
+  lora_<t>_raw / lora_<t>_out for t in q8_0, q4_0, q4_1, q5_0, q5_1, bf16, with lora_A f32 [1, 256],
+               lora_B f32 [16, 1], lora_row0 = 8, lora_scale = 0.75: a [48, 256] weight quantized
+               by gguf-py, and the same bytes with rows [8, 24) replaced by gguf-py's quantize of
+               dequant(w) + fl(fl(B A) scale) (rank 1, so the delta has one rounding order)
 """
 import os
 import sys
@@ -61,6 +67,29 @@ def main():
         deq = quants.dequantize(blocks.reshape(-1), getattr(gguf.GGMLQuantizationType, name)).reshape(80, be)
         extra[name.lower() + "_blocks"] = blocks
         extra[name.lower() + "_deq"] = deq.astype(np.float32)
+
+    for tid, name in ((oracle.GGML_Q4_0, "Q4_0"), (oracle.GGML_Q4_1, "Q4_1"), (oracle.GGML_Q5_0, "Q5_0"),
+                      (oracle.GGML_Q5_1, "Q5_1")):
+        qin = oracle.randn(40 + tid, (16, 256), 0.05)
+        qin[3, 32:64] = 0.0
+        extra[name.lower() + "_qin"] = qin
+        extra[name.lower() + "_qblocks"] = quants.quantize(qin, getattr(gguf.GGMLQuantizationType, name))
+
+    lora_A = oracle.randn(60, (1, 256), 0.5)
+    lora_B = oracle.randn(61, (16, 1), 0.5)
+    row0, scale = 8, np.float32(0.75)
+    delta = ((lora_B * lora_A).astype(np.float32) * scale).astype(np.float32)
+    extra.update(lora_A=lora_A, lora_B=lora_B, lora_row0=np.int64(row0), lora_scale=scale)
+    w = oracle.randn(62, (48, 256), 0.05)
+    for name in ("Q8_0", "Q4_0", "Q4_1", "Q5_0", "Q5_1", "BF16"):
+        gt = getattr(gguf.GGMLQuantizationType, name)
+        raw = quants.quantize(w, gt)
+        deq = quants.dequantize(raw, gt).reshape(w.shape).astype(np.float32)
+        merged = (deq[row0:row0 + 16] + delta).astype(np.float32)
+        out_raw = raw.copy()
+        out_raw[row0:row0 + 16] = quants.quantize(merged, gt)
+        extra["lora_" + name.lower() + "_raw"] = raw
+        extra["lora_" + name.lower() + "_out"] = out_raw
 
     out = os.path.join(os.path.dirname(os.path.abspath(__file__)), "codec_golden.npz")
     np.savez_compressed(out, q8_in=q8_in, q8_blocks=q8_blocks, q8_deq=q8_deq,
