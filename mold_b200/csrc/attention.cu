@@ -9,14 +9,16 @@
 //   warp 1      MMA issuer. Per KV block j the tensor core runs, in order,
 //                 PV_0(j), S_0(j+1) = Q_0 K_{j+1}^T, PV_1(j), S_1(j+1)
 //               so while one tile's softmax works, the tensor core serves the other.
-//   warps 4-11  softmax of tile 0, warps 12-19 softmax of tile 1: two threads per query
-//               row (= TMEM lane), 64 key columns each, exchanging the row max through
-//               shared memory. Row max, exp2, row sum; P (bf16) of each half is written back into
-//               TMEM over the S columns it was computed from and consumed directly as the
-//               A operand of O += P V (O in TMEM). O is rescaled lazily, only when the row
-//               max grows by more than 2^8, which leaves the final O / l unchanged.
+//   warps 4-7   softmax of tile 0, warps 8-11 softmax of tile 1: one thread per query row
+//               (= TMEM lane) holding the row's 128 scores in registers. Row max, exp2, row sum;
+//               P (bf16) is written back into TMEM over the first 64 S columns and consumed
+//               directly as the A operand of O += P V (O in TMEM). O is rescaled lazily, only
+//               when the row max grows by more than 2^8, which leaves the final O / l unchanged.
 //               A fixed share of each row's exp2 is evaluated with a polynomial on the FMA
 //               pipe instead of the MUFU unit (which alone would cap the kernel).
+//               Two softmax warps per SM sub-partition (not four): every always-ready warp beside
+//               the MMA issuer on its sub-partition slows tcgen05.mma issue by ~25 cycles per
+//               instruction, and at 64 tensor cycles per 128x128x16 MMA the issuer has no slack.
 // TMEM (512 columns): S_0 [0,128), S_1 [128,256), O_0 [256,384), O_1 [384,512).
 // V is consumed in its natural [keys, d] layout as an MN-major B operand.
 #include "common.cuh"
@@ -26,10 +28,10 @@ namespace mb {
 namespace attn {
 
 constexpr int BQ = 128, BKV = 128, D = 128, NT = 2;
-constexpr int kThreads = 640;  // warp 0 TMA, warp 1 MMA, warps 4-11 softmax tile 0, 12-19 tile 1
+constexpr int kThreads = 384;  // warp 0 TMA, warp 1 MMA, warps 4-7 softmax tile 0, 8-11 tile 1
 constexpr uint32_t kTile = 128 * 128 * 2;  // 32 KB: one 128x128 bf16 tile (two 64-wide swizzle atoms)
 constexpr uint32_t kHalf = kTile / 2;      // 16 KB: one 64-wide atom column
-constexpr size_t kSmem = 1024 + 6 * (size_t)kTile + 256 + 6 * 1024;  // + row-max / row-sum exchange
+constexpr size_t kSmem = 1024 + 6 * (size_t)kTile + 256;
 constexpr float kScaleLog2 = 0.12751743082459868f;  // log2(e) / sqrt(128)
 constexpr float kRescaleThreshold = 8.f;
 #ifndef MB_ATTN_POLY
@@ -163,16 +165,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* s_full = bars + 7;    // [2] per tile
   uint64_t* p_full = bars + 9;    // [2] per tile
   uint64_t* o_full = bars + 11;   // [2] per tile
-  uint64_t* pair_bar = bars + 13;  // [8] per (tile, lane quarter): the two softmax warps of a row
-  uint32_t* tmem_slot = (uint32_t*)(bars + 21);
+  uint32_t* tmem_slot = (uint32_t*)(bars + 13);
   volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
-  float* xch = (float*)(smem + 6 * kTile + 256);  // [2 parity][2 tiles][128 rows][2 halves] maxima, then [2][128][2] sums
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int h = blockIdx.y, q0 = blockIdx.x * (NT * BQ);
   const int n_kv = p.n_kv;
 #ifdef MB_TRACE
-  unsigned long long tr_[9] = {0, 0, 0, 0, 0, 0, 0, 0, 0};
+  unsigned long long tr_[16] = {};
   const long long t_start_ = clock64();
 #endif
 
@@ -183,10 +183,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&v_full[i], 1);
       mbar_init(&kv_empty[i], 1);
       mbar_init(&s_full[i], 1);
-      mbar_init(&p_full[i], 8);
+      mbar_init(&p_full[i], 4);
       mbar_init(&o_full[i], 1);
     }
-    for (int i = 0; i < 8; i++) mbar_init(&pair_bar[i], 2);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -248,10 +247,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int kk = 0; kk < BKV / 16; kk++) {
           // V [keys, d]: MN-major; 64-wide d chunks kHalf apart (LBO), 8-key groups 1024 B apart (SBO).
           const uint64_t bdesc = sw128_desc(va + kk * 16 * 128, kHalf, 1024);
-          // P of keys 0..63 sits in S columns [0, 32), of keys 64..127 in [64, 96) (each softmax half
-          // writes P into its own S columns)
-          const uint32_t pcol = kk < 4 ? kk * 8 : 64 + (kk - 4) * 8;
-          umma_ts_a(tmem + 256 + t * 128, tmem + t * 128 + pcol, bdesc, idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
+          // P of keys 16kk .. 16kk+15 sits in S columns [8kk, 8kk + 8) (bf16 pairs)
+          umma_ts_a(tmem + 256 + t * 128, tmem + t * 128 + kk * 8, bdesc, idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
         }
       }
       __syncwarp();
@@ -291,97 +288,77 @@ __global__ void __launch_bounds__(kThreads, 1)
 #ifdef MB_TRACE
     tr_[7] = (unsigned long long)(clock64() - t_start_);
 #endif
-  } else if (warp >= 4) {
+  } else if (warp >= 4 && warp < 12) {
     // ---------------------------------------------------------------- softmax
-    // 8 warps per tile: the two warps of a lane quarter split each query row's 128 key columns
-    // (half 0: columns 0..63, half 1: 64..127). They share the row max of every KV block through
-    // shared memory (pair barrier), keep partial row sums, and each rescales / normalises its
-    // half of the row's 128 O columns.
-    const int t = (warp - 4) >> 3;
-    const int half = ((warp - 4) >> 2) & 1;
+    // 4 warps per tile; thread = query row = TMEM lane (warp w may only touch lanes 32 (w % 4) ..).
+    const int t = (warp - 4) >> 2;
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;
     const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
     const uint32_t tS = tmem + t * 128 + lane_addr, tO = tmem + 256 + t * 128 + lane_addr;
-    uint64_t* pbar = &pair_bar[t * 4 + quarter];
     float m_run = -INFINITY, l_run = 0.f;
     bool ok = true;
     for (int j = 0; j < n_kv; j++) {
       if (!(ok = AW(t ? 8 : 5, mbar_wait(&s_full[t], j & 1, abort_flag, p.status, kDevTimeoutAttn)))) break;
       tc_fence_after();
-      const int valid = p.n_valid - j * BKV - half * 64;  // keys >= valid are masked in this half
-      // pass 1: row max of this half (32 columns at a time; S is read again for the exponentials)
-      float mx = -INFINITY;
-#pragma unroll 1
-      for (int c = 0; c < 2; c++) {
-        uint32_t v[32];
-        if (AABL(1)) {
+      const int valid = p.n_valid - j * BKV;  // keys >= valid are masked
+#ifdef MB_TRACE
+      long long tph = clock64();
+#define APH(slot)                                  \
+  do {                                             \
+    const long long n__ = clock64();               \
+    if (t == 0) tr_[slot] += (unsigned long long)(n__ - tph); \
+    tph = n__;                                     \
+  } while (0)
+#else
+#define APH(slot) \
+  do {            \
+  } while (0)
+#endif
+      uint32_t v[4][32];
+      if (AABL(1)) {
 #pragma unroll
-          for (int i = 0; i < 32; i++) v[i] = __float_as_uint((float)(i + c));
-        } else {
-          tmem_ld32(tS + half * 64 + c * 32, v);
-          tmem_wait_ld();
-        }
-        if (valid < 64) {
+        for (int c = 0; c < 4; c++)
+#pragma unroll
+          for (int i = 0; i < 32; i++) v[c][i] = __float_as_uint((float)(i + c));
+      } else {
+#pragma unroll
+        for (int c = 0; c < 4; c++) tmem_ld32(tS + c * 32, v[c]);
+        tmem_wait_ld();
+      }
+      if (valid < BKV) {
+#pragma unroll
+        for (int c = 0; c < 4; c++)
 #pragma unroll
           for (int i = 0; i < 32; i++)
-            if (c * 32 + i >= valid) v[i] = __float_as_uint(-INFINITY);
-        }
-#pragma unroll
-        for (int i = 0; i < 32; i += 2) mx = max3(mx, __uint_as_float(v[i]), __uint_as_float(v[i + 1]));
+            if (c * 32 + i >= valid) v[c][i] = __float_as_uint(-INFINITY);
       }
-      // row max over both halves
-      float* xm = xch + ((j & 1) * 2 + t) * 256;
-      xm[r * 2 + half] = mx;
-      __syncwarp();
-      if (lane == 0) mbar_arrive(pbar);
-      if (!(ok = mbar_wait(pbar, j & 1, abort_flag, p.status, kDevTimeoutAttn))) break;
-      mx = fmaxf(mx, xm[r * 2 + (half ^ 1)]);
+      APH(11);
+      // row max: four independent max3 chains (one per 32-column chunk), then combined
+      float mc[4];
+#pragma unroll
+      for (int c = 0; c < 4; c++) {
+        mc[c] = fmaxf(__uint_as_float(v[c][0]), __uint_as_float(v[c][1]));
+#pragma unroll
+        for (int i = 2; i < 32; i += 2) mc[c] = max3(mc[c], __uint_as_float(v[c][i]), __uint_as_float(v[c][i + 1]));
+      }
+      const float mx = fmaxf(fmaxf(mc[0], mc[1]), fmaxf(mc[2], mc[3]));
+      APH(12);
       const float m_new = fmaxf(m_run, mx * kScaleLog2);
-      if (j == 0) {
-        m_run = m_new;
-      } else {
-        // S_t(j) complete implies PV_t(j-1) complete (same issuing thread, in order): O_t is stable.
-        const bool need = m_new > m_run + kRescaleThreshold;
-        if (__any_sync(0xffffffffu, need)) {
-          const float alpha = need ? ex2_approx(m_run - m_new) : 1.f;
-#pragma unroll 1
-          for (int c = 0; c < 2; c++) {
-            uint32_t o[32];
-            tmem_ld32(tO + half * 64 + c * 32, o);
-            tmem_wait_ld();
-#pragma unroll
-            for (int i = 0; i < 32; i++) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-            tmem_st32(tO + half * 64 + c * 32, o);
-          }
-          tmem_wait_st();
-          l_run *= alpha;
-          if (need) m_run = m_new;
-        }
-      }
+      // lazy rescale: only rows whose max grew by more than 2^8 move their reference point
+      const bool need = j == 0 || m_new > m_run + kRescaleThreshold;
+      const float alpha = (need && j > 0) ? ex2_approx(m_run - m_new) : 1.f;
+      if (need) m_run = m_new;
       const uint64_t sc2 = pk2(kScaleLog2, kScaleLog2), nm2 = pk2(-m_run, -m_run);
       uint64_t sum2 = pk2(0.f, 0.f);
-      // pass 2: exponentials, 32 columns at a time; P chunk c (16 words) lands over S columns
-      // [32h + 16c, 32h + 16c + 16), which belong to chunk c of this half that is already read
-#pragma unroll 1
-      for (int c = 0; c < 2; c++) {
-        uint32_t v[32];
-        if (AABL(1)) {
+      // exponentials, 32 keys at a time; P of keys 32c .. 32c+31 (16 bf16 pairs) goes to S columns
+      // [16c, 16c + 16), all of which were read above
 #pragma unroll
-          for (int i = 0; i < 32; i++) v[i] = __float_as_uint((float)(i - c));
-        } else {
-          tmem_ld32(tS + half * 64 + c * 32, v);
-          tmem_wait_ld();
-        }
-        if (valid < 64) {
-#pragma unroll
-          for (int i = 0; i < 32; i++)
-            if (c * 32 + i >= valid) v[i] = __float_as_uint(-INFINITY);
-        }
+      for (int c = 0; c < 4; c++) {
         uint32_t pk[16];
 #pragma unroll
         for (int i = 0; i < 16; i++) {
-          const uint64_t x2 = fma2(pk2(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1])), sc2, nm2);
+          const uint64_t x2 = fma2(pk2(__uint_as_float(v[c][2 * i]), __uint_as_float(v[c][2 * i + 1])), sc2, nm2);
           float e0, e1;
           if (AABL(4)) {
             up2(x2, e0, e1);
@@ -396,39 +373,41 @@ __global__ void __launch_bounds__(kThreads, 1)
           sum2 = add2(sum2, pk2(e0, e1));
           pk[i] = pack_bf16x2(e0, e1);
         }
-        // P words 16c .. 16c+15 of this half (keys 64h + 32c ..) go to S columns 64h + 16c ..,
-        // which this thread has already read (chunk 0 covers columns 64h .. 64h+31)
-        if (!AABL(2)) tmem_st16a(tS + half * 64 + c * 16, pk);
+        if (!AABL(2)) tmem_st16a(tS + c * 16, pk);
       }
+      APH(13);
       float sa, sb;
       up2(sum2, sa, sb);
-      const float sum = sa + sb;
+      if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+        // S_t(j) complete implies PV_t(j-1) complete (same issuing thread, in order): O_t is stable.
+#pragma unroll 1
+        for (int c = 0; c < 4; c++) {
+          uint32_t o[32];
+          tmem_ld32(tO + c * 32, o);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; i++) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+          tmem_st32(tO + c * 32, o);
+        }
+      }
       tmem_wait_st();
-      l_run += sum;
+      l_run = l_run * alpha + (sa + sb);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_full[t]);
-    }
-    // row sum over both halves (pair barrier phase n_kv)
-    if (ok) {
-      float* xs = xch + 4 * 256 + t * 256;
-      xs[r * 2 + half] = l_run;
-      __syncwarp();
-      if (lane == 0) mbar_arrive(pbar);
-      ok = mbar_wait(pbar, n_kv & 1, abort_flag, p.status, kDevTimeoutAttn);
-      if (ok) l_run += xs[r * 2 + (half ^ 1)];
+      APH(14);
     }
     if (ok) ok = mbar_wait(&o_full[t], 0, abort_flag, p.status, kDevTimeoutAttn);
     if (ok) {
       tc_fence_after();
       const int qrow = q0 + t * BQ + r;
       const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
-      __nv_bfloat16* orow = (qrow < p.split ? p.out + (int64_t)qrow * p.ldo : p.out2 + (int64_t)(qrow - p.split) * p.ldo) +
-                            (int64_t)h * D + half * 64;
+      __nv_bfloat16* orow =
+          (qrow < p.split ? p.out + (int64_t)qrow * p.ldo : p.out2 + (int64_t)(qrow - p.split) * p.ldo) + (int64_t)h * D;
 #pragma unroll 1
-      for (int c = 0; c < 2; c++) {
+      for (int c = 0; c < 4; c++) {
         uint32_t o[32];
-        tmem_ld32(tO + half * 64 + c * 32, o);
+        tmem_ld32(tO + c * 32, o);
         tmem_wait_ld();
         if (qrow < p.Lq) {
 #pragma unroll
@@ -449,8 +428,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 
 #ifdef MB_TRACE
-  if (p.trace && lane == 0 && (warp <= 1 || warp == 4 || warp == 12))
-    for (int i = 0; i < 9; i++)
+  if (p.trace && lane == 0 && (warp <= 1 || warp == 4 || warp == 8))
+    for (int i = 0; i < 16; i++)
       if (tr_[i]) atomicAdd(p.trace + i, tr_[i]);
 #endif
   tc_fence_before();
