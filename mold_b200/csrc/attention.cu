@@ -6,12 +6,13 @@
 //
 // One CTA = 256 query rows (two 128-row tiles) of one head, sharing every K/V block.
 //   warp 0      TMA: both Q tiles once, then K_j and V_j (128 keys) into a 2-deep ring.
-//   warp 1      MMA issuer. Per KV block j the tensor core runs, in order,
-//                 PV_0(j), S_0(j+1) = Q_0 K_{j+1}^T, PV_1(j), S_1(j+1)
-//               so while one tile's softmax works, the tensor core serves the other.
+//   warps 1, 2  MMA issuers of tile 0 and tile 1. Each KV block is processed as two 64-key
+//               sub-blocks whose scores go to the two halves of the tile's S columns, so the
+//               tensor core computes S(g + 1) while the softmax works on S(g): per tile, per
+//               sub-block g, PV_t(g) then S_t(g + 2).
 //   warps 4-7   softmax of tile 0, warps 8-11 softmax of tile 1: one thread per query row
-//               (= TMEM lane) holding the row's 128 scores in registers. Row max, exp2, row sum;
-//               P (bf16) is written back into TMEM over the first 64 S columns and consumed
+//               (= TMEM lane) holding the sub-block's 64 scores in registers. Row max, exp2, row
+//               sum; P (bf16) is written back into TMEM over the first 32 columns of the S half and consumed
 //               directly as the A operand of O += P V (O in TMEM). O is rescaled lazily, only
 //               when the row max grows by more than 2^8, which leaves the final O / l unchanged.
 //               A fixed share of each row's exp2 is evaluated with a polynomial on the FMA
@@ -19,7 +20,7 @@
 //               Two softmax warps per SM sub-partition (not four): every always-ready warp beside
 //               the MMA issuer on its sub-partition slows tcgen05.mma issue by ~25 cycles per
 //               instruction, and at 64 tensor cycles per 128x128x16 MMA the issuer has no slack.
-// TMEM (512 columns): S_0 [0,128), S_1 [128,256), O_0 [256,384), O_1 [384,512).
+// TMEM (512 columns): S_0 [0,128) (halves of 64), S_1 [128,256), O_0 [256,384), O_1 [384,512).
 // V is consumed in its natural [keys, d] layout as an MN-major B operand.
 #include "common.cuh"
 #include "internal.h"
@@ -35,7 +36,7 @@ constexpr size_t kSmem = 1024 + 6 * (size_t)kTile + 256;
 constexpr float kScaleLog2 = 0.12751743082459868f;  // log2(e) / sqrt(128)
 constexpr float kRescaleThreshold = 8.f;
 #ifndef MB_ATTN_POLY
-#define MB_ATTN_POLY 6
+#define MB_ATTN_POLY 0
 #endif
 constexpr int kPolyPerChunk = MB_ATTN_POLY;  // of every 32 exponentials, this many use the FMA-pipe polynomial
 
@@ -162,10 +163,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* k_full = bars + 1;    // [2] per stage
   uint64_t* v_full = bars + 3;    // [2]
   uint64_t* kv_empty = bars + 5;  // [2]
-  uint64_t* s_full = bars + 7;    // [2] per tile
-  uint64_t* p_full = bars + 9;    // [2] per tile
-  uint64_t* o_full = bars + 11;   // [2] per tile
-  uint32_t* tmem_slot = (uint32_t*)(bars + 13);
+  uint64_t* s_full = bars + 7;    // [tile][half]
+  uint64_t* p_full = bars + 11;   // [tile][half]
+  uint64_t* o_full = bars + 15;   // [tile]
+  uint64_t* pv_done = bars + 17;  // [tile]: one completion per P V sub-block
+  uint32_t* tmem_slot = (uint32_t*)(bars + 19);
   volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -181,10 +183,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int i = 0; i < 2; i++) {
       mbar_init(&k_full[i], 1);
       mbar_init(&v_full[i], 1);
-      mbar_init(&kv_empty[i], 1);
+      mbar_init(&kv_empty[i], 2);  // one commit per MMA issuer
+      mbar_init(&o_full[i], 1);
+      mbar_init(&pv_done[i], 1);
+    }
+    for (int i = 0; i < 4; i++) {
       mbar_init(&s_full[i], 1);
       mbar_init(&p_full[i], 4);
-      mbar_init(&o_full[i], 1);
     }
     *abort_flag = 0;
     fence_mbar_init();
@@ -220,70 +225,82 @@ __global__ void __launch_bounds__(kThreads, 1)
         tma_load_3d(sV + s * kTile + kHalf, &tv, &v_full[s], 64, j * BKV, h);
       }
     }
-  } else if (warp == 1) {
-    constexpr uint32_t idesc_s = idesc_bf16(BQ, BKV, false);
+  } else if (warp == 1 || warp == 2) {
+    // MMA issuer of tile t = warp - 1 (the two issuers sit on different SM sub-partitions).
+    // Sub-block g = 2j + hh covers keys 64hh .. 64hh+63 of K/V stage j; its scores go to the
+    // tile's S half hh, so S_t(g + 2) is issued while the softmax works on S_t(g + 1).
+    const int t = warp - 1;
+    constexpr uint32_t idesc_s = idesc_bf16(BQ, 64, false);
     constexpr uint32_t idesc_o = idesc_bf16(BQ, D, true);
-    const uint32_t qa = smem_u32(sQ);
+    const uint32_t qa = smem_u32(sQ) + t * kTile;
+    const int n_sub = 2 * n_kv;
     bool ok = mbar_wait(q_full, 0, abort_flag, p.status, kDevTimeoutAttn);
-    // S_t = Q_t K_j^T into the tile's S columns
-    auto issue_s = [&](int t, int j) {
+    // S_t(g) = Q_t K_g^T (64 keys) into S half g & 1
+    auto issue_s = [&](int g) {
+#ifdef MB_TRACE
+      const long long ti0 = clock64();
+#endif
+      const int hh = g & 1;
       if (lane == 0) {
-        const uint32_t ka = smem_u32(sK + (j & 1) * kTile);
+        const uint32_t ka = smem_u32(sK + ((g >> 1) & 1) * kTile) + hh * 8192;
 #pragma unroll
         for (int kk = 0; kk < D / 16; kk++) {
           const uint32_t off = (kk >> 2) * kHalf + (kk & 3) * 32;
-          umma_f16(tmem + t * 128, sw128_desc(qa + t * kTile + off, 16, 1024), sw128_desc(ka + off, 16, 1024),
-                   idesc_s, kk > 0);
+          umma_f16(tmem + t * 128 + hh * 64, sw128_desc(qa + off, 16, 1024), sw128_desc(ka + off, 16, 1024), idesc_s,
+                   kk > 0);
         }
-        umma_commit(&s_full[t]);
+        umma_commit(&s_full[t * 2 + hh]);
       }
       __syncwarp();
+#ifdef MB_TRACE
+      if (t == 0) tr_[9] += (unsigned long long)(clock64() - ti0);
+#endif
     };
-    // O_t += P_t V_j with P_t read from TMEM (bf16 pairs over the S columns)
-    auto issue_pv = [&](int t, int j) {
+    // O_t += P_t(g) V_g with P read from TMEM (bf16 pairs over the first 32 columns of S half g & 1)
+    auto issue_pv = [&](int g) {
+#ifdef MB_TRACE
+      const long long ti0 = clock64();
+#endif
+      const int hh = g & 1;
       if (lane == 0) {
-        const uint32_t va = smem_u32(sV + (j & 1) * kTile);
+        const uint32_t va = smem_u32(sV + ((g >> 1) & 1) * kTile);
 #pragma unroll
-        for (int kk = 0; kk < BKV / 16; kk++) {
+        for (int kk = 0; kk < 4; kk++) {
           // V [keys, d]: MN-major; 64-wide d chunks kHalf apart (LBO), 8-key groups 1024 B apart (SBO).
-          const uint64_t bdesc = sw128_desc(va + kk * 16 * 128, kHalf, 1024);
-          // P of keys 16kk .. 16kk+15 sits in S columns [8kk, 8kk + 8) (bf16 pairs)
-          umma_ts_a(tmem + 256 + t * 128, tmem + t * 128 + kk * 8, bdesc, idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
+          const uint64_t bdesc = sw128_desc(va + (hh * 4 + kk) * 16 * 128, kHalf, 1024);
+          umma_ts_a(tmem + 256 + t * 128, tmem + t * 128 + hh * 64 + kk * 8, bdesc, idesc_o, (g > 0 || kk > 0) ? 1u : 0u);
         }
+        umma_commit(&pv_done[t]);
+        if (hh == 1) umma_commit(&kv_empty[(g >> 1) & 1]);
       }
       __syncwarp();
+#ifdef MB_TRACE
+      if (t == 0) tr_[10] += (unsigned long long)(clock64() - ti0);
+#endif
     };
     if (ok && n_kv > 0) {
       if ((ok = mbar_wait(&k_full[0], 0, abort_flag, p.status, kDevTimeoutAttn))) {
         tc_fence_after();
-        issue_s(0, 0);
-        issue_s(1, 0);
+        issue_s(0);
+        issue_s(1);
       }
     }
-    for (int j = 0; j < n_kv && ok; j++) {
-      const uint32_t ph = (j >> 1) & 1;
-      if (!(ok = AW(1, mbar_wait(&v_full[j & 1], ph, abort_flag, p.status, kDevTimeoutAttn)))) break;
-      const bool more = j + 1 < n_kv;
-      if (!(ok = AW(2, mbar_wait(&p_full[0], j & 1, abort_flag, p.status, kDevTimeoutAttn)))) break;
+    for (int g = 0; g < n_sub && ok; g++) {
+      const int hh = g & 1, j = g >> 1;
+      if (hh == 0 && !(ok = AW(1, mbar_wait(&v_full[j & 1], (j >> 1) & 1, abort_flag, p.status, kDevTimeoutAttn))))
+        break;
+      if (!(ok = AW(2, mbar_wait(&p_full[t * 2 + hh], j & 1, abort_flag, p.status, kDevTimeoutAttn)))) break;
       tc_fence_after();
-      issue_pv(0, j);
-      if (more) {
-        if (!(ok = AW(3, mbar_wait(&k_full[(j + 1) & 1], ((j + 1) >> 1) & 1, abort_flag, p.status, kDevTimeoutAttn))))
+      issue_pv(g);
+      if (g + 2 < n_sub) {
+        if (hh == 0 &&
+            !(ok = AW(3, mbar_wait(&k_full[(j + 1) & 1], ((j + 1) >> 1) & 1, abort_flag, p.status, kDevTimeoutAttn))))
           break;
         tc_fence_after();
-        issue_s(0, j + 1);
+        issue_s(g + 2);
       }
-      if (!(ok = AW(4, mbar_wait(&p_full[1], j & 1, abort_flag, p.status, kDevTimeoutAttn)))) break;
-      tc_fence_after();
-      issue_pv(1, j);
-      if (lane == 0) umma_commit(&kv_empty[j & 1]);
-      __syncwarp();
-      if (more) issue_s(1, j + 1);
     }
-    if (ok && lane == 0) {
-      umma_commit(&o_full[0]);
-      umma_commit(&o_full[1]);
-    }
+    if (ok && lane == 0) umma_commit(&o_full[t]);
     __syncwarp();
 #ifdef MB_TRACE
     tr_[7] = (unsigned long long)(clock64() - t_start_);
@@ -298,10 +315,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t tS = tmem + t * 128 + lane_addr, tO = tmem + 256 + t * 128 + lane_addr;
     float m_run = -INFINITY, l_run = 0.f;
     bool ok = true;
-    for (int j = 0; j < n_kv; j++) {
-      if (!(ok = AW(t ? 8 : 5, mbar_wait(&s_full[t], j & 1, abort_flag, p.status, kDevTimeoutAttn)))) break;
+    for (int g = 0; g < 2 * n_kv; g++) {
+      const int hh = g & 1;
+      if (!(ok = AW(t ? 8 : 5, mbar_wait(&s_full[t * 2 + hh], (g >> 1) & 1, abort_flag, p.status, kDevTimeoutAttn))))
+        break;
       tc_fence_after();
-      const int valid = p.n_valid - j * BKV;  // keys >= valid are masked
+      const uint32_t tSh = tS + hh * 64;
+      const int valid = p.n_valid - g * 64;  // keys >= valid are masked
 #ifdef MB_TRACE
       long long tph = clock64();
 #define APH(slot)                                  \
@@ -315,46 +335,46 @@ __global__ void __launch_bounds__(kThreads, 1)
   do {            \
   } while (0)
 #endif
-      uint32_t v[4][32];
+      uint32_t v[2][32];
       if (AABL(1)) {
 #pragma unroll
-        for (int c = 0; c < 4; c++)
+        for (int c = 0; c < 2; c++)
 #pragma unroll
           for (int i = 0; i < 32; i++) v[c][i] = __float_as_uint((float)(i + c));
       } else {
-#pragma unroll
-        for (int c = 0; c < 4; c++) tmem_ld32(tS + c * 32, v[c]);
+        tmem_ld32(tSh, v[0]);
+        tmem_ld32(tSh + 32, v[1]);
         tmem_wait_ld();
       }
-      if (valid < BKV) {
+      if (valid < 64) {
 #pragma unroll
-        for (int c = 0; c < 4; c++)
+        for (int c = 0; c < 2; c++)
 #pragma unroll
           for (int i = 0; i < 32; i++)
             if (c * 32 + i >= valid) v[c][i] = __float_as_uint(-INFINITY);
       }
       APH(11);
-      // row max: four independent max3 chains (one per 32-column chunk), then combined
-      float mc[4];
+      // row max of the 64 keys: two independent max3 chains
+      float mc[2];
 #pragma unroll
-      for (int c = 0; c < 4; c++) {
+      for (int c = 0; c < 2; c++) {
         mc[c] = fmaxf(__uint_as_float(v[c][0]), __uint_as_float(v[c][1]));
 #pragma unroll
         for (int i = 2; i < 32; i += 2) mc[c] = max3(mc[c], __uint_as_float(v[c][i]), __uint_as_float(v[c][i + 1]));
       }
-      const float mx = fmaxf(fmaxf(mc[0], mc[1]), fmaxf(mc[2], mc[3]));
+      const float mx = fmaxf(mc[0], mc[1]);
       APH(12);
       const float m_new = fmaxf(m_run, mx * kScaleLog2);
       // lazy rescale: only rows whose max grew by more than 2^8 move their reference point
-      const bool need = j == 0 || m_new > m_run + kRescaleThreshold;
-      const float alpha = (need && j > 0) ? ex2_approx(m_run - m_new) : 1.f;
+      const bool need = g == 0 || m_new > m_run + kRescaleThreshold;
+      const float alpha = (need && g > 0) ? ex2_approx(m_run - m_new) : 1.f;
       if (need) m_run = m_new;
       const uint64_t sc2 = pk2(kScaleLog2, kScaleLog2), nm2 = pk2(-m_run, -m_run);
       uint64_t sum2 = pk2(0.f, 0.f);
-      // exponentials, 32 keys at a time; P of keys 32c .. 32c+31 (16 bf16 pairs) goes to S columns
-      // [16c, 16c + 16), all of which were read above
+      // exponentials, 32 keys at a time; P of keys 32c .. 32c+31 (16 bf16 pairs) goes to columns
+      // [16c, 16c + 16) of the S half, all of which were read above
 #pragma unroll
-      for (int c = 0; c < 4; c++) {
+      for (int c = 0; c < 2; c++) {
         uint32_t pk[16];
 #pragma unroll
         for (int i = 0; i < 16; i++) {
@@ -373,13 +393,16 @@ __global__ void __launch_bounds__(kThreads, 1)
           sum2 = add2(sum2, pk2(e0, e1));
           pk[i] = pack_bf16x2(e0, e1);
         }
-        if (!AABL(2)) tmem_st16a(tS + c * 16, pk);
+        if (!AABL(2)) tmem_st16a(tSh + c * 16, pk);
       }
       APH(13);
       float sa, sb;
       up2(sum2, sa, sb);
-      if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
-        // S_t(j) complete implies PV_t(j-1) complete (same issuing thread, in order): O_t is stable.
+      if (g > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+        // O_t must hold P V of sub-block g - 1 before it is rescaled (S_t(g) was issued before
+        // that P V, so its completion does not imply it)
+        if (!(ok = mbar_wait(&pv_done[t], (g - 1) & 1, abort_flag, p.status, kDevTimeoutAttn))) break;
+        tc_fence_after();
 #pragma unroll 1
         for (int c = 0; c < 4; c++) {
           uint32_t o[32];
@@ -394,7 +417,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       l_run = l_run * alpha + (sa + sb);
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&p_full[t]);
+      if (lane == 0) mbar_arrive(&p_full[t * 2 + hh]);
       APH(14);
     }
     if (ok) ok = mbar_wait(&o_full[t], 0, abort_flag, p.status, kDevTimeoutAttn);
