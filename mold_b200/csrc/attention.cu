@@ -122,14 +122,22 @@ MB_DEV void tmem_st16a(uint32_t taddr, const uint32_t (&r)[16]) {
       : "memory");
 }
 
-// D(tmem) (+)= A(tmem) * B(smem desc)^T
-MB_DEV void umma_ts_a(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+// Elected-lane forms for a converged warp (lane 0 issues): cheaper to issue than a lane-0 branch.
+MB_DEV void umma_ss_elect(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
   asm volatile(
-      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(
-          d_tmem),
+      "{\n .reg .pred p, e;\n .reg .b32 r;\n setp.ne.b32 p, %4, 0;\n elect.sync r|e, 0xffffffff;\n"
+      " @e tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+MB_DEV void umma_ts_elect(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p, e;\n .reg .b32 r;\n setp.ne.b32 p, %4, 0;\n elect.sync r|e, 0xffffffff;\n"
+      " @e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(d_tmem),
       "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
+
 
 #ifdef MB_TRACE
 #define AABL(bit) ((p.ablate & (bit)) != 0)
@@ -241,15 +249,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       const long long ti0 = clock64();
 #endif
       const int hh = g & 1;
-      if (lane == 0) {
+      {
         const uint32_t ka = smem_u32(sK + ((g >> 1) & 1) * kTile) + hh * 8192;
 #pragma unroll
         for (int kk = 0; kk < D / 16; kk++) {
           const uint32_t off = (kk >> 2) * kHalf + (kk & 3) * 32;
-          umma_f16(tmem + t * 128 + hh * 64, sw128_desc(qa + off, 16, 1024), sw128_desc(ka + off, 16, 1024), idesc_s,
-                   kk > 0);
+          umma_ss_elect(tmem + t * 128 + hh * 64, sw128_desc(qa + off, 16, 1024), sw128_desc(ka + off, 16, 1024),
+                        idesc_s, kk > 0);
         }
-        umma_commit(&s_full[t * 2 + hh]);
+        if (lane == 0) umma_commit(&s_full[t * 2 + hh]);
       }
       __syncwarp();
 #ifdef MB_TRACE
@@ -262,16 +270,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       const long long ti0 = clock64();
 #endif
       const int hh = g & 1;
-      if (lane == 0) {
+      {
         const uint32_t va = smem_u32(sV + ((g >> 1) & 1) * kTile);
 #pragma unroll
         for (int kk = 0; kk < 4; kk++) {
           // V [keys, d]: MN-major; 64-wide d chunks kHalf apart (LBO), 8-key groups 1024 B apart (SBO).
           const uint64_t bdesc = sw128_desc(va + (hh * 4 + kk) * 16 * 128, kHalf, 1024);
-          umma_ts_a(tmem + 256 + t * 128, tmem + t * 128 + hh * 64 + kk * 8, bdesc, idesc_o, (g > 0 || kk > 0) ? 1u : 0u);
+          umma_ts_elect(tmem + 256 + t * 128, tmem + t * 128 + hh * 64 + kk * 8, bdesc, idesc_o,
+                        (g > 0 || kk > 0) ? 1u : 0u);
         }
-        umma_commit(&pv_done[t]);
-        if (hh == 1) umma_commit(&kv_empty[(g >> 1) & 1]);
+        if (lane == 0) {
+          umma_commit(&pv_done[t]);
+          if (hh == 1) umma_commit(&kv_empty[(g >> 1) & 1]);
+        }
       }
       __syncwarp();
 #ifdef MB_TRACE

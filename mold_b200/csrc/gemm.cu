@@ -285,6 +285,14 @@ MB_DEV void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
 }
 
 // D(tmem) (+)= A(tmem) * B(smem desc)^T
+// The same, executed by a whole converged warp: the elected lane (lane 0) issues it.
+MB_DEV void umma_ts_elect(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p, e;\n .reg .b32 r;\n setp.ne.b32 p, %4, 0;\n elect.sync r|e, 0xffffffff;\n"
+      " @e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
 MB_DEV void umma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
   asm volatile(
       "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(
@@ -416,16 +424,25 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t sx = it % SX, px = (it / SX) & 1, sa = sx;
         if (!(ok = TW(3, mbar_wait(&full[sx], px, abort_flag, p.status, kDevTimeoutGemm)))) break;
         tc_fence_after();
-        if (lane == 0) {
+#ifdef MB_TRACE
+        const long long ti0 = clock64();
+#endif
+        {
+          // The whole (converged) warp runs the issue loop and lane 0 issues each MMA
+          // (elect.sync): measured 8-12 % faster than a lane-0-only branch, whose issue
+          // of 4 MMAs took ~537 cycles per 512-cycle stage.
           const uint32_t xaddr = smem_u32(xs + sx * kXStageBytes);
 #pragma unroll
           for (int kk = 0; kk < BK / 16; kk++) {
             const uint64_t bdesc = sw128_desc(xaddr + kk * 32, 16, 1024);
-            umma_ts(tmem, tmem + kTmemA + sa * 32 + kk * 8, bdesc, idesc, (ks | kk) != 0);
+            umma_ts_elect(tmem, tmem + kTmemA + sa * 32 + kk * 8, bdesc, idesc, (ks | kk) != 0);
           }
-          umma_commit(&empty[sx]);
+          if (lane == 0) umma_commit(&empty[sx]);
         }
         __syncwarp();
+#ifdef MB_TRACE
+        tr_[11] += (unsigned long long)(clock64() - ti0);
+#endif
       }
       if (!ok) break;
       if (lane == 0) umma_commit(acc_full);
