@@ -101,7 +101,9 @@ struct Params {
 #define ABL(bit) ((p.ablate & (bit)) != 0)
 // Cycles lane 0 of a role spends in a wait, accumulated in tr_[slot] and summed over CTAs at
 // exit. Slots: 0 TMA empty, 1 TMA r_empty, 2 MMA acc_empty, 3 MMA full, 4 epilogue drain,
-// 5 decode r_full, 6 decode empty, 7 epilogue acc_full, 8 MMA role total.
+// 5 decode r_full, 6 decode empty, 7 epilogue acc_full, 8 MMA role total, 9/10 drain phases,
+// 11 MMA issue, 12/13 MMA full waits in the first 4 / later stages of a tile, 14/15 decode
+// compute / TMEM store + arrive of one decoder warp.
 #define TW(slot, call)                          \
   ([&]() {                                      \
     const long long t0__ = clock64();           \
@@ -324,7 +326,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_tiles = p.n_tiles;
 #ifdef MB_TRACE
-  unsigned long long tr_[12] = {0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0};
+  unsigned long long tr_[16] = {};
   const long long t_start_ = clock64();
 #endif
   // problem of a global tile index and the tile's origin within it
@@ -422,7 +424,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       for (int ks = 0; ks < nks; ks++, it++) {
         const uint32_t sx = it % SX, px = (it / SX) & 1, sa = sx;
-        if (!(ok = TW(3, mbar_wait(&full[sx], px, abort_flag, p.status, kDevTimeoutGemm)))) break;
+        if (!(ok = TW(ks < 4 ? 12 : 13, mbar_wait(&full[sx], px, abort_flag, p.status, kDevTimeoutGemm)))) break;
         tc_fence_after();
 #ifdef MB_TRACE
         const long long ti0 = clock64();
@@ -484,6 +486,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int j = 0; j < kSPC; j++, it++) {
           const int ks = kc * kSPC + j;
           const uint32_t sa = it % SX, pa = (it / SX) & 1;
+#ifdef MB_TRACE
+          const long long td0 = clock64();
+#endif
           uint32_t o[16];
           if (ABL(1)) {
 #pragma unroll
@@ -541,7 +546,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             __syncwarp();
             if (lane == 0) mbar_arrive(&r_empty[sr]);
           }
+#ifdef MB_TRACE
+          tr_[14] += (unsigned long long)(clock64() - td0);
+#endif
           if (!(ok = TW(6, mbar_wait(&empty[sa], pa ^ 1, abort_flag, p.status, kDevTimeoutGemm)))) break;
+#ifdef MB_TRACE
+          const long long td1 = clock64();
+#endif
           tc_fence_after();
           if (!ABL(8)) {
             tmem_st16(tmem + lane_addr + kTmemA + sa * 32 + hh * 16, o);
@@ -550,6 +561,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(&full[sa]);
+#ifdef MB_TRACE
+          tr_[15] += (unsigned long long)(clock64() - td1);
+#endif
         }
       }
     }
@@ -720,7 +734,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 #ifdef MB_TRACE
   if (p.trace && (lane == 0 || (warp == 0 && lane == 1)) && (warp <= 2 || warp == 2 + kDW))
-    for (int i = 0; i < 12; i++)
+    for (int i = 0; i < 16; i++)
       if (tr_[i]) atomicAdd(p.trace + i, tr_[i]);
 #endif
   tc_fence_before();
