@@ -287,22 +287,22 @@ MB_DEV void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
 }
 
 // D(tmem) (+)= A(tmem) * B(smem desc)^T
-// The same, executed by a whole converged warp: the elected lane (lane 0) issues it.
-MB_DEV void umma_ts_elect(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+// One stage (4 K16 steps) in one instruction sequence for a whole converged warp: the elected
+// lane issues D (+)= A[a0 + 8k] * B[b0 + 32k bytes]^T for k = 0..3 (one election, one predicate).
+MB_DEV void umma_ts_stage4(uint32_t d_tmem, uint32_t a0, uint64_t b0, uint32_t idesc, uint32_t accumulate) {
   asm volatile(
-      "{\n .reg .pred p, e;\n .reg .b32 r;\n setp.ne.b32 p, %4, 0;\n elect.sync r|e, 0xffffffff;\n"
-      " @e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(d_tmem),
-      "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      "{\n .reg .pred p, e, t;\n .reg .b32 r, a1, a2, a3;\n .reg .b64 b1, b2, b3;\n"
+      " setp.ne.b32 p, %4, 0;\n setp.eq.b32 t, 0, 0;\n"
+      " add.u32 a1, %1, 8;\n add.u32 a2, %1, 16;\n add.u32 a3, %1, 24;\n"
+      " add.u64 b1, %2, 2;\n add.u64 b2, %2, 4;\n add.u64 b3, %2, 6;\n"
+      " elect.sync r|e, 0xffffffff;\n"
+      " @e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n"
+      " @e tcgen05.mma.cta_group::1.kind::f16 [%0], [a1], b1, %3, t;\n"
+      " @e tcgen05.mma.cta_group::1.kind::f16 [%0], [a2], b2, %3, t;\n"
+      " @e tcgen05.mma.cta_group::1.kind::f16 [%0], [a3], b3, %3, t;\n}\n" ::"r"(d_tmem),
+      "r"(a0), "l"(b0), "r"(idesc), "r"(accumulate)
       : "memory");
 }
-MB_DEV void umma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
-  asm volatile(
-      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(
-          d_tmem),
-      "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-
 template <int WT>
 __global__ void __launch_bounds__(kThreads, 1)
     k_qgemm(const __grid_constant__ CUtensorMap tm_x0, const __grid_constant__ CUtensorMap tm_w0,
@@ -430,15 +430,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         const long long ti0 = clock64();
 #endif
         {
-          // The whole (converged) warp runs the issue loop and lane 0 issues each MMA
-          // (elect.sync): measured 8-12 % faster than a lane-0-only branch, whose issue
-          // of 4 MMAs took ~537 cycles per 512-cycle stage.
+          // The whole (converged) warp runs the issue sequence and lane 0 issues the stage's four
+          // MMAs under one elect.sync (umma_ts_stage4): every instruction of the issuer costs
+          // extra cycles while the decoder warps of its SM sub-partition keep that sub-partition
+          // busy. Measured against a lane-0-only branch issuing one MMA per call (~537 issue
+          // cycles per 512-cycle stage): one election per MMA +8-12 %, one per stage +2 % more.
           const uint32_t xaddr = smem_u32(xs + sx * kXStageBytes);
-#pragma unroll
-          for (int kk = 0; kk < BK / 16; kk++) {
-            const uint64_t bdesc = sw128_desc(xaddr + kk * 32, 16, 1024);
-            umma_ts_elect(tmem, tmem + kTmemA + sa * 32 + kk * 8, bdesc, idesc, (ks | kk) != 0);
-          }
+          // the descriptor's address field is bits 0-13 (bytes >> 4): +32 bytes per K16 step = +2
+          static_assert(BK / 16 == 4, "one stage = four K16 MMAs");
+          umma_ts_stage4(tmem, tmem + kTmemA + sa * 32, sw128_desc(xaddr, 16, 1024), idesc, ks != 0);
           if (lane == 0) umma_commit(&empty[sx]);
         }
         __syncwarp();
