@@ -66,6 +66,7 @@ struct mb_flux {
   std::vector<int64_t> mod_off_double, mod_off_single;
   int64_t mod_off_final = 0, mod_total = 0;
   GemvJob* jobs_dev = nullptr;
+  int gemv_kinds = 0;  // bit gemv_kind(type) of every GEMV job's weight type
   int* blocks_dev = nullptr;
   int n_jobs[3] = {0, 0, 0}, n_blocks[3] = {0, 0, 0}, job0[3] = {0, 0, 0}, block0[3] = {0, 0, 0};
 
@@ -191,6 +192,7 @@ mb_status finalize(mb_flux* m) {
     GemvJob j = {};
     j.w = w->dev;
     j.type = w->type;
+    m->gemv_kinds |= 1 << gemv_kind(w->type);
     j.n_rows = (int)w->n_rows;
     j.n_cols = (int)w->n_cols;
     j.row_bytes = w->row_bytes;
@@ -253,7 +255,7 @@ mb_status finalize(mb_flux* m) {
 }
 
 mb_status gemv_table(const mb_flux* m, int table, const GemvInput* ins, int n_in, cudaStream_t st) {
-  return check_launch(launch_gemv_batch(m->jobs_dev, 0, m->blocks_dev + 2 * m->block0[table], m->n_blocks[table], ins,
+  return check_launch(launch_gemv_batch(m->jobs_dev, m->gemv_kinds, m->blocks_dev + 2 * m->block0[table], m->n_blocks[table], ins,
                                         n_in, m->gemv_stage, st),
                       "gemv batch");
 }

@@ -188,34 +188,150 @@ MB_DEV void rows_q8(const GemvJob& job, const float* __restrict__ xs, int r0, in
   finish_rows<LPR>(acc, r0, sub, sl, nr, job);
 }
 
+// Q6_K rows (224-byte device chunks of 256 values): unit u = values 32u .. 32u+31 of a chunk,
+// x_l = d sc[16-value group] (q6_l - 32). A lane keeps its unit's 32 staged x values in registers
+// and serves its rows RB at a time with all their loads issued first; the scales multiply the two
+// 16-value partial dots (exact decode is not needed for a float dot product).
+template <int LPR>
+MB_DEV void rows_q6k(const GemvJob& job, const float* __restrict__ xs, int r0, int nr, int lane) {
+  constexpr int NSUB = 32 / LPR, RPL = kRowsPerWarp / NSUB, RB = RPL < 4 ? RPL : 4;
+  const int sub = lane / LPR, sl = lane % LPR;
+  const int U = job.n_cols / 32;
+  const uint8_t* wbase = (const uint8_t*)job.w + (int64_t)r0 * job.row_bytes;
+  float acc[RPL];
+#pragma unroll
+  for (int i = 0; i < RPL; i++) acc[i] = 0.f;
+  for (int u = sl; u < U; u += LPR) {
+    const int c = u >> 3, uu = u & 7, n = uu >> 2, g = uu & 3;
+    const int nsh = (g >> 1) * 4, hsh = 2 * g;
+    float x[32];
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+      const float4 t = __ldg((const float4*)(xs + u * 32) + i);
+      x[4 * i] = t.x; x[4 * i + 1] = t.y; x[4 * i + 2] = t.z; x[4 * i + 3] = t.w;
+    }
+#pragma unroll
+    for (int i0 = 0; i0 < RPL; i0 += RB) {
+      uint4 L0[RB], L1[RB], H0[RB], H1[RB];
+      uint32_t SD[RB], DD[RB];
+#pragma unroll
+      for (int j = 0; j < RB; j++) {
+        const int rr = min(sub + (i0 + j) * NSUB, nr - 1);  // rows past the end re-read the last row
+        const uint8_t* b = wbase + (int64_t)rr * job.row_bytes + (int64_t)c * 224;
+        L0[j] = __ldg((const uint4*)(b + 64 * n + 32 * (g & 1)));
+        L1[j] = __ldg((const uint4*)(b + 64 * n + 32 * (g & 1) + 16));
+        H0[j] = __ldg((const uint4*)(b + 128 + 32 * n));
+        H1[j] = __ldg((const uint4*)(b + 128 + 32 * n + 16));
+        SD[j] = __ldg((const uint16_t*)(b + 192 + 8 * n + 2 * g));
+        DD[j] = __ldg((const uint16_t*)(b + 208));
+      }
+#pragma unroll
+      for (int j = 0; j < RB; j++) {
+        const uint32_t lw[8] = {L0[j].x, L0[j].y, L0[j].z, L0[j].w, L1[j].x, L1[j].y, L1[j].z, L1[j].w};
+        const uint32_t hw[8] = {H0[j].x, H0[j].y, H0[j].z, H0[j].w, H1[j].x, H1[j].y, H1[j].z, H1[j].w};
+        float dot0 = 0.f, dot1 = 0.f;
+#pragma unroll
+        for (int k = 0; k < 32; k++) {
+          const uint32_t lo = (lw[k >> 2] >> (8 * (k & 3) + nsh)) & 0xFu;
+          const uint32_t hi = (hw[k >> 2] >> (8 * (k & 3) + hsh)) & 3u;
+          const float q = (float)((int)(lo | (hi << 4)) - 32);
+          if (k < 16) dot0 = fmaf(q, x[k], dot0);
+          else dot1 = fmaf(q, x[k], dot1);
+        }
+        const float d = h16(DD[j]);
+        const float s0 = (float)(int8_t)(SD[j] & 0xFFu), s1 = (float)(int8_t)(SD[j] >> 8);
+        acc[i0 + j] += d * (s0 * dot0 + s1 * dot1);
+      }
+    }
+  }
+  finish_rows<LPR>(acc, r0, sub, sl, nr, job);
+}
+
+// Q4_1 rows: unit = one 20-byte block (f16 d, f16 m, 16 bytes of nibbles) of 32 values,
+// sum_j (d q_j + m) x_j = d sum_j q_j x_j + m sum_j x_j (the staged 32-value partial sums).
+template <int LPR>
+MB_DEV void rows_q41(const GemvJob& job, const float* __restrict__ xs, const float* __restrict__ xsum, int r0, int nr,
+                     int lane) {
+  constexpr int NSUB = 32 / LPR, RPL = kRowsPerWarp / NSUB, RB = RPL < 4 ? RPL : 4;
+  const int sub = lane / LPR, sl = lane % LPR;
+  const int U = job.n_cols / 32;
+  const uint8_t* wbase = (const uint8_t*)job.w + (int64_t)r0 * job.row_bytes;
+  float acc[RPL];
+#pragma unroll
+  for (int i = 0; i < RPL; i++) acc[i] = 0.f;
+  for (int u = sl; u < U; u += LPR) {
+    float x[32];
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+      const float4 t = __ldg((const float4*)(xs + u * 32) + i);
+      x[4 * i] = t.x; x[4 * i + 1] = t.y; x[4 * i + 2] = t.z; x[4 * i + 3] = t.w;
+    }
+    const float s = __ldg(xsum + u);
+#pragma unroll
+    for (int i0 = 0; i0 < RPL; i0 += RB) {
+      uint32_t w[RB][5];  // 20-byte blocks are 4-byte aligned
+#pragma unroll
+      for (int j = 0; j < RB; j++) {
+        const int rr = min(sub + (i0 + j) * NSUB, nr - 1);
+        const uint32_t* b = (const uint32_t*)(wbase + (int64_t)rr * job.row_bytes + (int64_t)u * 20);
+#pragma unroll
+        for (int k = 0; k < 5; k++) w[j][k] = __ldg(b + k);
+      }
+#pragma unroll
+      for (int j = 0; j < RB; j++) {
+        float dot = 0.f;
+#pragma unroll
+        for (int k = 0; k < 16; k++) {
+          const uint32_t byte = (w[j][1 + (k >> 2)] >> (8 * (k & 3))) & 0xFFu;
+          dot = fmaf((float)(byte & 0xF), x[k], dot);
+          dot = fmaf((float)(byte >> 4), x[k + 16], dot);
+        }
+        acc[i0 + j] += h16(w[j][0]) * dot + h16(w[j][0] >> 16) * s;
+      }
+    }
+  }
+  finish_rows<LPR>(acc, r0, sub, sl, nr, job);
+}
+
 // Other chunked types: unit = 32 values decoded by decode_unit<T> straight from global memory.
-// Rows run one at a time (one accumulator, reduced and stored per row) to keep registers low.
+// A lane serves its rows RB at a time (the RB decodes are independent, so their loads are in flight
+// together), reading the unit's staged x values once per row pair.
 template <int T, int LPR>
 MB_DEV void rows_units(const GemvJob& job, const float* __restrict__ xs, int r0, int nr, int lane) {
   constexpr int NSUB = 32 / LPR, RPL = kRowsPerWarp / NSUB;
+  constexpr int RB = T == MB_GGML_Q5_K ? 1 : (RPL < 2 ? RPL : 2);  // Q5_K's decode needs the registers
   const int sub = lane / LPR, sl = lane % LPR;
   const int U = job.n_cols / 32;
-#pragma unroll 1
-  for (int i = 0; i < RPL; i++) {
-    const int rr = sub + i * NSUB;
-    const uint8_t* row = (const uint8_t*)job.w + (int64_t)(r0 + min(rr, nr - 1)) * job.row_bytes;
-    float acc = 0.f;
-    for (int u = sl; u < U; u += LPR) {
-      float y[32];
-      decode_unit<T>(row + (int64_t)(u >> 3) * kDeviceChunk(T), u & 7, y);
+  const uint8_t* wbase = (const uint8_t*)job.w + (int64_t)r0 * job.row_bytes;
+  float acc[RPL];
+#pragma unroll
+  for (int i = 0; i < RPL; i++) acc[i] = 0.f;
+  for (int u = sl; u < U; u += LPR) {
+    const int64_t coff = (int64_t)(u >> 3) * kDeviceChunk(T);
+#pragma unroll
+    for (int i0 = 0; i0 < RPL; i0 += RB) {
+      float y[RB][32];
+#pragma unroll
+      for (int j = 0; j < RB; j++) {
+        const int rr = min(sub + (i0 + j) * NSUB, nr - 1);  // rows past the end re-read the last row
+        decode_unit<T>(wbase + (int64_t)rr * job.row_bytes + coff, u & 7, y[j]);
+      }
 #pragma unroll
       for (int k4 = 0; k4 < 8; k4++) {
         const float4 t = __ldg((const float4*)(xs + u * 32) + k4);
-        acc = fmaf(y[4 * k4], t.x, acc);
-        acc = fmaf(y[4 * k4 + 1], t.y, acc);
-        acc = fmaf(y[4 * k4 + 2], t.z, acc);
-        acc = fmaf(y[4 * k4 + 3], t.w, acc);
+#pragma unroll
+        for (int j = 0; j < RB; j++) {
+          float a = acc[i0 + j];
+          a = fmaf(y[j][4 * k4], t.x, a);
+          a = fmaf(y[j][4 * k4 + 1], t.y, a);
+          a = fmaf(y[j][4 * k4 + 2], t.z, a);
+          a = fmaf(y[j][4 * k4 + 3], t.w, a);
+          acc[i0 + j] = a;
+        }
       }
     }
-#pragma unroll
-    for (int o = LPR / 2; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-    if (sl == 0 && rr < nr) job.y[r0 + rr] = acc + (job.bias ? job.bias[r0 + rr] : 0.f);
   }
+  finish_rows<LPR>(acc, r0, sub, sl, nr, job);
 }
 
 template <int T>
@@ -249,49 +365,74 @@ MB_DEV void rows_plain(const GemvJob& job, const float* __restrict__ xs, int r0,
   finish_rows<32>(acc, r0, 0, lane, nr, job);
 }
 
-// One block = kWarps warps x kRowsPerWarp rows of one job (blocks[] = (job, first row)).
+MB_DEV bool fast_kind(int t) {
+  return t == MB_GGML_Q4_K || t == MB_GGML_Q8_0 || t == MB_GGML_F32 || t == MB_GGML_F16 || t == MB_GGML_BF16;
+}
+
+// One block = kWarps warps x kRowsPerWarp rows of one job (blocks[] = (job, first row)). Two
+// kernels (KIND 0: Q4_K, Q8_0, plain; KIND 1: the decode_unit types) so that each is compiled
+// for its own paths' registers; a block whose job is of the other kind returns at once.
+template <int KIND>
 __global__ void __launch_bounds__(kWarps * 32, 3)
     k_gemv(const GemvJob* __restrict__ jobs, const int2* __restrict__ blocks, GemvJob inline_job,
            const float* __restrict__ stage) {
   const int2 bj = jobs ? blocks[blockIdx.x] : make_int2(0, blockIdx.x * kGemvRowsPerBlock);
   const GemvJob job = jobs ? jobs[bj.x] : inline_job;
+  if (fast_kind(job.type) != (KIND == 0)) return;
   const float* xs = stage + (int64_t)job.x_slot * kStageStride;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int r0 = bj.y + warp * kRowsPerWarp;
   if (r0 >= job.n_rows) return;
   const int nr = min(kRowsPerWarp, job.n_rows - r0);
-  if (job.type == MB_GGML_Q4_K) {
-    if ((job.n_cols / 64) % 16 == 0)
-      rows_q4k<16>(job, xs, xs + kMaxLen, r0, nr, lane);
-    else
-      rows_q4k<32>(job, xs, xs + kMaxLen, r0, nr, lane);
-  } else if (job.type == MB_GGML_Q8_0) {
-    if ((job.n_cols / 32) % 32 == 0)
-      rows_q8<32>(job, xs, r0, nr, lane);
-    else
-      rows_q8<16>(job, xs, r0, nr, lane);
-  } else if (job.type == MB_GGML_Q4_0) {
-    rows_units_any<MB_GGML_Q4_0>(job, xs, r0, nr, lane);
-  } else if (job.type == MB_GGML_Q4_1) {
-    rows_units_any<MB_GGML_Q4_1>(job, xs, r0, nr, lane);
-  } else if (job.type == MB_GGML_Q5_0) {
-    rows_units_any<MB_GGML_Q5_0>(job, xs, r0, nr, lane);
-  } else if (job.type == MB_GGML_Q5_1) {
-    rows_units_any<MB_GGML_Q5_1>(job, xs, r0, nr, lane);
-  } else if (job.type == MB_GGML_Q5_K) {
-    rows_units_any<MB_GGML_Q5_K>(job, xs, r0, nr, lane);
-  } else if (job.type == MB_GGML_Q6_K) {
-    rows_units_any<MB_GGML_Q6_K>(job, xs, r0, nr, lane);
+  if constexpr (KIND == 0) {
+    if (job.type == MB_GGML_Q4_K) {
+      if ((job.n_cols / 64) % 16 == 0)
+        rows_q4k<16>(job, xs, xs + kMaxLen, r0, nr, lane);
+      else
+        rows_q4k<32>(job, xs, xs + kMaxLen, r0, nr, lane);
+    } else if (job.type == MB_GGML_Q8_0) {
+      if ((job.n_cols / 32) % 32 == 0)
+        rows_q8<32>(job, xs, r0, nr, lane);
+      else
+        rows_q8<16>(job, xs, r0, nr, lane);
+    } else {
+      rows_plain(job, xs, r0, nr, lane);
+    }
   } else {
-    rows_plain(job, xs, r0, nr, lane);
+    if (job.type == MB_GGML_Q4_0) {
+      rows_units_any<MB_GGML_Q4_0>(job, xs, r0, nr, lane);
+    } else if (job.type == MB_GGML_Q4_1) {
+      if ((job.n_cols / 32) % 32 == 0)
+        rows_q41<32>(job, xs, xs + kMaxLen, r0, nr, lane);
+      else
+        rows_q41<16>(job, xs, xs + kMaxLen, r0, nr, lane);
+    } else if (job.type == MB_GGML_Q5_0) {
+      rows_units_any<MB_GGML_Q5_0>(job, xs, r0, nr, lane);
+    } else if (job.type == MB_GGML_Q5_1) {
+      rows_units_any<MB_GGML_Q5_1>(job, xs, r0, nr, lane);
+    } else if (job.type == MB_GGML_Q5_K) {
+      rows_units_any<MB_GGML_Q5_K>(job, xs, r0, nr, lane);
+    } else {
+      if ((job.n_cols / 32) % 32 == 0)
+        rows_q6k<32>(job, xs, r0, nr, lane);
+      else
+        rows_q6k<16>(job, xs, r0, nr, lane);
+    }
   }
 }
 
 }  // namespace gemv
 
-cudaError_t launch_gemv_batch(const GemvJob* jobs_dev, int n_jobs, const int* block_job_dev, int n_blocks,
+int gemv_kind(int ggml_type) {
+  return (ggml_type == MB_GGML_Q4_K || ggml_type == MB_GGML_Q8_0 || ggml_type == MB_GGML_F32 ||
+          ggml_type == MB_GGML_F16 || ggml_type == MB_GGML_BF16)
+             ? 0
+             : 1;
+}
+
+cudaError_t launch_gemv_batch(const GemvJob* jobs_dev, int kinds, const int* block_job_dev, int n_blocks,
                               const GemvInput* inputs, int n_inputs, float* stage, cudaStream_t st) {
-  (void)n_jobs;
+  if (kinds & ~3) return cudaErrorInvalidValue;
   if (n_inputs < 1 || n_inputs > gemv::kMaxInputs || !stage) return cudaErrorInvalidValue;
   gemv::Inputs ins = {};
   for (int i = 0; i < n_inputs; i++) {
@@ -300,7 +441,8 @@ cudaError_t launch_gemv_batch(const GemvJob* jobs_dev, int n_jobs, const int* bl
   }
   gemv::k_gemv_stage<<<n_inputs, 256, 0, st>>>(ins, stage);
   GemvJob dummy = {};
-  gemv::k_gemv<<<n_blocks, gemv::kWarps * 32, 0, st>>>(jobs_dev, (const int2*)block_job_dev, dummy, stage);
+  if (kinds & 1) gemv::k_gemv<0><<<n_blocks, gemv::kWarps * 32, 0, st>>>(jobs_dev, (const int2*)block_job_dev, dummy, stage);
+  if (kinds & 2) gemv::k_gemv<1><<<n_blocks, gemv::kWarps * 32, 0, st>>>(jobs_dev, (const int2*)block_job_dev, dummy, stage);
   return cudaGetLastError();
 }
 
@@ -328,7 +470,10 @@ cudaError_t launch_gemv_single(const mb_weight* w, const float* x, int apply_sil
   ins.in[0].len = (int)w->n_cols;
   gemv::k_gemv_stage<<<1, 256, 0, st>>>(ins, stage);
   const int blocks = (int)((w->n_rows + kGemvRowsPerBlock - 1) / kGemvRowsPerBlock);
-  gemv::k_gemv<<<blocks, gemv::kWarps * 32, 0, st>>>(nullptr, nullptr, j, stage);
+  if (gemv_kind(w->type) == 0)
+    gemv::k_gemv<0><<<blocks, gemv::kWarps * 32, 0, st>>>(nullptr, nullptr, j, stage);
+  else
+    gemv::k_gemv<1><<<blocks, gemv::kWarps * 32, 0, st>>>(nullptr, nullptr, j, stage);
   return cudaGetLastError();
 }
 

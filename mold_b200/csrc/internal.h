@@ -104,8 +104,12 @@ constexpr int kGemvRowsPerBlock = 32;  // rows of one job handled by one GEMV bl
 // Runs a batch of GEMV jobs: one launch stages the inputs (len % 32 == 0, <= 4096) into
 // `stage` (gemv_stage_floats() floats, owned by the caller), one launch runs every job.
 // jobs_dev / block_job_dev live in device memory.
-cudaError_t launch_gemv_batch(const GemvJob* jobs_dev, int n_jobs, const int* block_job_dev, int n_blocks,
+// `kinds`: bit gemv_kind(type) set for every weight type among the jobs (one kernel per kind
+// runs; blocks of a job of the other kind exit at once).
+cudaError_t launch_gemv_batch(const GemvJob* jobs_dev, int kinds, const int* block_job_dev, int n_blocks,
                               const GemvInput* inputs, int n_inputs, float* stage, cudaStream_t st);
+// 0: Q4_K, Q8_0 and plain types (their own row kernels); 1: the other block types (decode_unit)
+int gemv_kind(int ggml_type);
 size_t gemv_stage_floats();
 
 cudaError_t launch_ln_modulate(const float* x, int64_t M, int64_t C, int64_t ldx, const float* shift,

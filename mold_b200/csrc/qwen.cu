@@ -82,6 +82,7 @@ struct mb_qwen {
   std::vector<int64_t> mod_off;
   int64_t mod_off_final = 0;
   GemvJob* jobs_dev = nullptr;
+  int gemv_kinds = 0;  // bit gemv_kind(type) of every GEMV job's weight type
   int* blocks_dev = nullptr;
   int n_blocks[3] = {0, 0, 0}, block0[3] = {0, 0, 0};
 
@@ -219,6 +220,7 @@ mb_status finalize(mb_qwen* m) {
     GemvJob j = {};
     j.w = w->dev;
     j.type = w->type;
+    m->gemv_kinds |= 1 << gemv_kind(w->type);
     j.n_rows = (int)w->n_rows;
     j.n_cols = (int)w->n_cols;
     j.row_bytes = w->row_bytes;
@@ -262,7 +264,7 @@ mb_status finalize(mb_qwen* m) {
 }
 
 mb_status gemv_table(const mb_qwen* m, int table, const GemvInput* in, cudaStream_t st) {
-  return check_launch(launch_gemv_batch(m->jobs_dev, 0, m->blocks_dev + 2 * m->block0[table], m->n_blocks[table], in,
+  return check_launch(launch_gemv_batch(m->jobs_dev, m->gemv_kinds, m->blocks_dev + 2 * m->block0[table], m->n_blocks[table], in,
                                         1, m->gemv_stage, st),
                       "gemv batch");
 }
