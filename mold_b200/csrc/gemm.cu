@@ -93,7 +93,8 @@ struct Params {
   int nprob;
   int n_tiles;
   int* status;
-  int ablate;  // builds with -DMB_TRACE only: 1 decode, 2 X loads, 4 raw loads, 8 TMEM stores, 16 epilogue
+  int ablate;  // builds with -DMB_TRACE only: 1 decode, 2 X loads, 4 raw loads, 8 TMEM stores, 16 epilogue,
+              // 32 drain staging stores, 64 drain arithmetic
   unsigned long long* trace;  // builds with -DMB_TRACE only: summed wait cycles per role (see TW)
 };
 
@@ -606,22 +607,36 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll 1
         for (int c = 0; c < 4; c++) {
           uint32_t v[32];
+#ifdef MB_TRACE
+          const long long tl0 = clock64();
+#endif
           tmem_ld32(tmem + lane_addr + ch * 128 + c * 32, v);
           tmem_wait_ld();
 #ifdef MB_TRACE
-          if (c == 0) tr_[9] += (unsigned long long)(clock64() - t_drain_);
+          tr_[9] += (unsigned long long)(clock64() - tl0);
 #endif
           uint32_t o[16];
+          if (ABL(64)) {
 #pragma unroll
-          for (int j = 0; j < 16; j++) {
-            float a0 = __uint_as_float(v[2 * j]) + bias, a1 = __uint_as_float(v[2 * j + 1]) + bias;
-            if (do_gelu) {
-              a0 = gelu_tanh(a0);
-              a1 = gelu_tanh(a1);
+            for (int j = 0; j < 16; j++) o[j] = v[2 * j] ^ v[2 * j + 1];
+          } else {
+#pragma unroll
+            for (int j = 0; j < 16; j++) {
+              float a0 = __uint_as_float(v[2 * j]) + bias, a1 = __uint_as_float(v[2 * j + 1]) + bias;
+              if (do_gelu) {
+                a0 = gelu_tanh(a0);
+                a1 = gelu_tanh(a1);
+              }
+              o[j] = pack_bf16x2(a0, a1);
             }
-            o[j] = pack_bf16x2(a0, a1);
           }
-          tmem_st16(stage + c * 16, o);
+#ifdef MB_TRACE
+          const long long tc1 = clock64();
+#endif
+          if (!ABL(32)) tmem_st16(stage + c * 16, o);
+#ifdef MB_TRACE
+          tr_[3] += (unsigned long long)(clock64() - tc1);  // slot 3: drain staging-store issue
+#endif
         }
         tmem_wait_st();
 #ifdef MB_TRACE
