@@ -340,6 +340,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const CUtensorMap* tm_w = pi_ ? &tm_w1 : &tm_w0;                         \
   (void)tm_x;                                                              \
   (void)tm_w;                                                              \
+  (void)lt_;                                                               \
   (void)nks;
 
   if (threadIdx.x == 0) {
