@@ -13,8 +13,8 @@
 //   * X (activations, bf16, K-major) is TMA-loaded with the 128-byte swizzle into
 //     an 8-stage ring and read by tcgen05.mma as the B operand.
 //   * Raw weight bytes are TMA-loaded in their GGUF layout (Q4_K: whole 144-byte
-//     super-blocks, one TMA per 4 stages, scales decoded once per super-block; Q8_0:
-//     the 80-byte window holding a stage's two 34-byte blocks; BF16: 128 bytes).
+//     super-blocks, one TMA per 4 stages, scales decoded once per super-block; Q8_0 and
+//     the other block types: whole 256-value chunks likewise; BF16: 128 bytes per stage).
 //   * Tile = 128 weight rows x 256 activation rows, so each decoded weight feeds
 //     256 MACs (the dequant rate needed is 16 values per SM clock at full MMA
 //     rate). TMEM: the 128x256 f32 accumulator in columns [0, 256) and an
@@ -67,7 +67,9 @@ struct Cfg<MB_GGML_Q4_K> {
 };
 template <>
 struct Cfg<MB_GGML_Q8_0> {
-  static constexpr int kRawRow = 80, kSPC = 1, kSR = 6, kSX = 4;
+  // whole 272-byte chunks of 8 blocks (loaded as 136 16-bit elements: a TMA box is <= 256 wide);
+  // measured +10 % over one 80-byte window per stage
+  static constexpr int kRawRow = 272, kSPC = 4, kSR = 2, kSX = 4;
 };
 template <>
 struct Cfg<MB_GGML_BF16> {
@@ -256,18 +258,21 @@ MB_DEV void dq_unit_q41(const uint8_t* c, int u, uint32_t (&o)[16]) {
   }
 }
 
-// Q8_0 block at byte offset P (compile-time) of a 48-byte window W[12].
-template <int P>
-MB_DEV void q8_block(const uint32_t (&W)[12], uint32_t (&o)[16]) {
-  constexpr int wi = P >> 2;
-  const float d = (P & 3) == 0 ? h16(W[wi]) : h16(W[wi] >> 16);
-  const uint64_t dd = f2(d, d);
-  constexpr int qb = P + 2;  // first quant byte
-  constexpr int qw = qb >> 2;
+// Q8_0 unit u (block u, 34 bytes at 34u) of a 272-byte chunk: blocks of even u start 4-byte
+// aligned, odd ones 2 bytes past a word boundary.
+MB_DEV void dq_unit_q8(const uint8_t* c, int u, uint32_t (&o)[16]) {
+  if ((u & 1) == 0) {
+    const uint32_t* a = (const uint32_t*)(c + 34 * u);
+    const float d = h16(a[0]);
+    const uint64_t dd = f2(d, d);
 #pragma unroll
-  for (int i = 0; i < 8; i++) {
-    const uint32_t q = (qb & 3) == 0 ? W[qw + i] : __byte_perm(W[qw + i], W[qw + i + 1], 0x5432);
-    dq8(q, dd, o[2 * i], o[2 * i + 1]);
+    for (int i = 0; i < 8; i++) dq8(__byte_perm(a[i], a[i + 1], 0x5432), dd, o[2 * i], o[2 * i + 1]);
+  } else {
+    const uint32_t* b = (const uint32_t*)(c + 34 * u - 2);
+    const float d = h16(b[0] >> 16);
+    const uint64_t dd = f2(d, d);
+#pragma unroll
+    for (int i = 0; i < 8; i++) dq8(b[1 + i], dd, o[2 * i], o[2 * i + 1]);
   }
 }
 
@@ -405,8 +410,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           mbar_expect_tx(&r_full[sr], kRawStage);
           uint8_t* rdst = rs + sr * kRawStage;
-          if (WT == MB_GGML_Q8_0) {
-            tma_load_2d(rdst, tm_w, &r_full[sr], (68 * ks) & ~15, n0);
+          if (WT == MB_GGML_Q8_0) {  // 16-bit elements
+            tma_load_2d(rdst, tm_w, &r_full[sr], (ks >> 2) * (Cfg<WT>::kRawRow / 2), n0);
           } else if (WT == MB_GGML_BF16) {
             tma_load_2d(rdst, tm_w, &r_full[sr], ks * 128, n0);
           } else {  // one whole 256-value chunk (ks is a multiple of kSPC = 4)
@@ -506,23 +511,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int i = 0; i < 8; i++) dq4(w[i] & mask, D1, C1, M1, o[2 * i], o[2 * i + 1]);
           } else if constexpr (WT == MB_GGML_Q8_0) {
-            const int off = (68 * ks) & 15;  // window offset of block 0 (0,4,8,12)
-            const int base16 = hh ? 32 : 0;  // 16-aligned start of the 48-byte window
-            const uint4* src = (const uint4*)(R + r * 80 + base16);
-            const uint4 a0 = src[0], a1 = src[1], a2 = src[2];
-            const uint32_t W[12] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w, a2.x, a2.y, a2.z, a2.w};
-            // block start within the window: hh=0 -> off ; hh=1 -> off + 34 - 32
-            const int P = hh ? off + 2 : off;
-            switch (P) {
-              case 0: q8_block<0>(W, o); break;
-              case 4: q8_block<4>(W, o); break;
-              case 8: q8_block<8>(W, o); break;
-              case 12: q8_block<12>(W, o); break;
-              case 2: q8_block<2>(W, o); break;
-              case 6: q8_block<6>(W, o); break;
-              case 10: q8_block<10>(W, o); break;
-              default: q8_block<14>(W, o); break;
-            }
+            dq_unit_q8(R + r * Cfg<WT>::kRawRow, 2 * j + hh, o);
           } else if constexpr (WT == MB_GGML_BF16) {
             const uint4* src = (const uint4*)(R + r * 128 + hh * 64);
 #pragma unroll
@@ -771,6 +760,9 @@ bool make_maps(const mb_weight* w, const void* x, int64_t M, int64_t ldx, CUtens
     return false;
   const uint64_t rb = (uint64_t)w->row_bytes, nr = (uint64_t)w->n_rows;
   const uint32_t box = (uint32_t)Cfg<WT>::kRawRow;
+  if (WT == MB_GGML_Q8_0)  // 16-bit elements: the 272-byte box is 136 wide
+    return make_tmap_2d(tw, w->dev, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, rb / 2, nr, rb, box / 2, TN,
+                        CU_TENSOR_MAP_SWIZZLE_NONE);
   return make_tmap_2d(tw, w->dev, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, rb, nr, rb, box, TN, CU_TENSOR_MAP_SWIZZLE_NONE);
 }
 
