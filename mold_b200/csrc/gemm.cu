@@ -258,6 +258,66 @@ MB_DEV void dq_unit_q41(const uint8_t* c, int u, uint32_t (&o)[16]) {
   }
 }
 
+// b - bias for the four bytes of b (0..255; bias = 8 or 16), times d, as two packed bf16 pairs:
+// both steps are exact (small integers, then an 11-bit x 5-bit product), one rounding to bf16.
+MB_DEV void dq_sym(uint32_t b, uint64_t dd, uint64_t bias, uint32_t& o0, uint32_t& o1) {
+  float f0, f1, f2v, f3;
+  magic4(b, f0, f1, f2v, f3);
+  o0 = bf16x2_of(fmul2(fsub2(f2(f0, f1), bias), dd));
+  o1 = bf16x2_of(fmul2(fsub2(f2(f2v, f3), bias), dd));
+}
+// the low bits of nibble-packed bytes plus a fifth bit per byte from 4 bits of qh
+MB_DEV uint32_t with_hi_bits(uint32_t nib, uint32_t qh4) {
+  return nib | (((qh4 * 0x00204081u) & 0x01010101u) << 4);
+}
+
+// Q4_0 unit u (block u: f16 d, 16 bytes of nibbles; 18 bytes at 18u, 2-byte aligned):
+// x_j = d (q_j - 8).
+MB_DEV void dq_unit_q40(const uint8_t* c, int u, uint32_t (&o)[16]) {
+  uint32_t w[5];
+  dec::words<5>(c + u * 18, w);
+  const float d = h16(w[0]);
+  const uint64_t dd = f2(d, d), bias = f2(8388616.f, 8388616.f);  // 2^23 + 8
+#pragma unroll
+  for (int k = 0; k < 4; k++) {
+    const uint32_t q = __byte_perm(w[k], w[k + 1], 0x5432);
+    dq_sym(q & 0x0F0F0F0Fu, dd, bias, o[2 * k], o[2 * k + 1]);
+    dq_sym((q >> 4) & 0x0F0F0F0Fu, dd, bias, o[8 + 2 * k], o[8 + 2 * k + 1]);
+  }
+}
+
+// Q5_0 unit u (block u: f16 d, u32 qh, 16 bytes of nibbles; 22 bytes at 22u):
+// x_j = d (q5_j - 16), fifth bit of value j = qh bit j.
+MB_DEV void dq_unit_q50(const uint8_t* c, int u, uint32_t (&o)[16]) {
+  uint32_t w[6];
+  dec::words<6>(c + u * 22, w);
+  const float d = h16(w[0]);
+  const uint32_t qh = (w[0] >> 16) | (w[1] << 16);
+  const uint64_t dd = f2(d, d), bias = f2(8388624.f, 8388624.f);  // 2^23 + 16
+#pragma unroll
+  for (int k = 0; k < 4; k++) {
+    const uint32_t q = __byte_perm(w[1 + k], w[2 + k], 0x5432);
+    dq_sym(with_hi_bits(q & 0x0F0F0F0Fu, (qh >> (4 * k)) & 0xFu), dd, bias, o[2 * k], o[2 * k + 1]);
+    dq_sym(with_hi_bits((q >> 4) & 0x0F0F0F0Fu, (qh >> (16 + 4 * k)) & 0xFu), dd, bias, o[8 + 2 * k],
+           o[8 + 2 * k + 1]);
+  }
+}
+
+// Q5_1 unit u (block u: f16 d, f16 m, u32 qh, 16 bytes of nibbles; 24 bytes at 24u, 8-byte
+// aligned): x_j = d q5_j + m.
+MB_DEV void dq_unit_q51(const uint8_t* c, int u, uint32_t (&o)[16]) {
+  const uint32_t* a = (const uint32_t*)(c + u * 24);
+  const float d = h16(a[0]), m = h16(a[0] >> 16);
+  const uint32_t qh = a[1];
+  const uint64_t D = f2(d, d), C = f2(-(d * 8388608.f), -(d * 8388608.f)), Mm = f2(-m, -m);
+#pragma unroll
+  for (int k = 0; k < 4; k++) {
+    const uint32_t q = a[2 + k];
+    dq4(with_hi_bits(q & 0x0F0F0F0Fu, (qh >> (4 * k)) & 0xFu), D, C, Mm, o[2 * k], o[2 * k + 1]);
+    dq4(with_hi_bits((q >> 4) & 0x0F0F0F0Fu, (qh >> (16 + 4 * k)) & 0xFu), D, C, Mm, o[8 + 2 * k], o[8 + 2 * k + 1]);
+  }
+}
+
 // Q8_0 unit u (block u, 34 bytes at 34u) of a 272-byte chunk: blocks of even u start 4-byte
 // aligned, odd ones 2 bytes past a word boundary.
 MB_DEV void dq_unit_q8(const uint8_t* c, int u, uint32_t (&o)[16]) {
@@ -525,6 +585,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             dq_unit_q5k(R + r * Cfg<WT>::kRawRow, 2 * j + hh, o);
           } else if constexpr (WT == MB_GGML_Q4_1) {
             dq_unit_q41(R + r * Cfg<WT>::kRawRow, 2 * j + hh, o);
+          } else if constexpr (WT == MB_GGML_Q4_0) {
+            dq_unit_q40(R + r * Cfg<WT>::kRawRow, 2 * j + hh, o);
+          } else if constexpr (WT == MB_GGML_Q5_0) {
+            dq_unit_q50(R + r * Cfg<WT>::kRawRow, 2 * j + hh, o);
+          } else if constexpr (WT == MB_GGML_Q5_1) {
+            dq_unit_q51(R + r * Cfg<WT>::kRawRow, 2 * j + hh, o);
           } else {
             float y[32];
             decode_unit<WT>(R + r * Cfg<WT>::kRawRow, 2 * j + hh, y);
