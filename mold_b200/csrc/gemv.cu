@@ -83,12 +83,14 @@ MB_DEV void finish_rows(const float (&acc)[kRowsPerWarp * LPR / 32], int r0, int
 
 // Q4_K rows: a group of LPR lanes serves one row; lane sl takes the 64-value units
 // sl, sl + LPR, ... (unit = the low and high nibbles of one 32-byte quant run = sub-blocks
-// 2g and 2g+1), keeps the unit's 64 staged x values in registers and applies them to its
-// RPL rows.
+// 2g and 2g+1) of its RPL rows.
 template <int LPR>
 MB_DEV void rows_q4k(const GemvJob& job, const float* __restrict__ xs, const float* __restrict__ xsum, int r0, int nr,
                      int lane) {
-  constexpr int NSUB = 32 / LPR, RPL = kRowsPerWarp / NSUB, RB = RPL < 4 ? RPL : 4;
+#ifndef MB_GEMV_Q4K_RB
+#define MB_GEMV_Q4K_RB 4
+#endif
+  constexpr int NSUB = 32 / LPR, RPL = kRowsPerWarp / NSUB, RB = RPL < MB_GEMV_Q4K_RB ? RPL : MB_GEMV_Q4K_RB;
   const int sub = lane / LPR, sl = lane % LPR;
   const int U = job.n_cols / 64;
   const uint8_t* wbase = (const uint8_t*)job.w + (int64_t)r0 * job.row_bytes;
@@ -97,45 +99,50 @@ MB_DEV void rows_q4k(const GemvJob& job, const float* __restrict__ xs, const flo
   for (int i = 0; i < RPL; i++) acc[i] = 0.f;
   for (int u = sl; u < U; u += LPR) {
     const int kb = u >> 2, g = u & 3;
-    float x[64];
-#pragma unroll
-    for (int i = 0; i < 16; i++) {
-      const float4 t = __ldg((const float4*)(xs + u * 64) + i);
-      x[4 * i] = t.x; x[4 * i + 1] = t.y; x[4 * i + 2] = t.z; x[4 * i + 3] = t.w;
-    }
+    const float4* x4 = (const float4*)(xs + u * 64);
     const float s_lo = __ldg(xsum + 2 * u), s_hi = __ldg(xsum + 2 * u + 1);
     // rows in batches of RB: all loads of a batch first (rows past the job's end re-read its
-    // last row; finish_rows drops them)
+    // last row; finish_rows drops them); the unit's x values are read per word (L1) and shared
+    // by the batch's rows, so no 64-value x array is held in registers
 #pragma unroll
     for (int i0 = 0; i0 < RPL; i0 += RB) {
-    uint4 H[RB], A[RB], B[RB];
+      uint4 H[RB], A[RB], B[RB];
 #pragma unroll
-    for (int j = 0; j < RB; j++) {
-      const int rr = min(sub + (i0 + j) * NSUB, nr - 1);
-      const uint8_t* b = wbase + (int64_t)rr * job.row_bytes + kb * 144;
-      H[j] = __ldg((const uint4*)b);
-      A[j] = __ldg((const uint4*)(b + 16 + 32 * g));
-      B[j] = __ldg((const uint4*)(b + 32 + 32 * g));
-    }
+      for (int j = 0; j < RB; j++) {
+        const int rr = min(sub + (i0 + j) * NSUB, nr - 1);
+        const uint8_t* b = wbase + (int64_t)rr * job.row_bytes + kb * 144;
+        H[j] = __ldg((const uint4*)b);
+        A[j] = __ldg((const uint4*)(b + 16 + 32 * g));
+        B[j] = __ldg((const uint4*)(b + 32 + 32 * g));
+      }
+      float dlo[RB], dhi[RB];
 #pragma unroll
-    for (int j = 0; j < RB; j++) {
-      const int i = i0 + j;
-      const float d = h16(H[j].x), dmin = h16(H[j].x >> 16);
-      int sc0, m0, sc1, m1;
-      q4k_sm(2 * g, H[j].y, H[j].z, H[j].w, sc0, m0);
-      q4k_sm(2 * g + 1, H[j].y, H[j].z, H[j].w, sc1, m1);
-      float dlo = 0.f, dhi = 0.f;
-#define MB_Q4_WORD(W, I)                                     \
-  _Pragma("unroll") for (int t = 0; t < 4; t++) {            \
-    const uint32_t byte = ((W) >> (8 * t)) & 0xFFu;          \
-    dlo = fmaf((float)(byte & 0xF), x[4 * (I) + t], dlo);    \
-    dhi = fmaf((float)(byte >> 4), x[32 + 4 * (I) + t], dhi); \
-  }
-      MB_Q4_WORD(A[j].x, 0) MB_Q4_WORD(A[j].y, 1) MB_Q4_WORD(A[j].z, 2) MB_Q4_WORD(A[j].w, 3)
-      MB_Q4_WORD(B[j].x, 4) MB_Q4_WORD(B[j].y, 5) MB_Q4_WORD(B[j].z, 6) MB_Q4_WORD(B[j].w, 7)
-#undef MB_Q4_WORD
-      acc[i] += d * (float)sc0 * dlo - dmin * (float)m0 * s_lo + d * (float)sc1 * dhi - dmin * (float)m1 * s_hi;
-    }
+      for (int j = 0; j < RB; j++) dlo[j] = dhi[j] = 0.f;
+#pragma unroll
+      for (int I = 0; I < 8; I++) {
+        const float4 xl = __ldg(x4 + I), xh = __ldg(x4 + 8 + I);
+#pragma unroll
+        for (int j = 0; j < RB; j++) {
+          const uint32_t W = I < 4 ? (I == 0 ? A[j].x : I == 1 ? A[j].y : I == 2 ? A[j].z : A[j].w)
+                                   : (I == 4 ? B[j].x : I == 5 ? B[j].y : I == 6 ? B[j].z : B[j].w);
+          dlo[j] = fmaf((float)(W & 0xFu), xl.x, dlo[j]);
+          dhi[j] = fmaf((float)((W >> 4) & 0xFu), xh.x, dhi[j]);
+          dlo[j] = fmaf((float)((W >> 8) & 0xFu), xl.y, dlo[j]);
+          dhi[j] = fmaf((float)((W >> 12) & 0xFu), xh.y, dhi[j]);
+          dlo[j] = fmaf((float)((W >> 16) & 0xFu), xl.z, dlo[j]);
+          dhi[j] = fmaf((float)((W >> 20) & 0xFu), xh.z, dhi[j]);
+          dlo[j] = fmaf((float)((W >> 24) & 0xFu), xl.w, dlo[j]);
+          dhi[j] = fmaf((float)(W >> 28), xh.w, dhi[j]);
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < RB; j++) {
+        const float d = h16(H[j].x), dmin = h16(H[j].x >> 16);
+        int sc0, m0, sc1, m1;
+        q4k_sm(2 * g, H[j].y, H[j].z, H[j].w, sc0, m0);
+        q4k_sm(2 * g + 1, H[j].y, H[j].z, H[j].w, sc1, m1);
+        acc[i0 + j] += d * (float)sc0 * dlo[j] - dmin * (float)m0 * s_lo + d * (float)sc1 * dhi[j] - dmin * (float)m1 * s_hi;
+      }
     }
   }
   finish_rows<LPR>(acc, r0, sub, sl, nr, job);
@@ -372,8 +379,11 @@ MB_DEV bool fast_kind(int t) {
 // One block = kWarps warps x kRowsPerWarp rows of one job (blocks[] = (job, first row)). Two
 // kernels (KIND 0: Q4_K, Q8_0, plain; KIND 1: the decode_unit types) so that each is compiled
 // for its own paths' registers; a block whose job is of the other kind returns at once.
+#ifndef MB_GEMV_MINB
+#define MB_GEMV_MINB 3
+#endif
 template <int KIND>
-__global__ void __launch_bounds__(kWarps * 32, 3)
+__global__ void __launch_bounds__(kWarps * 32, MB_GEMV_MINB)
     k_gemv(const GemvJob* __restrict__ jobs, const int2* __restrict__ blocks, GemvJob inline_job,
            const float* __restrict__ stage) {
   const int2 bj = jobs ? blocks[blockIdx.x] : make_int2(0, blockIdx.x * kGemvRowsPerBlock);
