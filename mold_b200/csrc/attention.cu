@@ -36,7 +36,7 @@ constexpr size_t kSmem = 1024 + 6 * (size_t)kTile + 256;
 constexpr float kScaleLog2 = 0.12751743082459868f;  // log2(e) / sqrt(128)
 constexpr float kRescaleThreshold = 8.f;
 #ifndef MB_ATTN_POLY
-#define MB_ATTN_POLY 0
+#define MB_ATTN_POLY 6
 #endif
 constexpr int kPolyPerChunk = MB_ATTN_POLY;  // of every 32 exponentials, this many use the FMA-pipe polynomial
 
@@ -50,22 +50,6 @@ struct Params {
   int split;
   int* status;
 };
-
-// 2^x for x <= ~8 (arguments below -125 return 0). x = n + f with n = round(x), |f| <= 1/2;
-// 2^f from its Taylor series in f*ln2 to 4th order (relative error < 5e-5, well below the
-// bf16 rounding P is stored with); 2^n is added to the exponent field.
-MB_DEV float exp2_poly(float x) {
-  const float t = x + 12582912.f;  // 1.5 * 2^23: rounds x to an integer in the low mantissa bits
-  const float n = t - 12582912.f;
-  const float f = x - n;
-  float p = 0.009618129107628477f;  // ln2^4 / 24
-  p = fmaf(p, f, 0.05550410866482158f);  // ln2^3 / 6
-  p = fmaf(p, f, 0.2402265069591007f);   // ln2^2 / 2
-  p = fmaf(p, f, 0.6931471805599453f);   // ln2
-  p = fmaf(p, f, 1.0f);
-  const int e = (int)((uint32_t)(__float_as_int(t) - 0x4B400000) << 23);
-  return x < -125.f ? 0.f : __int_as_float(__float_as_int(p) + e);
-}
 
 // ---- packed f32x2 helpers (sm_100): two IEEE single-precision ops per instruction
 MB_DEV uint64_t pk2(float a, float b) {
@@ -94,23 +78,26 @@ MB_DEV float max3(float a, float b, float c) {
   asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
   return r;
 }
-// exp2_poly on a pair (same method as exp2_poly, packed arithmetic).
-MB_DEV void exp2_poly2(uint64_t x2, float& e0, float& e1) {
+// 2^x for a pair by a degree-3 polynomial (own minimax fit of 2^f on [-1/2, 1/2], max relative
+// error 7.5e-5, far below the bf16 rounding P is stored with): x is clamped to >= -126 (masked
+// keys give ~1e-38), rounded to n by the 1.5 * 2^23 trick, and 2^n enters the exponent field.
+MB_DEV void exp2_poly3(uint64_t x2, float& e0, float& e1) {
+  float a, b;
+  up2(x2, a, b);
+  a = fmaxf(a, -126.f);
+  b = fmaxf(b, -126.f);
+  const uint64_t xc = pk2(a, b);
   const uint64_t magic = pk2(12582912.f, 12582912.f);
-  const uint64_t t2 = add2(x2, magic);
-  const uint64_t f = sub2(x2, sub2(t2, magic));
-  uint64_t p = pk2(0.009618129107628477f, 0.009618129107628477f);
-  p = fma2(p, f, pk2(0.05550410866482158f, 0.05550410866482158f));
-  p = fma2(p, f, pk2(0.2402265069591007f, 0.2402265069591007f));
-  p = fma2(p, f, pk2(0.6931471805599453f, 0.6931471805599453f));
-  p = fma2(p, f, pk2(1.0f, 1.0f));
-  float t0, t1, p0, p1, x0, x1;
+  const uint64_t t2 = add2(xc, magic);
+  const uint64_t f = sub2(xc, sub2(t2, magic));
+  uint64_t p = fma2(pk2(0.05517132207751274f, 0.05517132207751274f), f, pk2(0.24261054396629333f, 0.24261054396629333f));
+  p = fma2(p, f, pk2(0.6932609677314758f, 0.6932609677314758f));
+  p = fma2(p, f, pk2(0.9999281167984009f, 0.9999281167984009f));
+  float t0, t1, p0, p1;
   up2(t2, t0, t1);
   up2(p, p0, p1);
-  up2(x2, x0, x1);
-  // 2^n enters through the exponent field: (bits(t) - bits(1.5*2^23)) << 23 == bits(t) << 23 (mod 2^32)
-  e0 = x0 < -125.f ? 0.f : __int_as_float(__float_as_int(p0) + (int)((uint32_t)__float_as_int(t0) << 23));
-  e1 = x1 < -125.f ? 0.f : __int_as_float(__float_as_int(p1) + (int)((uint32_t)__float_as_int(t1) << 23));
+  e0 = __int_as_float(__float_as_int(p0) + (int)((uint32_t)__float_as_int(t0) << 23));
+  e1 = __int_as_float(__float_as_int(p1) + (int)((uint32_t)__float_as_int(t1) << 23));
 }
 
 MB_DEV void tmem_st16a(uint32_t taddr, const uint32_t (&r)[16]) {
@@ -394,7 +381,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (AABL(4)) {
             up2(x2, e0, e1);
           } else if (2 * i < kPolyPerChunk) {
-            exp2_poly2(x2, e0, e1);
+            exp2_poly3(x2, e0, e1);
           } else {
             float x0, x1;
             up2(x2, x0, x1);
