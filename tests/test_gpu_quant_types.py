@@ -89,3 +89,27 @@ def test_tiny_flux_forward_q6k_q4_1_mix(cuda):
     t = lambda a: torch.from_numpy(a).to(cuda)
     pred = m.forward(t(img), t(ids), t(txt), t(tids), 0.7, t(y), 3.5).cpu().numpy()
     assert rel_l2(pred, ref) < 2e-2
+
+
+def test_tiny_flux_forward_gemv_kinds_mixed(cuda):
+    """Q4_K linears with Q6_K / Q5_K modulation weights: the step's modulation GEMVs then need both
+    GEMV kernels (Q4_K / Q8_0 / plain rows, and the decode_unit types) in the same batch."""
+    from tests.test_gpu_flux import TINY, inputs, to_model
+    W = F.synth_weights(TINY, seed=12, qtype=oracle.GGML_Q4_K)
+    W6 = F.synth_weights(TINY, seed=12, qtype=oracle.GGML_Q6_K)
+    W5 = F.synth_weights(TINY, seed=12, qtype=oracle.GGML_Q5_K)
+    swapped = 0
+    for n in W:
+        if n.endswith("weight") and ("_mod.lin" in n or "modulation.lin" in n):
+            src = W6 if swapped % 2 == 0 else W5
+            if src[n].ggml_type in (oracle.GGML_Q6_K, oracle.GGML_Q5_K):
+                W[n] = src[n]
+                swapped += 1
+    assert swapped >= 2
+    m = to_model(TINY, W, 64, 256)
+    img, ids, txt, tids, y = inputs(TINY, 40, 12, 10)
+    ref = F.forward(W, TINY, img, ids, txt, tids, 0.7, y, 3.5)
+    t = lambda a: torch.from_numpy(a).to(cuda)
+    pred = m.forward(t(img), t(ids), t(txt), t(tids), 0.7, t(y), 3.5).cpu().numpy()
+    assert mb.device_status() == 0
+    assert rel_l2(pred, ref) < 2e-2
