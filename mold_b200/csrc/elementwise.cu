@@ -138,8 +138,11 @@ cudaError_t launch_ln_modulate_segs(const float* x, int64_t C, int64_t ldx, cons
   __nv_bfloat16* yb = (__nv_bfloat16*)y;
   // block per row (measured on 4608 x 3072 from cold L2: 2.6 TB/s warp per row, 3.8 TB/s with
   // 128 threads x 6 float4)
-  if (M < (int64_t)1 << 31 && C % 768 == 0 && C / 24 <= 1024) {
-    k_ln_modulate_blk<6><<<(unsigned)M, (unsigned)(C / 24), 0, st>>>(x, (int)C, ldx, segs, yb, ldy);
+#ifndef MB_LN_NV
+#define MB_LN_NV 6  // float4 per thread (4608 x 3072 from cold L2: 6 -> 22.5 us, 2 -> 24.5, 8 -> 26.6, 12 -> 30.7)
+#endif
+  if (M < (int64_t)1 << 31 && C % (128 * MB_LN_NV) == 0 && C / (4 * MB_LN_NV) <= 1024) {
+    k_ln_modulate_blk<MB_LN_NV><<<(unsigned)M, (unsigned)(C / (4 * MB_LN_NV)), 0, st>>>(x, (int)C, ldx, segs, yb, ldy);
     return cudaGetLastError();
   }
   if (M < (int64_t)1 << 31 && C % 256 == 0 && C / 8 <= 1024) {
@@ -291,7 +294,10 @@ cudaError_t launch_qk_norm_rope_segs(const void* qkv, int64_t ld_qkv, int H, con
 #define MB_QK_G 4
 #endif
   constexpr int G = MB_QK_G;
-  k_qk_norm_rope<G><<<grid_cap((M * ((H + G - 1) / G) + 7) / 8), 256, 0, st>>>(
+#ifndef MB_QK_BLK
+#define MB_QK_BLK 128  // threads per block (cold-L2 FLUX shape: 128 -> 36.9 us, 256 -> 40.9, 64 -> 38.9)
+#endif
+  k_qk_norm_rope<G><<<grid_cap((M * ((H + G - 1) / G) + MB_QK_BLK / 32 - 1) / (MB_QK_BLK / 32)), MB_QK_BLK, 0, st>>>(
       (const __nv_bfloat16*)qkv, ld_qkv, H, pe, L_total, segs, (__nv_bfloat16*)q, (__nv_bfloat16*)k, (__nv_bfloat16*)v);
   return cudaGetLastError();
 }
