@@ -74,11 +74,77 @@ MB_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, 
   }
 }
 
+// ---------------------------------------------------------------- CTA pairs (clusters of 2)
+MB_DEV uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+MB_DEV uint32_t cluster_size() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(r));
+  return r;
+}
+// All threads of all CTAs of the cluster (release / acquire at cluster scope).
+MB_DEV void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// shared::cluster address of the same shared-memory offset in CTA `rank` of this cluster.
+MB_DEV uint32_t smem_in_cta(const void* p, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
+  return r;
+}
+// Arrive on a barrier of another CTA of the cluster. Default semantics (release at CTA scope), as
+// the pair kernels use around tcgen05 fences: the consumer is the pair's tensor core, ordered by
+// tcgen05.fence::before_thread_sync here and ::after_thread_sync at the waiter.
+MB_DEV void mbar_arrive_cluster(uint32_t cl_addr) {
+#ifdef MB_PAIR_CLUSTER_SCOPE
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cl_addr) : "memory");
+#else
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cl_addr) : "memory");
+#endif
+}
+MB_DEV bool mbar_try_wait_cl(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;\n"
+      " selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+// mbar_wait for phases completed by arrivals from the other CTA of a pair.
+MB_DEV bool mbar_wait_cl(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* status, int code) {
+#ifndef MB_PAIR_CLUSTER_SCOPE
+  return mbar_wait(bar, parity, abort_flag, status, code);
+#endif
+  long long t0 = clock64();
+  while (true) {
+    if (mbar_try_wait_cl(bar, parity, 20000)) return true;
+    if (*abort_flag) return false;
+    if (clock64() - t0 > kSpinLimitCycles) {
+      *abort_flag = 1;
+      if (status) atomicExch(status, code);
+      return false;
+    }
+  }
+}
+
 // ---------------------------------------------------------------- TMA
 MB_DEV void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
   asm volatile(
       "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];"
       ::"r"(smem_u32(dst)), "l"(map), "r"(smem_u32(bar)), "r"(x), "r"(y)
+      : "memory");
+}
+// Pair form: this CTA's tile lands in its own shared memory; the byte count completes on the
+// barrier at cluster address `bar_cl` (the pair leader's); nothing is written to the other CTA.
+MB_DEV void tma_load_2d_pair(void* dst, const CUtensorMap* map, uint32_t bar_cl, int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];"
+      ::"r"(smem_u32(dst)), "l"(map), "r"(bar_cl), "r"(x), "r"(y)
       : "memory");
 }
 MB_DEV void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y, int z) {
@@ -101,6 +167,23 @@ MB_DEV void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {
 MB_DEV void tmem_relinquish() { asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory"); }
 MB_DEV void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
   asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+MB_DEV void tmem_alloc_pair(uint32_t* dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)), "r"(ncols)
+               : "memory");
+}
+MB_DEV void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+MB_DEV void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+// Pair MMAs: arrive on the barrier at this offset in every CTA of `mask` once they complete.
+MB_DEV void umma_commit_pair(uint64_t* bar, uint16_t mask) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+                   smem_u32(bar)),
+               "h"(mask)
+               : "memory");
 }
 MB_DEV void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 MB_DEV void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }

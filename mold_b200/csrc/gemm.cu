@@ -20,6 +20,13 @@
 //     rate). TMEM: the 128x256 f32 accumulator in columns [0, 256) and an
 //     8-deep ring of 64-wide bf16 A stages in [256, 512). The epilogue releases
 //     the accumulator as soon as its last columns are in registers.
+//   * CTA pairs (default): a cluster of two CTAs on two SMs computes a 256-weight-row x
+//     256-activation-row tile with tcgen05.mma.cta_group::2 (M = 256). Each CTA decodes its own
+//     128 weight rows into its own TMEM and TMA-loads only its 128-row half of the X tile; the
+//     leader's MMAs read both halves, so each SM streams half the activation bytes from L2
+//     (the unpaired kernel re-reads the full 256-row X tile per 128 weight rows). Both CTAs'
+//     X bytes and decoder arrivals complete on the leader's barriers; the leader's commits
+//     arrive on both CTAs' barriers (tcgen05.commit multicast); no TMA load is multicast.
 // Warp roles (576 threads): 0 TMA producer, 1 MMA issuer + TMEM owner,
 // 2..9 dequant (two threads per weight row, one per K half of a stage),
 // 10..17 epilogue (thread = output feature n; stores are coalesced along n).
@@ -80,9 +87,14 @@ static_assert(Cfg<MB_GGML_Q4_K>::kSX <= kMaxSX && Cfg<MB_GGML_Q8_0>::kSX <= kMax
                   Cfg<MB_GGML_Q6_K>::kSX <= kMaxSX,
               "A ring must fit below the epilogue staging columns");
 static_assert(1024 + 4 * 32768 + 3 * 128 * 224 + 512 <= 232448, "largest raw ring must fit in shared memory");
-template <int WT>
+// X bytes per stage and CTA: a CTA pair splits the tile's 256 activation rows between its two CTAs.
+template <bool PAIR>
+constexpr uint32_t x_stage_bytes() {
+  return PAIR ? kXStageBytes / 2 : kXStageBytes;
+}
+template <int WT, bool PAIR>
 constexpr size_t smem_bytes() {
-  return 1024 + (size_t)Cfg<WT>::kSX * kXStageBytes + (size_t)Cfg<WT>::kSR * TN * Cfg<WT>::kRawRow + 512;
+  return 1024 + (size_t)Cfg<WT>::kSX * x_stage_bytes<PAIR>() + (size_t)Cfg<WT>::kSR * TN * Cfg<WT>::kRawRow + 512;
 }
 
 struct Prob {  // one GEMM of a (possibly grouped) launch
@@ -369,16 +381,34 @@ MB_DEV void umma_ts_stage4(uint32_t d_tmem, uint32_t a0, uint64_t b0, uint32_t i
       "r"(a0), "l"(b0), "r"(idesc), "r"(accumulate)
       : "memory");
 }
-template <int WT>
+// Same for a CTA pair (issued by the leader): A rows 0-127 come from the leader's TMEM, 128-255 from
+// the peer's at the same address; B rows 0-127 from the leader's shared memory, 128-255 from the
+// peer's at the same offset; each CTA's TMEM receives its own 128 rows of D.
+MB_DEV void umma_ts_stage4_pair(uint32_t d_tmem, uint32_t a0, uint64_t b0, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p, e, t;\n .reg .b32 r, a1, a2, a3;\n .reg .b64 b1, b2, b3;\n"
+      " setp.ne.b32 p, %4, 0;\n setp.eq.b32 t, 0, 0;\n"
+      " add.u32 a1, %1, 8;\n add.u32 a2, %1, 16;\n add.u32 a3, %1, 24;\n"
+      " add.u64 b1, %2, 2;\n add.u64 b2, %2, 4;\n add.u64 b3, %2, 6;\n"
+      " elect.sync r|e, 0xffffffff;\n"
+      " @e tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, p;\n"
+      " @e tcgen05.mma.cta_group::2.kind::f16 [%0], [a1], b1, %3, t;\n"
+      " @e tcgen05.mma.cta_group::2.kind::f16 [%0], [a2], b2, %3, t;\n"
+      " @e tcgen05.mma.cta_group::2.kind::f16 [%0], [a3], b3, %3, t;\n}\n" ::"r"(d_tmem),
+      "r"(a0), "l"(b0), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+template <int WT, bool PAIR>
 __global__ void __launch_bounds__(kThreads, 1)
     k_qgemm(const __grid_constant__ CUtensorMap tm_x0, const __grid_constant__ CUtensorMap tm_w0,
             const __grid_constant__ CUtensorMap tm_x1, const __grid_constant__ CUtensorMap tm_w1, const Params p) {
   constexpr int kSR = Cfg<WT>::kSR, SX = Cfg<WT>::kSX, kSPC = Cfg<WT>::kSPC;
   constexpr uint32_t kRawStage = TN * Cfg<WT>::kRawRow;
+  constexpr uint32_t kXS = x_stage_bytes<PAIR>();
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-  uint8_t* xs = smem;                                    // SX x 32 KB, 1024-aligned
-  uint8_t* rs = smem + SX * kXStageBytes;                // kSR raw stages
+  uint8_t* xs = smem;                                    // SX x (32 or 16) KB, 1024-aligned
+  uint8_t* rs = smem + SX * kXS;                         // kSR raw stages
   uint64_t* bars = (uint64_t*)(rs + kSR * kRawStage);
   uint64_t* full = bars;         // X landed (TMA tx) and A decoded (kDW arrivals)
   uint64_t* empty = full + SX;    // the stage's MMAs completed (one commit)
@@ -391,6 +421,22 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_tiles = p.n_tiles;
+  // CTA pair (PAIR): the cluster's two CTAs share one 256 x 256 tile; rank r decodes weight rows
+  // [128 r, 128 r + 128) and loads activation rows [128 r, 128 r + 128); the leader (rank 0) issues
+  // the pair's MMAs. Tiles are walked per cluster.
+  uint32_t rank = 0;
+  if constexpr (PAIR) {
+    if (cluster_size() != 2) {  // launched without the cluster shape this code needs
+      if (threadIdx.x == 0) atomicExch(p.status, kDevTimeoutGemm);
+      return;
+    }
+    rank = cluster_rank();
+  }
+  const bool leader = rank == 0;
+  const int tile_first = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
+  const int tile_step = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
+  constexpr int kTileN = PAIR ? 2 * TN : TN;  // weight rows per tile
+  constexpr uint32_t kPairArrivals = PAIR ? 2 : 1;
 #ifdef MB_TRACE
   unsigned long long tr_[16] = {};
   const long long t_start_ = clock64();
@@ -409,16 +455,22 @@ __global__ void __launch_bounds__(kThreads, 1)
   (void)nks;
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < SX; i++) { mbar_init(&full[i], 1 + kDW); mbar_init(&empty[i], 1); }
+    // in a pair only the leader's full / acc_empty are waited on; they count both CTAs' arrivals
+    for (int i = 0; i < SX; i++) { mbar_init(&full[i], 1 + kPairArrivals * kDW); mbar_init(&empty[i], 1); }
     for (int i = 0; i < kSR; i++) { mbar_init(&r_full[i], 1); mbar_init(&r_empty[i], kDW); }
     mbar_init(acc_full, 1);
-    mbar_init(acc_empty, kEW);
+    mbar_init(acc_empty, kPairArrivals * kEW);
     *abort_flag = 0;
     fence_mbar_init();
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, kTmemCols);
-    tmem_relinquish();
+    if constexpr (PAIR) {
+      tmem_alloc_pair(tmem_slot, kTmemCols);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(tmem_slot, kTmemCols);
+      tmem_relinquish();
+    }
   }
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tm_x0);
@@ -430,6 +482,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   tc_fence_before();
   __syncthreads();
+  if constexpr (PAIR) cluster_sync();  // the peer's barriers are initialised before any remote arrive
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
@@ -440,26 +493,30 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       uint32_t it = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x) {
+      for (int tile = tile_first; tile < n_tiles && ok; tile += tile_step) {
         TILE_SETUP(tile);
-        const int m0 = (lt_ % P.tiles_m) * TM;
+        const int m0 = (lt_ % P.tiles_m) * TM + (int)rank * (TM / 2);
         for (int ks = 0; ks < nks && ok; ks++, it++) {
           const uint32_t sx = it % SX, px = (it / SX) & 1;
           if (!(ok = TW(0, mbar_wait(&empty[sx], px ^ 1, abort_flag, p.status, kDevTimeoutGemm)))) break;
-          if (ABL(2)) {
+          if constexpr (PAIR) {
+            // both halves complete on the leader's barrier, which expects the pair's bytes
+            if (leader) mbar_expect_tx(&full[sx], 2 * kXS);
+            tma_load_2d_pair(xs + sx * kXS, tm_x, smem_in_cta(&full[sx], 0), ks * BK, m0);
+          } else if (ABL(2)) {
             mbar_arrive(&full[sx]);
           } else {
-            mbar_expect_tx(&full[sx], kXStageBytes);
-            tma_load_2d(xs + sx * kXStageBytes, tm_x, &full[sx], ks * BK, m0);
+            mbar_expect_tx(&full[sx], kXS);
+            tma_load_2d(xs + sx * kXS, tm_x, &full[sx], ks * BK, m0);
           }
         }
       }
     } else if (lane == 1) {
       uint32_t ic = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x) {
+      for (int tile = tile_first; tile < n_tiles && ok; tile += tile_step) {
         TILE_SETUP(tile);
-        const int n0 = (lt_ / P.tiles_m) * TN;
+        const int n0 = (lt_ / P.tiles_m) * kTileN + (int)rank * TN;
         for (int ks = 0; ks < nks && ok; ks += kSPC) {  // one raw chunk (kSPC stages) per 128-row block
           const uint32_t sr = ic % kSR, pr = (ic / kSR) & 1;
           ic++;
@@ -481,17 +538,21 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else if (warp == 1) {
-    // ------------------------------------------------ MMA issuer
-    constexpr uint32_t idesc = idesc_bf16(TN, TM);
+    // ------------------------------------------------ MMA issuer (the leader's, in a pair)
+    constexpr uint32_t idesc = idesc_bf16(PAIR ? 2 * TN : TN, TM);
     uint32_t it = 0, tcount = 0;
     bool ok = true;
-    for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x, tcount++) {
+    for (int tile = tile_first; tile < n_tiles && ok && leader; tile += tile_step, tcount++) {
       TILE_SETUP(tile);
-      if (!(ok = TW(2, mbar_wait(acc_empty, (tcount & 1) ^ 1, abort_flag, p.status, kDevTimeoutGemm)))) break;
+      if (!(ok = TW(2, PAIR ? mbar_wait_cl(acc_empty, (tcount & 1) ^ 1, abort_flag, p.status, kDevTimeoutGemm)
+                            : mbar_wait(acc_empty, (tcount & 1) ^ 1, abort_flag, p.status, kDevTimeoutGemm))))
+        break;
       tc_fence_after();
       for (int ks = 0; ks < nks; ks++, it++) {
         const uint32_t sx = it % SX, px = (it / SX) & 1, sa = sx;
-        if (!(ok = TW(ks < 4 ? 12 : 13, mbar_wait(&full[sx], px, abort_flag, p.status, kDevTimeoutGemm)))) break;
+        if (!(ok = TW(ks < 4 ? 12 : 13, PAIR ? mbar_wait_cl(&full[sx], px, abort_flag, p.status, kDevTimeoutGemm)
+                                             : mbar_wait(&full[sx], px, abort_flag, p.status, kDevTimeoutGemm))))
+          break;
         tc_fence_after();
 #ifdef MB_TRACE
         const long long ti0 = clock64();
@@ -502,11 +563,16 @@ __global__ void __launch_bounds__(kThreads, 1)
           // extra cycles while the decoder warps of its SM sub-partition keep that sub-partition
           // busy. Measured against a lane-0-only branch issuing one MMA per call (~537 issue
           // cycles per 512-cycle stage): one election per MMA +8-12 %, one per stage +2 % more.
-          const uint32_t xaddr = smem_u32(xs + sx * kXStageBytes);
+          const uint32_t xaddr = smem_u32(xs + sx * kXS);
           // the descriptor's address field is bits 0-13 (bytes >> 4): +32 bytes per K16 step = +2
           static_assert(BK / 16 == 4, "one stage = four K16 MMAs");
-          umma_ts_stage4(tmem, tmem + kTmemA + sa * 32, sw128_desc(xaddr, 16, 1024), idesc, ks != 0);
-          if (lane == 0) umma_commit(&empty[sx]);
+          if constexpr (PAIR) {
+            umma_ts_stage4_pair(tmem, tmem + kTmemA + sa * 32, sw128_desc(xaddr, 16, 1024), idesc, ks != 0);
+            if (lane == 0) umma_commit_pair(&empty[sx], 3);
+          } else {
+            umma_ts_stage4(tmem, tmem + kTmemA + sa * 32, sw128_desc(xaddr, 16, 1024), idesc, ks != 0);
+            if (lane == 0) umma_commit(&empty[sx]);
+          }
         }
         __syncwarp();
 #ifdef MB_TRACE
@@ -514,7 +580,12 @@ __global__ void __launch_bounds__(kThreads, 1)
 #endif
       }
       if (!ok) break;
-      if (lane == 0) umma_commit(acc_full);
+      if (lane == 0) {
+        if constexpr (PAIR)
+          umma_commit_pair(acc_full, 3);
+        else
+          umma_commit(acc_full);
+      }
       __syncwarp();
     }
 #ifdef MB_TRACE
@@ -528,7 +599,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t lane_addr = (uint32_t)(q * 32) << 16;
     uint32_t it = 0, ic = 0;
     bool ok = true;
-    for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x) {
+    for (int tile = tile_first; tile < n_tiles && ok; tile += tile_step) {
       TILE_SETUP(tile);
       for (int kc = 0; kc < nks / kSPC && ok; kc++, ic++) {
         const uint32_t sr = ic % kSR, pr = (ic / kSR) & 1;
@@ -617,7 +688,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive(&full[sa]);
+          if (lane == 0) {
+            if constexpr (PAIR)
+              mbar_arrive_cluster(smem_in_cta(&full[sa], 0));
+            else
+              mbar_arrive(&full[sa]);
+          }
 #ifdef MB_TRACE
           tr_[15] += (unsigned long long)(clock64() - td1);
 #endif
@@ -626,15 +702,22 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ------------------------------------------------ epilogue (thread = output feature n)
+    // both CTAs of a pair release the accumulator on the leader's barrier
+    auto release_acc = [](uint64_t* bar) {
+      if constexpr (PAIR)
+        mbar_arrive_cluster(smem_in_cta(bar, 0));
+      else
+        mbar_arrive(bar);
+    };
     const int q = warp & 3;
     const int ch = (warp - 2 - kDW) >> 2;  // which 128 of the tile's 256 activation rows
     const uint32_t lane_addr = (uint32_t)(q * 32) << 16;
     uint32_t tcount = 0;
     bool ok = true;
-    for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x, tcount++) {
+    for (int tile = tile_first; tile < n_tiles && ok; tile += tile_step, tcount++) {
       TILE_SETUP(tile);
       const GemmEpilogue& e = P.epi;
-      const int m0 = (lt_ % P.tiles_m) * TM + ch * 128, n0 = (lt_ / P.tiles_m) * TN;
+      const int m0 = (lt_ % P.tiles_m) * TM + ch * 128, n0 = (lt_ / P.tiles_m) * kTileN + (int)rank * TN;
       const int n = n0 + q * 32 + lane;
       // per-feature epilogue operands are loaded before the accumulator wait (off the drain path)
       const bool nvalid = n < P.N;
@@ -652,7 +735,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool fast_bf16 = e.out_bf16 && e.kind != MB_EPI_GATE_RESIDUAL && (P.N & 1) == 0;
       if (ABL(16)) {
         __syncwarp();
-        if (lane == 0) mbar_arrive(acc_empty);
+        if (lane == 0) release_acc(acc_empty);
         DRAIN_DONE();
       } else if (fast_bf16) {
         // bf16 output: pack the warp's 128 accumulator columns to bf16 pairs (rows m, m+1 of
@@ -700,7 +783,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #endif
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(acc_empty);
+        if (lane == 0) release_acc(acc_empty);
         DRAIN_DONE();
         const bool odd = lane & 1;
         const int ncol = n - (odd ? 1 : 0);  // even feature of the pair this lane writes
@@ -738,7 +821,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_wait_st();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(acc_empty);
+        if (lane == 0) release_acc(acc_empty);
         DRAIN_DONE();
         // y usually aliases res: issue a batch of 16 residual loads before any store so their
         // latencies overlap (the compiler cannot reorder loads past aliasing stores). The TMEM
@@ -775,7 +858,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (c == 3) {  // the accumulator is free as soon as the last columns are in registers
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(acc_empty);
+            if (lane == 0) release_acc(acc_empty);
         DRAIN_DONE();
           }
           const int mb = m0 + c * 32;
@@ -810,19 +893,25 @@ __global__ void __launch_bounds__(kThreads, 1)
 #endif
   tc_fence_before();
   __syncthreads();
+  // a pair's CTAs stay resident until neither can still be reached by the other's arrivals,
+  // commits or MMA operand reads
+  if constexpr (PAIR) cluster_sync();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, kTmemCols);
+    if constexpr (PAIR)
+      tmem_dealloc_pair(tmem, kTmemCols);
+    else
+      tmem_dealloc(tmem, kTmemCols);
   }
 }
 
 int g_gemm_ablate = 0;
 unsigned long long* g_gemm_trace = nullptr;
 
-template <int WT>
+template <int WT, bool PAIR>
 bool make_maps(const mb_weight* w, const void* x, int64_t M, int64_t ldx, CUtensorMap* tx, CUtensorMap* tw) {
   if (!make_tmap_2d(tx, x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)w->n_cols, (uint64_t)M, (uint64_t)ldx * 2, BK,
-                    TM, CU_TENSOR_MAP_SWIZZLE_128B))
+                    PAIR ? TM / 2 : TM, CU_TENSOR_MAP_SWIZZLE_128B))
     return false;
   const uint64_t rb = (uint64_t)w->row_bytes, nr = (uint64_t)w->n_rows;
   const uint32_t box = (uint32_t)Cfg<WT>::kRawRow;
@@ -832,20 +921,32 @@ bool make_maps(const mb_weight* w, const void* x, int64_t M, int64_t ldx, CUtens
   return make_tmap_2d(tw, w->dev, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, rb, nr, rb, box, TN, CU_TENSOR_MAP_SWIZZLE_NONE);
 }
 
+// 1 (default): CTA pairs (cta_group::2); 0: one CTA per tile (MB_GEMM_PAIR=0). Both give
+// bit-identical results. Read once per process.
+int gemm_pair_mode() {
+  static int mode = -1;
+  if (mode < 0) {
+    const char* e = getenv("MB_GEMM_PAIR");
+    mode = (e && e[0] == '0') ? 0 : 1;
+  }
+  return mode;
+}
+
 // Launches one persistent kernel over the tiles of n (1 or 2) GEMMs with the same weight type.
-template <int WT>
+template <int WT, bool PAIR>
 cudaError_t launch_t(int n, const GemmProblem* g, cudaStream_t st) {
+  constexpr int kTileN = PAIR ? 2 * TN : TN;
   CUtensorMap tx[2], tw[2];
   Params p;
   int tiles = 0;
   for (int i = 0; i < n; i++) {
-    if (!make_maps<WT>(g[i].w, g[i].x, g[i].M, g[i].ldx, &tx[i], &tw[i])) return cudaErrorInvalidValue;
+    if (!make_maps<WT, PAIR>(g[i].w, g[i].x, g[i].M, g[i].ldx, &tx[i], &tw[i])) return cudaErrorInvalidValue;
     Prob& P = p.pr[i];
     P.M = (int)g[i].M;
     P.N = (int)g[i].w->n_rows;
     P.K = (int)g[i].w->n_cols;
     P.tiles_m = (int)((g[i].M + TM - 1) / TM);
-    P.tiles_n = (int)((g[i].w->n_rows + TN - 1) / TN);
+    P.tiles_n = (int)((g[i].w->n_rows + kTileN - 1) / kTileN);
     P.tile0 = tiles;
     P.epi = g[i].epi;
     tiles += P.tiles_m * P.tiles_n;
@@ -860,18 +961,46 @@ cudaError_t launch_t(int n, const GemmProblem* g, cudaStream_t st) {
   p.status = device_status_ptr();
   p.ablate = g_gemm_ablate;
   p.trace = g_gemm_trace;
-  const int grid = tiles < num_sms() ? tiles : num_sms();
-  constexpr size_t smem = smem_bytes<WT>();
-  static int attr_done[64];  // per template instance and device
+  constexpr size_t smem = smem_bytes<WT, PAIR>();
+  static int attr_done[64];  // per template instance and device: 1 + the co-resident cluster count
   int dev = 0;
   cudaGetDevice(&dev);
-  if (!attr_done[dev & 63]) {
-    cudaError_t e = cudaFuncSetAttribute(k_qgemm<WT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return e;
-    attr_done[dev & 63] = 1;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  if (PAIR) {
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
   }
-  k_qgemm<WT><<<grid, kThreads, smem, st>>>(tx[0], tw[0], tx[1], tw[1], p);
-  return cudaGetLastError();
+  if (!attr_done[dev & 63]) {
+    cudaError_t e = cudaFuncSetAttribute(k_qgemm<WT, PAIR>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    int slots = num_sms();
+    if (PAIR) {  // pairs that fit at once (a GPC with an odd SM count leaves one SM out)
+      int nc = 0;
+      cfg.gridDim = dim3((unsigned)num_sms() & ~1u);
+      e = cudaOccupancyMaxActiveClusters(&nc, k_qgemm<WT, PAIR>, &cfg);
+      if (e != cudaSuccess) return e;
+      if (nc < 1) return cudaErrorInvalidConfiguration;
+      slots = nc;
+    }
+    attr_done[dev & 63] = 1 + slots;
+  }
+  const int slots = attr_done[dev & 63] - 1;
+  const int units = tiles < slots ? tiles : slots;  // CTAs, or CTA pairs
+  cfg.gridDim = dim3((unsigned)(PAIR ? 2 * units : units));
+  return cudaLaunchKernelEx(&cfg, k_qgemm<WT, PAIR>, tx[0], tw[0], tx[1], tw[1], p);
+}
+
+template <int WT>
+cudaError_t launch_w(int n, const GemmProblem* g, cudaStream_t st) {
+  return gemm_pair_mode() ? launch_t<WT, true>(n, g, st) : launch_t<WT, false>(n, g, st);
 }
 
 }  // namespace gemm
@@ -889,15 +1018,15 @@ cudaError_t launch_qgemm_group(int n, const GemmProblem* g, cudaStream_t st) {
   for (int i = 0; i < n; i++)
     if (g[i].M <= 0 || g[i].w->type != g[0].w->type) return cudaErrorInvalidValue;
   switch (g[0].w->type) {
-    case MB_GGML_Q4_K: return gemm::launch_t<MB_GGML_Q4_K>(n, g, st);
-    case MB_GGML_Q8_0: return gemm::launch_t<MB_GGML_Q8_0>(n, g, st);
-    case MB_GGML_BF16: return gemm::launch_t<MB_GGML_BF16>(n, g, st);
-    case MB_GGML_Q4_0: return gemm::launch_t<MB_GGML_Q4_0>(n, g, st);
-    case MB_GGML_Q4_1: return gemm::launch_t<MB_GGML_Q4_1>(n, g, st);
-    case MB_GGML_Q5_0: return gemm::launch_t<MB_GGML_Q5_0>(n, g, st);
-    case MB_GGML_Q5_1: return gemm::launch_t<MB_GGML_Q5_1>(n, g, st);
-    case MB_GGML_Q5_K: return gemm::launch_t<MB_GGML_Q5_K>(n, g, st);
-    case MB_GGML_Q6_K: return gemm::launch_t<MB_GGML_Q6_K>(n, g, st);
+    case MB_GGML_Q4_K: return gemm::launch_w<MB_GGML_Q4_K>(n, g, st);
+    case MB_GGML_Q8_0: return gemm::launch_w<MB_GGML_Q8_0>(n, g, st);
+    case MB_GGML_BF16: return gemm::launch_w<MB_GGML_BF16>(n, g, st);
+    case MB_GGML_Q4_0: return gemm::launch_w<MB_GGML_Q4_0>(n, g, st);
+    case MB_GGML_Q4_1: return gemm::launch_w<MB_GGML_Q4_1>(n, g, st);
+    case MB_GGML_Q5_0: return gemm::launch_w<MB_GGML_Q5_0>(n, g, st);
+    case MB_GGML_Q5_1: return gemm::launch_w<MB_GGML_Q5_1>(n, g, st);
+    case MB_GGML_Q5_K: return gemm::launch_w<MB_GGML_Q5_K>(n, g, st);
+    case MB_GGML_Q6_K: return gemm::launch_w<MB_GGML_Q6_K>(n, g, st);
     default: return cudaErrorInvalidValue;
   }
 }
