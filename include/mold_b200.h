@@ -128,9 +128,9 @@ MB_API mb_status mb_qlinear(const mb_weight* w, const void* x, int x_dtype, int6
                      const float* residual, int64_t ldr, void* stream);
 
 /* Same as mb_qlinear with an f32 x, but allocates nothing. No counterpart in the
- * reference: it is for callers that cannot let the library call cudaMalloc (code
- * running during CUDA-graph capture, callers whose device memory comes from their
- * own pool or arena, hosts that forbid allocation after start-up). The bf16 copy of
+ * reference: it is for callers that cannot let the library call cudaMalloc (callers
+ * whose device memory comes from their own pool or arena, hosts that forbid
+ * allocation after start-up). The bf16 copy of
  * x is staged in a fixed 8 MiB array in the library's device image (M * K must be
  * <= 4,194,304; larger inputs are rejected with MB_ERR_INVALID); every GPU that
  * loads the library holds that array until exit. mb_init must have been called on

@@ -1,10 +1,10 @@
 // mb_qlinear_f32_static: the f32-input quantized linear without any device allocation.
 //
 // mb_qlinear with an f32 x first casts x to bf16 into a per-device scratch buffer
-// that the library grows with cudaMalloc. Some callers cannot allow that: code
-// that runs while a CUDA graph is being captured, callers whose device memory is
-// handed out by their own pool or arena and must not be fragmented or grown behind
-// their back, and hosts that forbid allocation after start-up. This entry point
+// that the library grows with cudaMalloc. Some callers cannot allow that: callers
+// whose device memory is handed out by their own pool or arena and must not be
+// fragmented or grown behind their back, and hosts that forbid allocation after
+// start-up (a fixed memory budget per process, measured once at start). This entry point
 // stages the bf16 copy of x in a fixed array that lives in the library's own
 // device image instead, so it never calls cudaMalloc, cudaFree or any allocating
 // routine.

@@ -1,8 +1,7 @@
 """mb_qlinear_f32_static: the f32-input quantized linear that allocates nothing.
 
-Callers that cannot let the library call cudaMalloc (code running during CUDA-graph
-capture, callers that hand out device memory from their own pool, hosts that forbid
-allocation after start-up) use this entry point; it stages the bf16 copy of x in a
+Callers that cannot let the library call cudaMalloc (callers that hand out device
+memory from their own pool, hosts that forbid allocation after start-up) use this entry point; it stages the bf16 copy of x in a
 fixed 8 MiB array compiled into the library instead of a grown scratch buffer.
 Its results must equal mb_qlinear's on the same f32 input. This file is collected
 last so that a run stopping at the first failure has run every other test first.
