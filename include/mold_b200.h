@@ -122,7 +122,12 @@ MB_API mb_status mb_dequant(const mb_weight* w, void* out, int out_dtype, void* 
  * must be f32, gate is f32 [N] and residual f32 [M, ldr] (may equal y).
  * Replaces `QMatMul::forward` (candle, called through quantized_nn::Linear inside
  * flux::quantized_model; flux/transformer.rs:64-72) and `QwenLinear::forward`
- * (qwen_image/quantized_transformer.rs:54-77). */
+ * (qwen_image/quantized_transformer.rs:54-77).
+ * Scratch: with an f32 x the bf16 copy goes to a per-device scratch buffer that the
+ * library owns and shares with mb_qgemv. It grows on demand; growing it frees the old
+ * buffer after a cudaDeviceSynchronize (so that call is not asynchronous) and allocates
+ * a larger one. Calls on one device from several host threads or streams whose work
+ * overlaps race on this buffer; serialise them, or pass bf16 x (no scratch). */
 MB_API mb_status mb_qlinear(const mb_weight* w, const void* x, int x_dtype, int64_t M, int64_t ldx, void* y, int y_dtype,
                      int64_t ldy, const float* bias, int epilogue, int64_t gelu_from, const float* gate,
                      const float* residual, int64_t ldr, void* stream);
@@ -143,7 +148,10 @@ MB_API mb_status mb_qlinear_f32_static(const mb_weight* w, const float* x, int64
                                        void* stream);
 
 /* K3. Quantized GEMV for the modulation vectors: y[N] = W silu?(x)[K] + bias.
- * Replaces Modulation1/2::forward's silu(vec)->Linear (flux/offload.rs:117-156). */
+ * Replaces Modulation1/2::forward's silu(vec)->Linear (flux/offload.rs:117-156).
+ * Stages silu(x) in the per-device scratch buffer that mb_qlinear's f32 path uses
+ * (grown on demand with a device synchronisation; overlapping calls on one device
+ * race on it, as for mb_qlinear). */
 MB_API mb_status mb_qgemv(const mb_weight* w, const float* x, int apply_silu, const float* bias, float* y, void* stream);
 
 /* K5. LayerNorm (no affine, eps 1e-6) + AdaLN modulate: y = LN(x) * (1 + scale) + shift.

@@ -297,6 +297,7 @@ mb_status mb_qlinear(const mb_weight* w, const void* x, int x_dtype, int64_t M, 
   const void* xb = x;
   int64_t ldxb = ldx;
   if (x_dtype == MB_DT_F32) {
+    MB_CHECK(ldx % 4 == 0 && aligned16(x), MB_ERR_INVALID, "f32 x must be 16-byte aligned with ldx % 4 == 0");
     void* s = device_scratch((size_t)M * K * 2);
     MB_CHECK(s || M == 0, MB_ERR_NOMEM, "scratch allocation for the f32->bf16 input failed");
     MB_CUDA(launch_cast_f32_bf16((const float*)x, M, K, ldx, s, K, st));

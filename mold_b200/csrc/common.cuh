@@ -95,41 +95,24 @@ MB_DEV uint32_t smem_in_cta(const void* p, uint32_t rank) {
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
   return r;
 }
-// Arrive on a barrier of another CTA of the cluster. Default semantics (release at CTA scope), as
-// the pair kernels use around tcgen05 fences: the consumer is the pair's tensor core, ordered by
-// tcgen05.fence::before_thread_sync here and ::after_thread_sync at the waiter.
+// Arrive on a barrier of another CTA of the cluster. Default semantics (release at CTA scope).
+// This is enough for the pair kernels because no ordinary load ever reads what the arrival
+// publishes: the peer's decoded weights sit in its TMEM (tcgen05.st completed by
+// tcgen05.wait::st, then tcgen05.fence::before_thread_sync before the arrival) and its X tile
+// arrives by TMA (counted by the barrier's transaction bytes), and the only consumer is the
+// pair's tensor core, whose MMAs the leader issues after its wait and a
+// tcgen05.fence::after_thread_sync. That fence pair orders tcgen05 operations across the
+// barrier; the cluster-scope release would additionally order generic-proxy writes, of which
+// there are none. Measured: .release.cluster arrivals with .acquire.cluster waits halved the
+// GEMM's rate (690 vs 1324+ TFLOP/s on linear1), because each decoder warp stalls on the
+// release once per stage and the decoders are the throughput limit.
 MB_DEV void mbar_arrive_cluster(uint32_t cl_addr) {
-#ifdef MB_PAIR_CLUSTER_SCOPE
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cl_addr) : "memory");
-#else
   asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cl_addr) : "memory");
-#endif
 }
-MB_DEV bool mbar_try_wait_cl(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
-  uint32_t ok;
-  asm volatile(
-      "{\n .reg .pred p;\n mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;\n"
-      " selp.u32 %0, 1, 0, p;\n}\n"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
-      : "memory");
-  return ok != 0;
-}
-// mbar_wait for phases completed by arrivals from the other CTA of a pair.
+// mbar_wait for phases completed by arrivals from the other CTA of a pair (see above for why a
+// CTA-scope acquire suffices).
 MB_DEV bool mbar_wait_cl(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* status, int code) {
-#ifndef MB_PAIR_CLUSTER_SCOPE
   return mbar_wait(bar, parity, abort_flag, status, code);
-#endif
-  long long t0 = clock64();
-  while (true) {
-    if (mbar_try_wait_cl(bar, parity, 20000)) return true;
-    if (*abort_flag) return false;
-    if (clock64() - t0 > kSpinLimitCycles) {
-      *abort_flag = 1;
-      if (status) atomicExch(status, code);
-      return false;
-    }
-  }
 }
 
 // ---------------------------------------------------------------- TMA

@@ -59,12 +59,14 @@ extern "C" mb_status mb_qlinear_f32_static(const mb_weight* w, const float* x, i
            "mb_qlinear_f32_static supports BF16 and the quantized types Q4_0, Q4_1, Q5_0, Q5_1, Q8_0, Q4_K, Q5_K, "
            "Q6_K (got ggml type " + std::to_string(w->type) + ")");
   const int64_t K = w->n_cols, N = w->n_rows;
-  MB_CHECK((size_t)M * (size_t)K <= kStaticElems, MB_ERR_INVALID,
-           "mb_qlinear_f32_static: M * K = " + std::to_string(M * K) + " exceeds the fixed staging buffer of " +
-               std::to_string(kStaticElems) + " values (8 MiB); use mb_qlinear for larger inputs");
-  MB_CHECK(K % 64 == 0, MB_ERR_INVALID, "K must be a multiple of 64");
+  MB_CHECK(K > 0 && K % 64 == 0, MB_ERR_INVALID, "K must be a positive multiple of 64");
+  // Bound M by division so that no product of caller-supplied sizes can wrap.
+  MB_CHECK(M <= (int64_t)(kStaticElems / (size_t)K), MB_ERR_INVALID,
+           "mb_qlinear_f32_static: M = " + std::to_string(M) + " rows of K = " + std::to_string(K) +
+               " exceed the fixed staging buffer of " + std::to_string(kStaticElems) +
+               " values (8 MiB, M * K must be <= that); use mb_qlinear for larger inputs");
   MB_CHECK(w->type == MB_GGML_BF16 || K % 256 == 0, MB_ERR_INVALID, "quantized K must be a multiple of 256");
-  MB_CHECK(N < (1LL << 31), MB_ERR_INVALID, "N must fit in 31 bits");
+  MB_CHECK(M < (1LL << 31) && N < (1LL << 31), MB_ERR_INVALID, "M and N must fit in 31 bits");
   MB_CHECK(ldx >= K && ldx % 4 == 0 && ((uintptr_t)x & 15) == 0, MB_ERR_INVALID,
            "x must be 16-byte aligned with ldx >= K and ldx % 4 == 0");
   MB_CHECK(ldy >= N, MB_ERR_INVALID, "ldy must be >= N");

@@ -1,4 +1,5 @@
 """GPU parity of the single kernels against the CPU oracle, through the C ABI."""
+import ctypes
 import math
 
 import numpy as np
@@ -8,6 +9,7 @@ import torch
 import mold_b200 as mb
 import oracle
 from oracle import flux_ref as F
+from mold_b200 import _lib
 from tests.conftest import rel_l2
 
 pytestmark = pytest.mark.gpu
@@ -124,6 +126,21 @@ def test_qlinear_f32_input(cuda):
     y = w.forward(torch.from_numpy(x).to(cuda))
     assert y.dtype == torch.float32
     assert rel_l2(y.cpu().numpy(), ref) < 1e-2
+
+
+def test_qlinear_f32_unaligned_rejected(cuda):
+    """An f32 x that is not 16-byte aligned, or whose row stride is not a multiple of 4,
+    is rejected with MB_ERR_INVALID before any kernel runs."""
+    N, K, M = 256, 512, 8
+    w, _ = qmat(oracle.randn(19, (N, K), 0.02), oracle.GGML_Q4_K)
+    buf = torch.zeros(M * (K + 4) + 4, device=cuda)
+    y = torch.empty((M, N), device=cuda)
+    P = ctypes.c_void_p
+    for off, ld in ((1, K), (0, K + 1)):  # 4-byte offset base; odd row stride
+        rc = mb.lib().mb_qlinear(w.handle, P(buf.data_ptr() + 4 * off), _lib.DT_F32, M, ld, P(y.data_ptr()),
+                                 _lib.DT_F32, N, None, 0, 0, None, None, 0, None)
+        assert rc == _lib.MB_ERR_INVALID, (off, ld)
+        assert b"16-byte aligned" in mb.lib().mb_last_error()
 
 
 # ------------------------------------------------------------------ K3 GEMV
