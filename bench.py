@@ -52,6 +52,11 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline sample")
     ap.add_argument("--kernels-only", action="store_true", help="only the standalone kernel timings (profiling)")
+    ap.add_argument("--kernel", default="gemm,attention",
+                    help="with --kernels-only: comma list of gemm, attention, gemv, ln_modulate, qk_norm_rope, "
+                         "dequant (the HBM-bound ones at the FLUX step's shapes, L2 flushed between launches)")
+    ap.add_argument("--sweep", action="store_true",
+                    help="BASELINE config 2: the Q4_K dequant-GEMM over the ten FLUX linear shapes, one JSON line each")
     return ap.parse_args()
 
 
@@ -215,7 +220,7 @@ def build_flux(quant, device, seed=0):
     keep = {}
     gtype, qfn, _ = quantizer(quant)
     for i, (name, shape) in enumerate(mb.flux.tensor_specs(cfg)):
-        g.manual_seed(seed * 1000003 + i)
+        g.manual_seed(WEIGHT_SALT + seed * 1000003 + i)
         if len(shape) == 2:
             x = torch.randn(shape, generator=g, device=f"cuda:{device}") * 0.02
             if shape[1] % 256 == 0:
@@ -250,7 +255,7 @@ def build_qwen(quant, device, seed=0):
     keep = {}
     gtype, qfn, _ = quantizer(quant)
     for i, (name, shape) in enumerate(mb.qwen.tensor_specs(cfg)):
-        g.manual_seed(seed * 1000003 + i)
+        g.manual_seed(WEIGHT_SALT + seed * 1000003 + i)
         x = torch.randn(shape, generator=g, device=f"cuda:{device}") * 0.02
         if len(shape) == 2:
             if shape[1] % 256 == 0:
@@ -388,10 +393,7 @@ def time_gemm(raw, gtype, shape, M, device, reps=20):
     import mold_b200 as mb
     st = torch.cuda.current_stream()
     N, K = shape
-    h = ctypes.c_void_p()
-    mb._lib.check(mb.lib().mb_weight_create(gtype, N, K, ctypes.c_void_p(raw.data_ptr()), raw.numel(), 1,
-                                            ctypes.byref(h)))
-    w = mb.QMatMul(h, N, K, gtype, device)
+    w = mb.QMatMul.from_device_bytes(raw, gtype, N, K, device)
     x = torch.randn((M, K), device=f"cuda:{device}").bfloat16()
     y = torch.empty((M, N), device=f"cuda:{device}", dtype=torch.bfloat16)
     for _ in range(3):
@@ -432,6 +434,81 @@ def time_attention(L, H, device, reps=20):
     return {"shape": [H, L, L, 128], "ms": ams, "tflops": 4.0 * L * L * 128 * H / ams / 1e9}
 
 
+def _events_ms(fn, reps, flush, st):
+    """Median CUDA-event time of fn() on stream st over `reps` launches, each preceded (outside the
+    timed pair of events) by a write of `flush` (256 MB, larger than L2)."""
+    import torch
+    for _ in range(3):
+        fn()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(reps)]
+    for e0, e1 in ev:
+        flush.fill_(1.0)
+        e0.record(st)
+        fn()
+        e1.record(st)
+    torch.cuda.synchronize()
+    return statistics.median(e0.elapsed_time(e1) for e0, e1 in ev)
+
+
+def time_hbm_kernels(want, raw, gtype, qfn, device, peaks, reps=10):
+    """The HBM-bound kernels alone at the FLUX step's shapes, from a cold L2, with their
+    algorithmic bytes (every input byte read once, every output byte written once):
+      gemv          mb_qgemv over 264,192 x 3072 rows (a quarter of the step's 1,056,768
+                    modulation rows; 456 MB in Q4_K), f32 x, silu, bias
+      ln_modulate   4608 x 3072 f32 in -> bf16 out (+ 2 x 3072 f32 shift/scale)
+      qk_norm_rope  4608 x 9216 bf16 qkv in -> q, k, v bf16 [24, 4608, 128] out, + the RoPE table
+      dequant       the linear1 weight (21504 x 3072, GGUF) -> bf16"""
+    import torch
+    import mold_b200 as mb
+    dev = f"cuda:{device}"
+    st = torch.cuda.current_stream()
+    flush = torch.empty(64 << 20, dtype=torch.float32, device=dev)
+    out = {}
+    g = torch.Generator(device=dev).manual_seed(11)
+    hbm = peaks["hbm_gbs"]
+
+    def rec(name, ms, nbytes, shape):
+        out[name] = {"shape": shape, "ms": ms, "bytes": nbytes, "gbs": nbytes / ms / 1e6,
+                     "frac_of_hbm": nbytes / ms / 1e6 / hbm}
+
+    if "gemv" in want:
+        N, K = 264192, 3072
+        parts = [qfn(torch.randn((N // 8, K), generator=g, device=dev) * 0.02) for _ in range(8)]
+        wr = torch.cat(parts)
+        del parts
+        w = mb.QMatMul.from_device_bytes(wr, gtype, N, K, device)
+        del wr
+        x = torch.randn(K, generator=g, device=dev)
+        b = torch.randn(N, generator=g, device=dev) * 0.02
+        ms = _events_ms(lambda: mb.qgemv(w, x, True, b), reps, flush, st)
+        rec("gemv", ms, N * mb.ops.row_bytes(gtype, K) + 4 * (K + 2 * N), [N, K])
+        del w
+    L, C = L_TXT + L_IMG, 3072
+    if "ln_modulate" in want:
+        x = torch.randn((L, C), generator=g, device=dev)
+        sh, sc = torch.randn(C, generator=g, device=dev), torch.randn(C, generator=g, device=dev)
+        ms = _events_ms(lambda: mb.ln_modulate(x, sh, sc), reps, flush, st)
+        rec("ln_modulate", ms, L * C * 6 + 8 * C, [L, C])
+    if "qk_norm_rope" in want:
+        qkv = torch.randn((L, 3 * C), generator=g, device=dev).bfloat16()
+        qs, ks = torch.ones(128, device=dev), torch.ones(128, device=dev)
+        pe = mb.rope_table(torch.cat([mb.sampling.txt_ids(L_TXT, device=dev),
+                                      mb.sampling.img_ids(LAT_H // 2, LAT_W // 2, device=dev)]))
+        q, k_, v = (torch.empty((24, L, 128), dtype=torch.bfloat16, device=dev) for _ in range(3))
+        ms = _events_ms(lambda: mb.qk_norm_rope(qkv, 24, qs, ks, pe, q=q, k=k_, v=v), reps, flush, st)
+        rec("qk_norm_rope", ms, L * 3 * C * 2 * 2 + pe.numel() * 4, [L, 3 * C])
+    if "dequant" in want:
+        N, K = 3 * 3072 + 12288, 3072
+        w = mb.QMatMul.from_device_bytes(raw, gtype, N, K, device)
+        o = torch.empty((N, K), dtype=torch.bfloat16, device=dev)
+        ms = _events_ms(lambda: mb.lib().mb_dequant(w.handle, ctypes.c_void_p(o.data_ptr()), mb.DT_BF16,
+                                                   ctypes.c_void_p(st.cuda_stream)), reps, flush, st)
+        rec("dequant", ms, raw.numel() + N * K * 2, [N, K])
+    if mb.device_status() != 0:
+        raise RuntimeError("a kernel reported a bounded-wait timeout")
+    return out
+
+
 def time_kernels(keep, device, peaks, reps=20):
     """Standalone CUDA-event timings of the dominant FLUX kernels on the launching stream."""
     raw, gtype, shape = keep["linear1"]
@@ -461,8 +538,12 @@ def phys_gpu(local):
 
 # ------------------------------------------------------------------ replica plumbing (one image per GPU)
 def image_seed(rank):
-    """Each rank denoises its own image: seed = rank (offset so it never equals the weight seed)."""
-    return 1000 + rank
+    """Each rank denoises its own image: seed = rank, so 8 GPUs run seeds 0-7.
+    The weights' generator streams are salted (WEIGHT_SALT) so no latent repeats a weight stream."""
+    return rank
+
+
+WEIGHT_SALT = 0x5EED0000
 
 
 def max_over_ranks(value, world, device):
@@ -478,6 +559,54 @@ def max_over_ranks(value, world, device):
 def whole_job_rate(units_per_rank, world, ms_max):
     """Units of all ranks per second, timed by the slowest rank (weak scaling)."""
     return world * units_per_rank / (ms_max / 1e3)
+
+
+# ------------------------------------------------------------------ config 2: GEMM sweep
+SWEEP_M = (1536, 4608)
+SWEEP_KN = (("qkv", 3072, 9216), ("mlp_in", 3072, 12288), ("mlp_out", 12288, 3072),
+            ("single_proj_out", 15360, 3072), ("attn_out", 3072, 3072))
+
+
+def sweep(args, local, peaks, reps=10):
+    """Q4_K dequant-GEMM over M x (K->N) of BASELINE config 2 (weights quantized from N(0, 0.02),
+    bf16 N(0, 1) activations, seed 0). Each launch is timed alone with CUDA events on the launching
+    stream after 3 warm-ups; a 256 MB buffer is written between launches so that every launch reads
+    its weight and activations from HBM (L2 flushed), and the median of `reps` launches is kept."""
+    import torch
+    import mold_b200 as mb
+    dev = f"cuda:{local}"
+    st = torch.cuda.current_stream()
+    flush = torch.empty(64 << 20, dtype=torch.float32, device=dev)
+    gtype, qfn, _ = quantizer(args.quant)
+    g = torch.Generator(device=dev)
+    for name, K, N in SWEEP_KN:
+        g.manual_seed(WEIGHT_SALT + K * 7 + N)
+        raw = qfn(torch.randn((N, K), generator=g, device=dev) * 0.02)
+        w = mb.QMatMul.from_device_bytes(raw, gtype, N, K, local)
+        for M in SWEEP_M:
+            x = torch.randn((M, K), generator=g, device=dev).bfloat16()
+            y = torch.empty((M, N), device=dev, dtype=torch.bfloat16)
+            for _ in range(3):
+                w.forward(x, out=y)
+            ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(reps)]
+            for e0, e1 in ev:
+                flush.fill_(1.0)
+                e0.record(st)
+                w.forward(x, out=y)
+                e1.record(st)
+            torch.cuda.synchronize()
+            ms = statistics.median(e0.elapsed_time(e1) for e0, e1 in ev)
+            flops = 2.0 * M * N * K
+            alg = raw.numel() + 2 * M * K + 2 * M * N
+            print(json.dumps({"sweep": "config2_q4k_gemm", "linear": name, "quant": args.quant, "M": M, "K": K,
+                              "N": N, "ms": ms, "tflops": flops / ms / 1e9,
+                              "frac_of_burst": flops / ms / 1e9 / peaks["bf16_tflops"],
+                              "peak": peaks["bf16_tflops"], "peak_source": peaks["source"],
+                              "algorithmic_bytes": alg, "gbs": alg / ms / 1e6, "l2": "flushed between launches"}),
+                  flush=True)
+        del w
+    if mb.device_status() != 0:
+        raise RuntimeError("a kernel reported a bounded-wait timeout")
 
 
 # ------------------------------------------------------------------ main arm
@@ -506,9 +635,21 @@ def main():
         x = torch.randn((3 * 3072 + 12288, 3072), generator=g, device=dev) * 0.02
         gtype, qfn, _ = quantizer(args.quant)
         raw = qfn(x)
-        k = time_kernels({"linear1": (raw, gtype, tuple(x.shape))}, local, peaks, reps=5)
+        del x
+        want = set(args.kernel.split(","))
+        k = {}
+        if "gemm" in want:
+            k["gemm_linear1"] = time_gemm(raw, gtype, (3 * 3072 + 12288, 3072), L_TXT + L_IMG, local, 5)
+        if "attention" in want:
+            k["attention"] = time_attention(L_TXT + L_IMG, 24, local, 5)
+        k.update(time_hbm_kernels(want, raw, gtype, qfn, local, peaks))
         if rank == 0:
             print(json.dumps({"kernels": k}), flush=True)
+        return
+
+    if args.sweep:
+        if rank == 0:
+            sweep(args, local, peaks)
         return
 
     if args.model == "qwen":
@@ -531,7 +672,11 @@ def main():
         return ts + [sched[n % N_SCHEDULE] if n % N_SCHEDULE else 0.0]
 
     # the dominant kernels timed alone first, at burst clocks (their roofline peak is the burst figure)
-    kern = time_kernels(keep, local, peaks) if rank == 0 else None
+    kern = None
+    if rank == 0:
+        kern = time_kernels(keep, local, peaks)
+        kern.update(time_hbm_kernels({"gemv", "ln_modulate", "qk_norm_rope"}, None, None, quantizer(args.quant)[1],
+                                     local, peaks))
     img = img0.clone()
     st = torch.cuda.current_stream()
     # warm-up: first call captures the step graph, then W replays

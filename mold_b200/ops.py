@@ -86,6 +86,16 @@ class QMatMul:
                                      qt.raw.size, 0, ctypes.byref(h)))
         return cls(h, qt.n_rows, qt.n_cols, qt.ggml_type, device)
 
+    @classmethod
+    def from_device_bytes(cls, raw, ggml_type, n_rows, n_cols, device=0):
+        """A weight from GGUF bytes already in device memory (a uint8 CUDA tensor, GGUF layout);
+        the library takes its own copy."""
+        init(device)
+        h = ctypes.c_void_p()
+        check(lib().mb_weight_create(int(ggml_type), n_rows, n_cols, ctypes.c_void_p(raw.data_ptr()), raw.numel(), 1,
+                                     ctypes.byref(h)))
+        return cls(h, n_rows, n_cols, int(ggml_type), device)
+
     def __del__(self):
         h = getattr(self, "_h", None)
         if h is not None and h.value and lib is not None:

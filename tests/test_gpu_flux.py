@@ -53,7 +53,7 @@ def test_tiny_flux_denoise_cosine(cuda):
     W = F.synth_weights(TINY, seed=2, qtype=oracle.GGML_Q4_K)
     m = to_model(TINY, W, 64, 256)
     img, ids, txt, tids, y = inputs(TINY, 32, 8, 8, seed=200)
-    ts = F.get_schedule(6, 64)
+    ts = mb.sampling.get_schedule(6, 64)  # the product's schedule (equal to the oracle's, tests/test_sampling.py)
     ref = F.denoise(W, TINY, img, ids, txt, tids, y, ts, 3.5)
     t = lambda a: torch.from_numpy(a).to(cuda)
     gi = t(img).clone()

@@ -7,6 +7,7 @@ import torch
 
 import bench
 import mold_b200 as mb
+import oracle
 
 pytestmark = pytest.mark.gpu
 
@@ -27,14 +28,21 @@ def test_linear1_full_size(cuda, qt):
     x = torch.randn((M, K), device="cuda", generator=g).bfloat16()
     bias = torch.randn(N, device="cuda", generator=g) * 0.02
     y = w.forward(x, bias=bias, out_dtype=torch.float32)
-    # fp32 reference on the bf16 operands the tensor core sees (the exact decode rounded to bf16)
-    wb = mb.dequantize(w, torch.bfloat16).float()
-    ref = x.float() @ wb.t() + bias
-    err = ((y - ref).norm() / ref.norm()).item()
-    assert err < 1e-4, err
-    # and against the unrounded decode (what the GGML weights mean)
-    ref32 = x.float() @ mb.dequantize(w, torch.float32).t() + bias
-    assert ((y - ref32).norm() / ref32.norm()).item() < 4e-3
+    # the oracle's decode of the same GGUF bytes (C, on the host), bit-equal to the device decode
+    wf = torch.from_numpy(oracle.dequantize(w.download(), qt, (N, K))).cuda()
+    assert torch.equal(mb.dequantize(w, torch.float32), wf)
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        # fp32 reference on the bf16 operands the tensor core sees (the exact decode rounded to bf16)
+        ref = x.float() @ wf.bfloat16().float().t() + bias
+        err = ((y - ref).norm() / ref.norm()).item()
+        assert err < 1e-4, err
+        # and against the unrounded decode (what the GGML weights mean)
+        ref32 = x.float() @ wf.t() + bias
+        assert ((y - ref32).norm() / ref32.norm()).item() < 4e-3
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
     assert mb.device_status() == 0
 
 

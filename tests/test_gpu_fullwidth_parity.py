@@ -1,0 +1,189 @@
+"""Parity with the oracle at the headline widths and token counts (FLUX.1-dev and Qwen-Image at
+1024x1024: hidden 3072, 24 heads, 512 + 4096 FLUX tokens, 256 + 4096 Qwen tokens), against the
+fixtures made by tests/golden/make_fullwidth.py from the numpy oracle (reduced depth: the
+oracle needs ~30 s per full-width FLUX forward on a CPU).
+
+  * FLUX double block 0 and single block 0, composed from the C-ABI ops in the order the model
+    runs them (flux/offload.rs:275-323, :377-396): rel-L2 <= 1e-2 of each stream's update.
+  * The whole model (stems, 1 double + 1 single block, final layer) through mb_flux_forward:
+    rel-L2 <= 1e-2 of the prediction.
+  * The 28-step denoise through mb_flux_denoise with the product's own schedule
+    (flux/transformer.rs:50-95): cosine >= 0.999 of the final latent.
+  * Qwen-Image one block at 4096 + 256 tokens with a partial text mask through mb_qwen_forward,
+    and one CFG Euler step through mb_qwen_denoise (cond + uncond prompts with different masks,
+    qwen_image/pipeline.rs:2655-2716): rel-L2 <= 1e-2.
+
+Both GGUF types of the path (Q4_K and Q8_0) are covered for FLUX; Qwen uses Q4_K."""
+import dataclasses
+import os
+
+import numpy as np
+import pytest
+import torch
+
+import mold_b200 as mb
+import oracle
+from oracle import flux_ref as F
+from oracle import qwen_ref as Q
+from tests.conftest import rel_l2
+from tests.golden import make_fullwidth as G
+
+pytestmark = pytest.mark.gpu
+GOLD = os.path.join(os.path.dirname(__file__), "golden")
+
+
+def fixture(name):
+    p = os.path.join(GOLD, f"fullwidth_{name}.npz")
+    if not os.path.exists(p):
+        pytest.fail(f"missing fixture {p}: run tests/golden/make_fullwidth.py {name}")
+    return np.load(p)
+
+
+def t(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def rows(a):
+    return a[::G.ROW_STRIDE]
+
+
+@pytest.fixture(scope="module", params=list(G.FLUX_CASES))
+def flux_case(request, cuda):
+    name = request.param
+    qt, seed = G.FLUX_CASES[name]
+    cfg = G.flux_config()
+    W = F.synth_weights(cfg, seed=seed, qtype=qt)
+    return name, cfg, W, G.flux_inputs(seed), fixture(name)
+
+
+def flux_model(cfg_o, W):
+    cfg = mb.FluxConfig(in_channels=cfg_o.in_channels, vec_in_dim=cfg_o.vec_in_dim,
+                        context_in_dim=cfg_o.context_in_dim, hidden_size=cfg_o.hidden_size,
+                        mlp_ratio=cfg_o.mlp_ratio, num_heads=cfg_o.num_heads, depth=cfg_o.depth,
+                        depth_single_blocks=cfg_o.depth_single_blocks, axes_dim=cfg_o.axes_dim,
+                        theta=cfg_o.theta, guidance_embed=cfg_o.guidance_embed)
+    m = mb.FluxTransformer(cfg, max_txt=G.LT, max_img=G.HT * G.WT)
+    for name, qt in W.items():
+        m.set_tensor(name, mb.QTensor(qt.ggml_type, qt.shape, qt.raw))
+    assert m.missing() == []
+    return m
+
+
+def qmats(W, prefix):
+    return {n[len(prefix):]: mb.QMatMul.from_weights(mb.QTensor(W[n].ggml_type, W[n].shape, W[n].raw))
+            for n in W if n.startswith(prefix) and n.endswith("weight")}
+
+
+def vecs(W, prefix):
+    return {n[len(prefix):]: t(W[n].f32()) for n in W if n.startswith(prefix) and not n.endswith("weight")}
+
+
+def test_flux_double_block_full_width(flux_case):
+    name, cfg, W, (img, ids, txt, tids, y, _), gold = flux_case
+    h, H, lt = cfg.hidden_size, cfg.num_heads, G.LT
+    img_h, txt_h, vec, pe = G.flux_block_inputs(W, cfg, img, ids, txt, tids, y)
+    p = "double_blocks.0."
+    qm, bv = qmats(W, p), vecs(W, p)
+    gvec, gpe = t(vec), t(pe)
+    L = lt + img_h.shape[0]
+    q = torch.empty((H, L, 128), dtype=torch.bfloat16, device="cuda")
+    k, v = torch.empty_like(q), torch.empty_like(q)
+    streams = {"img": (t(img_h), lt), "txt": (t(txt_h), 0)}
+    mods = {}
+    for s, (x, off) in streams.items():
+        m = mb.qgemv(qm[f"{s}_mod.lin.weight"], gvec, apply_silu=True, bias=bv[f"{s}_mod.lin.bias"])
+        mods[s] = [m[i * h:(i + 1) * h] for i in range(6)]   # shift1, scale1, gate1, shift2, scale2, gate2
+        xm = mb.ln_modulate(x, mods[s][0], mods[s][1])
+        qkv = qm[f"{s}_attn.qkv.weight"].forward(xm, bias=bv[f"{s}_attn.qkv.bias"])
+        mb.qk_norm_rope(qkv, H, bv[f"{s}_attn.norm.query_norm.scale"], bv[f"{s}_attn.norm.key_norm.scale"], gpe,
+                        row_offset=off, L_total=L, q=q, k=k, v=v)
+    attn = mb.attention(q, k, v)
+    for s, (x, off) in streams.items():
+        a = attn[off:off + x.shape[0]]
+        qm[f"{s}_attn.proj.weight"].forward(a, bias=bv[f"{s}_attn.proj.bias"], epilogue=mb.EPI_GATE_RESIDUAL,
+                                            gate=mods[s][2], residual=x, out=x)
+        xm = mb.ln_modulate(x, mods[s][3], mods[s][4])
+        hid = qm[f"{s}_mlp.0.weight"].forward(xm, bias=bv[f"{s}_mlp.0.bias"], epilogue=mb.EPI_GELU_TANH, gelu_from=0)
+        qm[f"{s}_mlp.2.weight"].forward(hid, bias=bv[f"{s}_mlp.2.bias"], epilogue=mb.EPI_GATE_RESIDUAL,
+                                        gate=mods[s][5], residual=x, out=x)
+    torch.cuda.synchronize()
+    assert mb.device_status() == 0
+    for s, x0, key in (("img", img_h, "d_img"), ("txt", txt_h, "d_txt")):
+        got = rows(streams[s][0].cpu().numpy()) - rows(x0)
+        ref = gold[key].astype(np.float32)
+        err = rel_l2(got, ref)
+        assert err < 1e-2, (name, s, err)
+        assert rel_l2(rows(x0) + got, rows(x0) + ref) < 1e-2
+
+
+def test_flux_single_block_full_width(flux_case):
+    name, cfg, W, (img, ids, txt, tids, y, xs), gold = flux_case
+    h, H = cfg.hidden_size, cfg.num_heads
+    _, _, vec, pe = G.flux_block_inputs(W, cfg, img, ids, txt, tids, y)
+    p = "single_blocks.0."
+    qm, bv = qmats(W, p), vecs(W, p)
+    mods = mb.qgemv(qm["modulation.lin.weight"], t(vec), apply_silu=True, bias=bv["modulation.lin.bias"])
+    shift, scale, gate = mods[:h], mods[h:2 * h], mods[2 * h:]
+    x = t(xs)
+    xm = mb.ln_modulate(x, shift, scale)
+    Y = qm["linear1.weight"].forward(xm, bias=bv["linear1.bias"], epilogue=mb.EPI_GELU_TANH, gelu_from=3 * h)
+    q, k, v = mb.qk_norm_rope(Y, H, bv["norm.query_norm.scale"], bv["norm.key_norm.scale"], t(pe))
+    mb.attention(q, k, v, out=Y[:, 2 * h:3 * h])
+    qm["linear2.weight"].forward(Y[:, 2 * h:], bias=bv["linear2.bias"], epilogue=mb.EPI_GATE_RESIDUAL, gate=gate,
+                                 residual=x, out=x)
+    torch.cuda.synchronize()
+    assert mb.device_status() == 0
+    got = rows(x.cpu().numpy()) - rows(xs)
+    err = rel_l2(got, gold["d_single"].astype(np.float32))
+    assert err < 1e-2, (name, err)
+
+
+def test_flux_forward_and_28_step_denoise_full_width(flux_case):
+    name, cfg, W, (img, ids, txt, tids, y, _), gold = flux_case
+    m = flux_model(cfg, W)
+    pred = m.forward(t(img), t(ids), t(txt), t(tids), G.T_BLOCK, t(y), G.GUIDANCE).cpu().numpy()
+    err = rel_l2(pred, gold["pred"].astype(np.float32))
+    assert err < 1e-2, (name, err)
+    sched = mb.sampling.get_schedule(G.N_STEPS, G.HT * G.WT)
+    gi = t(img).clone()
+    m.denoise(gi, t(ids), t(txt), t(tids), t(y), sched, G.GUIDANCE)
+    got = gi.cpu().numpy()
+    ref = gold["denoise"].astype(np.float32)
+    cos = float(np.dot(got.ravel(), ref.ravel()) / np.linalg.norm(got) / np.linalg.norm(ref))
+    assert mb.device_status() == 0
+    assert cos >= 0.999, (name, cos)
+    # the same bar on what the 28 steps added to the initial latent
+    du, dr = (got - img).ravel(), (ref - img).ravel()
+    assert float(np.dot(du, dr) / np.linalg.norm(du) / np.linalg.norm(dr)) >= 0.999
+
+
+@pytest.fixture(scope="module")
+def qwen_case(cuda):
+    cfg = G.qwen_config()
+    W = Q.synth_weights(cfg, seed=13, qtype=oracle.GGML_Q4_K)
+    m = mb.QwenTransformer(mb.QwenConfig(**dataclasses.asdict(cfg)), max_txt=G.Q_LT, max_img=G.HT * G.WT,
+                           max_batch=2)
+    for n, qt in W.items():
+        m.set_tensor(n, mb.QTensor(qt.ggml_type, qt.shape, qt.raw))
+    assert m.missing() == []
+    return m, G.qwen_inputs(), fixture("qwen_q4_k")
+
+
+def test_qwen_block_full_width_masked(qwen_case):
+    m, (x, txt, mk, _), gold = qwen_case
+    got = m.forward(t(x[None]), G.Q_T, t(txt[:1]), t(mk[:1]), G.HT, G.WT).cpu().numpy()[0]
+    err = rel_l2(got, gold["pred"].astype(np.float32))
+    assert err < 1e-2, err
+    assert mb.device_status() == 0
+
+
+def test_qwen_cfg_step_full_width(qwen_case):
+    m, (_, txt, mk, latent), gold = qwen_case
+    sig = mb.sampling.qwen_sigmas(G.Q_STEPS, G.HT * G.WT)[:2]
+    gi = t(F.patchify(latent))
+    m.denoise(gi, t(txt), t(mk), G.HT, G.WT, sig, G.Q_GUIDANCE)
+    got = F.unpack(gi.cpu().numpy(), 2 * G.HT, 2 * G.WT)
+    d_ref = gold["d_cfg_step"].astype(np.float32)
+    assert mb.device_status() == 0
+    assert rel_l2(got - latent, d_ref) < 1e-2   # the step's update
+    assert rel_l2(got, latent + d_ref) < 1e-2
