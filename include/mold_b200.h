@@ -268,6 +268,33 @@ MB_API mb_status mb_flux_denoise(mb_flux* m, float* img, const float* img_ids, i
                           const float* txt_ids, int64_t L_txt, const float* y, const double* timesteps,
                           int n_timesteps, float guidance, void* stream);
 
+/* Called on a CUDA host-function thread once denoising step `step` (1-based) of `total` has
+ * finished on the device. It must not call CUDA or mold_b200 functions. Replaces the
+ * per-step `ProgressEvent::DenoiseStep { step, total, elapsed }` of flux/transformer.rs:89-93
+ * and qwen_image/pipeline.rs:2720-2724 (the host can time steps by the calls' wall clock). */
+typedef void (*mb_step_callback)(void* user, int step, int total);
+
+/* Flow-matching inpainting inputs, all device f32 in the packed latent layout
+ * [L_img, in_channels] (patchified like img; the mask is the latent-resolution mask broadcast
+ * over the latent channels before packing): 1 = repaint, 0 = preserve. */
+typedef struct {
+  const float* mask;
+  const float* original;  /* clean (VAE-encoded) latents of the source image */
+  const float* noise;     /* the noise the initial latent was drawn with */
+} mb_inpaint;
+
+/* mb_flux_denoise with inpainting and per-step progress (either may be NULL). After each
+ * step's Euler update, with t = the step's t_prev:
+ *   img = img * mask + (original * (1 - t) + noise * t) * (1 - mask)
+ * inside the same replayed step graph (flux/transformer.rs:79-87, img2img.rs:36-42,79-98).
+ * on_step(user, step, total) runs after each step has finished on the device; the call
+ * itself stays asynchronous. The reference blends [1, 16, H, W] context tensors with the
+ * packed state; here every operand is packed, so the caller patchifies them once. */
+MB_API mb_status mb_flux_denoise_ex(mb_flux* m, float* img, const float* img_ids, int64_t L_img, const float* txt,
+                                    const float* txt_ids, int64_t L_txt, const float* y, const double* timesteps,
+                                    int n_timesteps, float guidance, const mb_inpaint* inpaint,
+                                    mb_step_callback on_step, void* user, void* stream);
+
 /* ------------------------------------------------------------------ Qwen-Image model */
 
 typedef struct mb_qwen mb_qwen;
@@ -322,6 +349,15 @@ MB_API mb_status mb_qwen_forward(mb_qwen* m, const float* img, int64_t h_tokens,
 MB_API mb_status mb_qwen_denoise(mb_qwen* m, float* img, int64_t h_tokens, int64_t w_tokens, const float* txt,
                                  const uint8_t* txt_mask, int64_t L_txt, int batch, const double* sigmas, int n_sigmas,
                                  float guidance, void* stream);
+
+/* mb_qwen_denoise with inpainting and per-step progress (either may be NULL): after each
+ * step's (CFG) Euler update, img = img * mask + (original * (1 - s) + noise * s) * (1 - mask)
+ * with s = sigmas[i + 1] (qwen_image/pipeline.rs:2708-2715, img2img::apply_flow_match_inpaint),
+ * on packed [L_img, in_channels] operands; on_step as for mb_flux_denoise_ex. */
+MB_API mb_status mb_qwen_denoise_ex(mb_qwen* m, float* img, int64_t h_tokens, int64_t w_tokens, const float* txt,
+                                    const uint8_t* txt_mask, int64_t L_txt, int batch, const double* sigmas,
+                                    int n_sigmas, float guidance, const mb_inpaint* inpaint,
+                                    mb_step_callback on_step, void* user, void* stream);
 
 /* ------------------------------------------------------------------ GGUF files */
 

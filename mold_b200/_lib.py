@@ -20,6 +20,8 @@ _STATUS_NAMES = {0: "MB_OK", 1: "MB_ERR_INVALID", 2: "MB_ERR_UNSUPPORTED", 3: "M
 
 # Every exported symbol with (restype, argtypes). Kept in the order of include/mold_b200.h.
 P, I32, I64, F32, SZ = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_float, ctypes.c_size_t
+# mb_step_callback: void (*)(void* user, int step, int total)
+STEP_CALLBACK = ctypes.CFUNCTYPE(None, ctypes.c_void_p, ctypes.c_int, ctypes.c_int)
 SIGNATURES = {
     "mb_last_error": (ctypes.c_char_p, []),
     "mb_version": (I32, []),
@@ -48,12 +50,14 @@ SIGNATURES = {
     "mb_flux_missing": (I32, [P, P, SZ]),
     "mb_flux_forward": (I32, [P, P, P, I64, P, P, I64, F32, P, F32, P, P]),
     "mb_flux_denoise": (I32, [P, P, P, I64, P, P, I64, P, P, I32, F32, P]),
+    "mb_flux_denoise_ex": (I32, [P, P, P, I64, P, P, I64, P, P, I32, F32, P, STEP_CALLBACK, P, P]),
     "mb_qwen_create": (I32, [P, I64, I64, I32, P]),
     "mb_qwen_destroy": (I32, [P]),
     "mb_qwen_set_tensor": (I32, [P, ctypes.c_char_p, I32, I64, I64, P, SZ, I32]),
     "mb_qwen_missing": (I32, [P, P, SZ]),
     "mb_qwen_forward": (I32, [P, P, I64, I64, P, P, I64, I32, F32, P, P]),
     "mb_qwen_denoise": (I32, [P, P, I64, I64, P, P, I64, I32, P, I32, F32, P]),
+    "mb_qwen_denoise_ex": (I32, [P, P, I64, I64, P, P, I64, I32, P, I32, F32, P, STEP_CALLBACK, P, P]),
     "mb_gguf_inspect": (I32, [ctypes.c_char_p, P, SZ, P]),
     "mb_flux_load_gguf": (I32, [P, ctypes.c_char_p, ctypes.c_char_p, P]),
     "mb_qwen_load_gguf": (I32, [P, ctypes.c_char_p, P]),
@@ -72,6 +76,10 @@ class FluxConfigC(ctypes.Structure):
     _fields_ = [("in_channels", I32), ("vec_in_dim", I32), ("context_in_dim", I32), ("hidden_size", I32),
                 ("mlp_hidden", I32), ("num_heads", I32), ("depth", I32), ("depth_single", I32),
                 ("axes_dim", I32 * 3), ("theta", I32), ("guidance_embed", I32)]
+
+
+class InpaintC(ctypes.Structure):
+    _fields_ = [("mask", P), ("original", P), ("noise", P)]
 
 
 class QwenConfigC(ctypes.Structure):

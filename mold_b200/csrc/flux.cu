@@ -54,7 +54,7 @@ struct mb_flux {
   __nv_bfloat16* txt_bf = nullptr;
   __nv_bfloat16* img_bf = nullptr;
   float* pred = nullptr;
-  float* scal = nullptr;   // [0] t, [1] guidance, [2] dt
+  float* scal = nullptr;   // [0] t, [1] guidance, [2] dt, [3] t_next, [4] 1 - t_next
   int* counter = nullptr;
   double* sched = nullptr;
   int sched_cap = 0;
@@ -73,7 +73,7 @@ struct mb_flux {
   // graph cache
   cudaGraphExec_t graph = nullptr;
   int64_t graph_lt = -1, graph_li = -1;
-  const void* graph_key[6] = {nullptr, nullptr, nullptr, nullptr, nullptr, nullptr};
+  const void* graph_key[7] = {nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr};
 
   int64_t H() const { return cfg.num_heads; }
   int64_t h() const { return cfg.hidden_size; }
@@ -427,7 +427,7 @@ mb_status mb_flux_create(const mb_flux_config* cfg, int64_t max_txt, int64_t max
       (s = dalloc(&m->q, H * L * 128)) || (s = dalloc(&m->k, H * L * 128)) || (s = dalloc(&m->v, H * L * 128)) ||
       (s = dalloc(&m->pe, L * 256)) || (s = dalloc(&m->ids, L * 3)) ||
       (s = dalloc(&m->txt_bf, max_txt * cfg->context_in_dim)) || (s = dalloc(&m->img_bf, max_img * cfg->in_channels)) ||
-      (s = dalloc(&m->pred, max_img * cfg->in_channels)) || (s = dalloc(&m->scal, 4)) ||
+      (s = dalloc(&m->pred, max_img * cfg->in_channels)) || (s = dalloc(&m->scal, 8)) ||
       (s = dalloc(&m->counter, 1)) || (s = dalloc(&m->temb, 512)) || (s = dalloc(&m->hid, 3 * h)) ||
       (s = dalloc(&m->parts, 3 * h)) || (s = dalloc(&m->gemv_stage, gemv_stage_floats()))) {
     mb_flux_destroy(m);
@@ -533,11 +533,14 @@ mb_status mb_flux_forward(mb_flux* m, const float* img, const float* img_ids, in
   return MB_OK;
 }
 
-mb_status mb_flux_denoise(mb_flux* m, float* img, const float* img_ids, int64_t L_img, const float* txt,
-                          const float* txt_ids, int64_t L_txt, const float* y, const double* timesteps,
-                          int n_timesteps, float guidance, void* stream) {
+mb_status mb_flux_denoise_ex(mb_flux* m, float* img, const float* img_ids, int64_t L_img, const float* txt,
+                             const float* txt_ids, int64_t L_txt, const float* y, const double* timesteps,
+                             int n_timesteps, float guidance, const mb_inpaint* inpaint, mb_step_callback on_step,
+                             void* user, void* stream) {
   MB_CHECK(m && img && img_ids && txt && txt_ids && y && timesteps, MB_ERR_INVALID, "NULL argument");
   MB_CHECK(n_timesteps >= 2, MB_ERR_INVALID, "need at least two timesteps");
+  MB_CHECK(!inpaint || (inpaint->mask && inpaint->original && inpaint->noise), MB_ERR_INVALID,
+           "inpaint needs mask, original and noise");
   MB_TRY(check_complete(m));
   cudaStream_t st = (cudaStream_t)stream;
   MB_TRY(prepare(m, img_ids, L_img, txt_ids, L_txt, st));
@@ -552,7 +555,8 @@ mb_status mb_flux_denoise(mb_flux* m, float* img, const float* img_ids, int64_t 
   MB_CUDA(cudaMemsetAsync(m->counter, 0, sizeof(int), st));
   MB_CUDA(launch_set_scalars(m->scal, (float)timesteps[0], guidance, st));
   const int64_t n_img = L_img * m->cfg.in_channels;
-  const void* key[6] = {img, txt, y, m->sched, nullptr, nullptr};
+  const void* key[7] = {img, txt, y, m->sched, inpaint ? inpaint->mask : nullptr,
+                        inpaint ? inpaint->original : nullptr, inpaint ? inpaint->noise : nullptr};
   const bool reuse = m->graph && m->graph_lt == L_txt && m->graph_li == L_img &&
                      memcmp(key, m->graph_key, sizeof(key)) == 0;
   if (!reuse) {
@@ -572,6 +576,8 @@ mb_status mb_flux_denoise(mb_flux* m, float* img, const float* img_ids, int64_t 
     launch_step_prologue(m->sched, m->counter, m->scal, cs);
     mb_status s = run_forward(m, img, L_img, txt, L_txt, y, cs);
     cudaError_t le = launch_euler_dev(img, m->pred, n_img, m->scal + 2, cs);
+    if (le == cudaSuccess && inpaint)
+      le = launch_inpaint_blend(img, n_img, m->scal, inpaint->mask, inpaint->original, inpaint->noise, cs);
     cudaError_t ce = cudaStreamEndCapture(cs, &g);
     cudaStreamDestroy(cs);
     if (s != MB_OK) return s;
@@ -584,8 +590,15 @@ mb_status mb_flux_denoise(mb_flux* m, float* img, const float* img_ids, int64_t 
     m->graph_li = L_img;
     memcpy(m->graph_key, key, sizeof(key));
   }
-  for (int i = 0; i + 1 < n_timesteps; i++) MB_CUDA(cudaGraphLaunch(m->graph, st));
+  MB_CUDA(enqueue_steps(m->graph, n_timesteps - 1, on_step, user, st));
   return MB_OK;
+}
+
+mb_status mb_flux_denoise(mb_flux* m, float* img, const float* img_ids, int64_t L_img, const float* txt,
+                          const float* txt_ids, int64_t L_txt, const float* y, const double* timesteps,
+                          int n_timesteps, float guidance, void* stream) {
+  return mb_flux_denoise_ex(m, img, img_ids, L_img, txt, txt_ids, L_txt, y, timesteps, n_timesteps, guidance,
+                            nullptr, nullptr, nullptr, stream);
 }
 
 }  // extern "C"

@@ -12,18 +12,79 @@ __global__ void k_set_scalars(float* dst, float a, float b) {
   dst[1] = b;
 }
 
+// scal: [0] t (or sigma), [2] dt = t_next - t, [3] t_next, [4] 1 - t_next (the inpaint blend's
+// weights, each formed in f64 and rounded once, as the reference's f64 scalar multiplies are).
 __global__ void k_step_prologue(const double* sched, int* counter, float* scal) {
   const int i = *counter;
   scal[0] = (float)sched[i];
   scal[2] = (float)(sched[i + 1] - sched[i]);
+  scal[3] = (float)sched[i + 1];
+  scal[4] = (float)(1.0 - sched[i + 1]);
   *counter = i + 1;
+}
+
+// Per-step host callbacks: one context per enqueued step; the last one frees the array.
+struct StepCallCtx {
+  mb_step_callback fn;
+  void* user;
+  int step, total;
+  StepCallCtx* array;
+};
+void CUDART_CB step_trampoline(void* p) {
+  StepCallCtx* c = (StepCallCtx*)p;
+  c->fn(c->user, c->step, c->total);
+  if (c->step == c->total) delete[] c->array;
 }
 
 }  // namespace
 
+cudaError_t enqueue_steps(cudaGraphExec_t graph, int n_steps, mb_step_callback fn, void* user, cudaStream_t st) {
+  if (!fn) {
+    for (int i = 0; i < n_steps; i++) {
+      cudaError_t e = cudaGraphLaunch(graph, st);
+      if (e != cudaSuccess) return e;
+    }
+    return cudaSuccess;
+  }
+  StepCallCtx* ctx = new StepCallCtx[n_steps];
+  for (int i = 0; i < n_steps; i++) ctx[i] = StepCallCtx{fn, user, i + 1, n_steps, ctx};
+  for (int i = 0; i < n_steps; i++) {
+    cudaError_t e = cudaGraphLaunch(graph, st);
+    if (e == cudaSuccess) e = cudaLaunchHostFunc(st, step_trampoline, &ctx[i]);
+    // On failure the callbacks already enqueued may still run and read ctx: it is leaked.
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
+}
+
 bool profile_requested() {
   const char* pe = getenv("MOLD_B200_PROFILE");
   return pe && pe[0] == '1';
+}
+
+namespace {
+// Inpainting blend after the step's Euler update (flux/transformer.rs:79-87,
+// img2img.rs:36-42,79-98): img = img * mask + ((orig * (1 - t_next)) + (noise * t_next)) * (1 - mask),
+// each product and sum rounded separately as the reference's tensor ops are.
+__global__ void k_inpaint_blend(float* __restrict__ img, int64_t n, const float* __restrict__ scal,
+                                const float* __restrict__ mask, const float* __restrict__ orig,
+                                const float* __restrict__ noise) {
+  const float t = scal[3], omt = scal[4];
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const float m = mask[i];
+    const float keep = __fadd_rn(__fmul_rn(orig[i], omt), __fmul_rn(noise[i], t));
+    img[i] = __fadd_rn(__fmul_rn(img[i], m), __fmul_rn(keep, __fsub_rn(1.f, m)));
+  }
+}
+}  // namespace
+
+cudaError_t launch_inpaint_blend(float* img, int64_t n, const float* scal, const float* mask, const float* orig,
+                                 const float* noise, cudaStream_t st) {
+  if (n <= 0) return cudaSuccess;
+  int64_t blocks = (n + 255) / 256;
+  if (blocks > 148 * 8) blocks = 148 * 8;
+  k_inpaint_blend<<<(int)blocks, 256, 0, st>>>(img, n, scal, mask, orig, noise);
+  return cudaGetLastError();
 }
 
 cudaError_t launch_set_scalars(float* scal, float a, float b, cudaStream_t st) {

@@ -76,9 +76,16 @@ bool profile_requested();  // MOLD_B200_PROFILE=1
 
 // scal[0] = a, scal[1] = b.
 cudaError_t launch_set_scalars(float* scal, float a, float b, cudaStream_t st);
-// scal[0] = sched[i], scal[2] = sched[i+1] - sched[i] (f64 difference), then ++*counter.
-// Runs at the start of each replayed step so one captured graph serves every step.
+// scal[0] = sched[i], scal[2] = sched[i+1] - sched[i] (f64 difference), scal[3] = sched[i+1],
+// scal[4] = 1 - sched[i+1], then ++*counter. Runs at the start of each replayed step so one
+// captured graph serves every step. scal must hold 8 floats.
 cudaError_t launch_step_prologue(const double* sched, int* counter, float* scal, cudaStream_t st);
+// img[i] = img[i] * mask[i] + (orig[i] * scal[4] + noise[i] * scal[3]) * (1 - mask[i]), f32 [n].
+cudaError_t launch_inpaint_blend(float* img, int64_t n, const float* scal, const float* mask, const float* orig,
+                                 const float* noise, cudaStream_t st);
+// Launches `graph` n_steps times on st; with fn, a host function after each launch calls
+// fn(user, step, n_steps) once that step has finished on the device (cudaLaunchHostFunc).
+cudaError_t enqueue_steps(cudaGraphExec_t graph, int n_steps, mb_step_callback fn, void* user, cudaStream_t st);
 
 // Uploads a 1-D F32/F16/BF16 tensor as f32.
 mb_status upload_vec1(int ggml_type, int64_t len, const void* data, size_t nbytes, int on_device, Vec1* out);

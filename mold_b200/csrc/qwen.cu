@@ -69,7 +69,7 @@ struct mb_qwen {
   __nv_bfloat16* txt_bf = nullptr;
   __nv_bfloat16* img_bf = nullptr;
   float* pred = nullptr;
-  float* scal = nullptr;  // [0] t, [2] dt
+  float* scal = nullptr;  // [0] t, [2] dt, [3] sigma_next, [4] 1 - sigma_next
   int* counter = nullptr;
   double* sched = nullptr;
   int sched_cap = 0;
@@ -531,7 +531,7 @@ mb_status mb_qwen_create(const mb_qwen_config* cfg, int64_t max_txt, int64_t max
       (s = dalloc(&m->kv_pos, max_batch * L)) ||
       (s = dalloc(&m->txt_bf, max_batch * max_txt * cfg->joint_attention_dim)) ||
       (s = dalloc(&m->img_bf, max_batch * max_img * cfg->in_channels)) ||
-      (s = dalloc(&m->pred, max_batch * max_img * cfg->in_channels)) || (s = dalloc(&m->scal, 4)) ||
+      (s = dalloc(&m->pred, max_batch * max_img * cfg->in_channels)) || (s = dalloc(&m->scal, 8)) ||
       (s = dalloc(&m->counter, 1)) || (s = dalloc(&m->temb, 256)) || (s = dalloc(&m->hid, h)) ||
       (s = dalloc(&m->tvec, h)) || (s = dalloc(&m->gemv_stage, gemv_stage_floats()))) {
     mb_qwen_destroy(m);
@@ -626,10 +626,13 @@ mb_status mb_qwen_forward(mb_qwen* m, const float* img, int64_t h_tokens, int64_
   return MB_OK;
 }
 
-mb_status mb_qwen_denoise(mb_qwen* m, float* img, int64_t h_tokens, int64_t w_tokens, const float* txt,
-                          const uint8_t* txt_mask, int64_t L_txt, int batch, const double* sigmas, int n_sigmas,
-                          float guidance, void* stream) {
+mb_status mb_qwen_denoise_ex(mb_qwen* m, float* img, int64_t h_tokens, int64_t w_tokens, const float* txt,
+                             const uint8_t* txt_mask, int64_t L_txt, int batch, const double* sigmas, int n_sigmas,
+                             float guidance, const mb_inpaint* inpaint, mb_step_callback on_step, void* user,
+                             void* stream) {
   MB_CHECK(m && img && txt && sigmas, MB_ERR_INVALID, "NULL argument");
+  MB_CHECK(!inpaint || (inpaint->mask && inpaint->original && inpaint->noise), MB_ERR_INVALID,
+           "inpaint needs mask, original and noise");
   MB_CHECK(n_sigmas >= 2, MB_ERR_INVALID, "need at least two sigmas");
   cudaStream_t st = (cudaStream_t)stream;
   MB_TRY(prepare(m, h_tokens, w_tokens, txt_mask, L_txt, batch, st));
@@ -650,12 +653,20 @@ mb_status mb_qwen_denoise(mb_qwen* m, float* img, int64_t h_tokens, int64_t w_to
   std::vector<int64_t> key = {(int64_t)(uintptr_t)img, (int64_t)(uintptr_t)txt, (int64_t)(uintptr_t)m->sched,
                               L_txt, Li, batch, (int64_t)gbits};
   for (int64_t nv : m->n_valid) key.push_back(nv);
+  for (const void* p : {inpaint ? (const void*)inpaint->mask : nullptr, inpaint ? (const void*)inpaint->original : nullptr,
+                        inpaint ? (const void*)inpaint->noise : nullptr})
+    key.push_back((int64_t)(uintptr_t)p);
   const bool reuse = m->graph && key == m->graph_key;
   auto step_tail = [&](cudaStream_t s) -> cudaError_t {
+    cudaError_t e;
     if (batch == 2)
-      return launch_cfg_euler(img, m->pred, m->pred + Li * cin, Li, m->cfg.out_channels,
-                              m->cfg.patch_size * m->cfg.patch_size, guidance, 0.f, m->scal + 2, s);
-    return launch_euler_dev(img, m->pred, Li * cin, m->scal + 2, s);
+      e = launch_cfg_euler(img, m->pred, m->pred + Li * cin, Li, m->cfg.out_channels,
+                           m->cfg.patch_size * m->cfg.patch_size, guidance, 0.f, m->scal + 2, s);
+    else
+      e = launch_euler_dev(img, m->pred, Li * cin, m->scal + 2, s);
+    if (e == cudaSuccess && inpaint)
+      e = launch_inpaint_blend(img, Li * cin, m->scal, inpaint->mask, inpaint->original, inpaint->noise, s);
+    return e;
   };
   if (!reuse) {
     if (m->graph) {
@@ -685,8 +696,15 @@ mb_status mb_qwen_denoise(mb_qwen* m, float* img, int64_t h_tokens, int64_t w_to
     MB_CUDA(ie);
     m->graph_key = key;
   }
-  for (int i = 0; i + 1 < n_sigmas; i++) MB_CUDA(cudaGraphLaunch(m->graph, st));
+  MB_CUDA(enqueue_steps(m->graph, n_sigmas - 1, on_step, user, st));
   return MB_OK;
+}
+
+mb_status mb_qwen_denoise(mb_qwen* m, float* img, int64_t h_tokens, int64_t w_tokens, const float* txt,
+                          const uint8_t* txt_mask, int64_t L_txt, int batch, const double* sigmas, int n_sigmas,
+                          float guidance, void* stream) {
+  return mb_qwen_denoise_ex(m, img, h_tokens, w_tokens, txt, txt_mask, L_txt, batch, sigmas, n_sigmas, guidance,
+                            nullptr, nullptr, nullptr, stream);
 }
 
 }  // extern "C"

@@ -12,7 +12,7 @@ from dataclasses import dataclass
 import torch
 
 from ._lib import FluxConfigC, check, lib
-from .ops import QTensor, _lora_operands, _ptr, _stream, init
+from .ops import QTensor, _lora_operands, _ptr, _stream, denoise_extras, init
 
 
 @dataclass
@@ -159,12 +159,22 @@ class FluxTransformer:
                                     txt.shape[0], float(t), _ptr(y), float(guidance), _ptr(pred), _stream()))
         return pred
 
-    def denoise(self, img, img_ids, txt, txt_ids, y, timesteps, guidance):
-        """In-place Euler loop over `timesteps` (list of floats); returns img."""
+    def denoise(self, img, img_ids, txt, txt_ids, y, timesteps, guidance, inpaint=None, on_step=None):
+        """In-place Euler loop over `timesteps` (list of floats); returns img. inpaint =
+        (mask, original, noise) packed like img blends the preserved region back after every
+        step; on_step(step, total) reports progress (FluxTransformer::denoise's inpaint_ctx and
+        DenoiseStep events, flux/transformer.rs:79-93)."""
         assert img.dtype == torch.float32 and img.is_contiguous()
         ts = (ctypes.c_double * len(timesteps))(*[float(t) for t in timesteps])
         txt, txt_ids, img_ids, y = (a.contiguous().float() for a in (txt, txt_ids, img_ids, y))
-        self._keep = (txt, txt_ids, img_ids, y)
-        check(lib().mb_flux_denoise(self._h, _ptr(img), _ptr(img_ids), img.shape[0], _ptr(txt), _ptr(txt_ids),
-                                    txt.shape[0], _ptr(y), ts, len(timesteps), float(guidance), _stream()))
+        if inpaint is None and on_step is None:
+            self._keep = (txt, txt_ids, img_ids, y)
+            check(lib().mb_flux_denoise(self._h, _ptr(img), _ptr(img_ids), img.shape[0], _ptr(txt), _ptr(txt_ids),
+                                        txt.shape[0], _ptr(y), ts, len(timesteps), float(guidance), _stream()))
+            return img
+        ip, cb, keep = denoise_extras(inpaint, on_step)
+        self._keep = (txt, txt_ids, img_ids, y, keep)
+        check(lib().mb_flux_denoise_ex(self._h, _ptr(img), _ptr(img_ids), img.shape[0], _ptr(txt), _ptr(txt_ids),
+                                       txt.shape[0], _ptr(y), ts, len(timesteps), float(guidance), ip, cb, None,
+                                       _stream()))
         return img

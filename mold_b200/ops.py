@@ -8,7 +8,7 @@ import ctypes
 import numpy as np
 import torch
 
-from ._lib import (DT_BF16, DT_F32, EPI_GATE_RESIDUAL, EPI_GELU_TANH, EPI_NONE, GGML_BF16, GGML_F16, GGML_F32,
+from ._lib import (STEP_CALLBACK, InpaintC, DT_BF16, DT_F32, EPI_GATE_RESIDUAL, EPI_GELU_TANH, EPI_NONE, GGML_BF16, GGML_F16, GGML_F32,
                    GGML_Q4_0, GGML_Q4_1, GGML_Q4_K, GGML_Q5_0, GGML_Q5_1, GGML_Q5_K, GGML_Q6_K, GGML_Q8_0, check, lib)
 
 # (values, bytes) per GGUF block
@@ -278,3 +278,21 @@ def gguf_inspect(path):
             f = line.split("\t")
             out.append((f[0], int(f[1]), tuple(int(x) for x in f[2:])))
     return out
+
+
+def denoise_extras(inpaint, on_step):
+    """ctypes arguments of the *_denoise_ex calls: (pointer to an mb_inpaint or None, callback,
+    objects to keep alive while the steps run). inpaint = (mask, original, noise), f32 CUDA
+    tensors shaped like the packed latent (1 = repaint, 0 = preserve); on_step(step, total) is
+    called from a CUDA host-function thread once each step has finished on the device (keep it
+    short, and synchronise the stream before relying on every call having happened)."""
+    keep = []
+    ip = None
+    if inpaint is not None:
+        ts = [a.contiguous().float() for a in inpaint]
+        keep += ts
+        ip = InpaintC(*[ctypes.c_void_p(a.data_ptr()) for a in ts])
+        keep.append(ip)
+    cb = STEP_CALLBACK(lambda user, step, total: on_step(step, total)) if on_step is not None else STEP_CALLBACK()
+    keep.append(cb)
+    return (ctypes.byref(ip) if ip is not None else None), cb, keep

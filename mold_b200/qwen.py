@@ -12,7 +12,7 @@ from dataclasses import dataclass
 import torch
 
 from ._lib import QwenConfigC, check, lib
-from .ops import QTensor, _ptr, _stream, init
+from .ops import QTensor, _ptr, _stream, denoise_extras, init
 
 
 @dataclass
@@ -148,16 +148,24 @@ class QwenTransformer:
                                     float(t), _ptr(pred), _stream()))
         return pred
 
-    def denoise(self, img, txt, txt_mask, h_tokens, w_tokens, sigmas, guidance=1.0):
+    def denoise(self, img, txt, txt_mask, h_tokens, w_tokens, sigmas, guidance=1.0, inpaint=None, on_step=None):
         """In place on packed latents img [L_img, 64] f32: the Qwen step loop over `sigmas`
-        (with batch-2 txt / txt_mask: CFG with norm rescale at `guidance`). Returns img."""
+        (with batch-2 txt / txt_mask: CFG with norm rescale at `guidance`). Returns img.
+        inpaint = (mask, original, noise) and on_step(step, total) as for FluxTransformer.denoise
+        (qwen_image/pipeline.rs:2708-2724)."""
         assert img.dtype == torch.float32 and img.is_contiguous()
         txt = txt.contiguous().float()
         if txt.dim() == 2:
             txt = txt[None]
         mask = self._mask(txt_mask, txt)
         sg = (ctypes.c_double * len(sigmas))(*[float(s) for s in sigmas])
-        self._keep = (txt, mask)
-        check(lib().mb_qwen_denoise(self._h, _ptr(img), h_tokens, w_tokens, _ptr(txt), _ptr(mask), txt.shape[1],
-                                    txt.shape[0], sg, len(sigmas), float(guidance), _stream()))
+        if inpaint is None and on_step is None:
+            self._keep = (txt, mask)
+            check(lib().mb_qwen_denoise(self._h, _ptr(img), h_tokens, w_tokens, _ptr(txt), _ptr(mask), txt.shape[1],
+                                        txt.shape[0], sg, len(sigmas), float(guidance), _stream()))
+            return img
+        ip, cb, keep = denoise_extras(inpaint, on_step)
+        self._keep = (txt, mask, keep)
+        check(lib().mb_qwen_denoise_ex(self._h, _ptr(img), h_tokens, w_tokens, _ptr(txt), _ptr(mask), txt.shape[1],
+                                       txt.shape[0], sg, len(sigmas), float(guidance), ip, cb, None, _stream()))
         return img

@@ -336,12 +336,24 @@ def get_schedule(num_steps, image_seq_len=None, base_shift=0.5, max_shift=1.15):
     return [shift(t) for t in ts]
 
 
-def denoise(W, cfg, img, img_ids, txt, txt_ids, y, timesteps, guidance):
-    """flux/transformer.rs:50-95 (no inpaint): img += pred * (t_prev - t_curr)."""
+def inpaint_blend(img, inpaint, t):
+    """flux/transformer.rs:79-87 and img2img.rs:36-42,79-98: the original re-noised to t,
+    orig * (1 - t) + noise * t (f64 scalars rounded to f32), restored where mask = 0:
+    img * mask + preserved * (1 - mask); every operand in the same (packed) layout."""
+    mask, orig, noise = (np.asarray(a, np.float32) for a in inpaint)
+    keep = (orig * np.float32(1.0 - t)).astype(np.float32) + (noise * np.float32(t)).astype(np.float32)
+    return ((img * mask).astype(np.float32) + (keep * (np.float32(1.0) - mask)).astype(np.float32)).astype(np.float32)
+
+
+def denoise(W, cfg, img, img_ids, txt, txt_ids, y, timesteps, guidance, inpaint=None):
+    """flux/transformer.rs:50-95: img += pred * (t_prev - t_curr), then the inpaint blend at
+    t_prev when inpaint = (mask, original, noise) is given."""
     img = img.astype(np.float32).copy()
     for t_curr, t_prev in zip(timesteps[:-1], timesteps[1:]):
         pred = forward(W, cfg, img, img_ids, txt, txt_ids, t_curr, y, guidance)
         img = (img + pred * np.float32(t_prev - t_curr)).astype(np.float32)
+        if inpaint is not None:
+            img = inpaint_blend(img, inpaint, t_prev)
     return img
 
 

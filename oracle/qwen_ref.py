@@ -272,7 +272,8 @@ def cfg_combine(cond, uncond, guidance):
     return (comb * (cn / bn)).astype(np.float32)
 
 
-def denoise(W, cfg, latent, txt_c, mask_c, sigmas, txt_u=None, mask_u=None, guidance=1.0, n_layers=None):
+def denoise(W, cfg, latent, txt_c, mask_c, sigmas, txt_u=None, mask_u=None, guidance=1.0, n_layers=None,
+            inpaint=None):
     """The Qwen denoise loop on a [C, H, W] latent: t = sigma * 1000, CFG when an unconditional
     prompt is given, Euler x += pred * (sigma_next - sigma) in f32."""
     from .flux_ref import patchify, unpack
@@ -288,4 +289,7 @@ def denoise(W, cfg, latent, txt_c, mask_c, sigmas, txt_u=None, mask_u=None, guid
         else:
             pred = pc
         x = (x + pred * np.float32(s_next - s)).astype(np.float32)
+        if inpaint is not None:  # pipeline.rs:2708-2715 at sigmas[step + 1], [C, H, W] operands
+            from .flux_ref import inpaint_blend
+            x = inpaint_blend(x, inpaint, s_next)
     return x

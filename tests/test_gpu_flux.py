@@ -110,3 +110,31 @@ def test_config1_single_block_ops(cuda):
     err = rel_l2(xg.cpu().numpy() - x, ref - x)  # error relative to the block's update
     assert err < 1e-2, err
     assert rel_l2(xg.cpu().numpy(), ref) < 1e-2
+
+
+def test_tiny_flux_denoise_inpaint_and_progress(cuda):
+    """FluxTransformer::denoise with an inpaint context and progress events
+    (flux/transformer.rs:79-93) through mb_flux_denoise_ex: the blend runs inside the replayed
+    step graph, the callback reports steps 1..n in order, and the result matches the oracle."""
+    W = F.synth_weights(TINY, seed=2, qtype=oracle.GGML_Q4_K)
+    m = to_model(TINY, W, 64, 256)
+    img, ids, txt, tids, y = inputs(TINY, 32, 8, 8, seed=210)
+    ts = mb.sampling.get_schedule(6, 64)
+    mask = (np.random.default_rng(3).random((64, 1)) < 0.5).astype(np.float32) * np.ones((1, 64), np.float32)
+    orig = oracle.randn(211, img.shape)
+    noise = img.copy()
+    ref = F.denoise(W, TINY, img, ids, txt, tids, y, ts, 3.5, inpaint=(mask, orig, noise))
+    t = lambda a: torch.from_numpy(a).to(cuda)
+    seen = []
+    gi = t(img).clone()
+    m.denoise(gi, t(ids), t(txt), t(tids), t(y), ts, 3.5, inpaint=(t(mask), t(orig), t(noise)),
+              on_step=lambda step, total: seen.append((step, total)))
+    torch.cuda.synchronize()
+    got = gi.cpu().numpy()
+    assert seen == [(i, 6) for i in range(1, 7)]
+    cos = float(np.dot(got.ravel(), ref.ravel()) / np.linalg.norm(got) / np.linalg.norm(ref))
+    assert cos >= 0.999, cos
+    # preserved tokens hold exactly the re-noised original at the last t (0): the original
+    keep = mask[:, 0] == 0
+    assert np.allclose(got[keep], orig[keep], atol=1e-6)
+    assert rel_l2(got[~keep], ref[~keep]) < 2e-2

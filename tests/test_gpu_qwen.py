@@ -155,3 +155,31 @@ def test_config5_one_block_q4k(cuda):
     ref = Q.forward(W, cfg, x[0], 700.0, txt[0], mk[0].astype(bool), hh, ww)
     got = m.forward(t(x, cuda), 700.0, t(txt, cuda), t(mk, cuda), hh, ww).cpu().numpy()[0]
     assert rel_l2(got, ref) < 1e-2
+
+
+def test_tiny_qwen_denoise_inpaint_and_progress(cuda):
+    """The Qwen step loop with the flow-matching inpaint blend at sigma_next and per-step
+    progress (qwen_image/pipeline.rs:2708-2724) through mb_qwen_denoise_ex, CFG batch 2."""
+    W = Q.synth_weights(TINY, seed=6, qtype=oracle.GGML_Q4_K)
+    m = to_model(TINY, W, 64, 256)
+    hh, ww, lt = 8, 10, 32
+    latent = oracle.randn(72, (TINY.out_channels, 2 * hh, 2 * ww))
+    orig = oracle.randn(73, latent.shape)
+    mask = np.broadcast_to((np.random.default_rng(4).random((1, 2 * hh, 2 * ww)) < 0.5), latent.shape)
+    mask = np.ascontiguousarray(mask, dtype=np.float32)
+    txt = oracle.randn(74, (2, lt, TINY.joint_attention_dim))
+    mk = masks(lt)
+    sig = Q.scheduler_sigmas(4, hh * ww)
+    ref = Q.denoise(W, TINY, latent, txt[0], mk[0].astype(bool), sig, txt[1], mk[1].astype(bool), 4.0,
+                    inpaint=(mask, orig, latent))
+    seen = []
+    gi = t(F.patchify(latent), cuda)
+    m.denoise(gi, t(txt, cuda), t(mk, cuda), hh, ww, sig, 4.0,
+              inpaint=(t(F.patchify(mask), cuda), t(F.patchify(orig), cuda), t(F.patchify(latent), cuda)),
+              on_step=lambda step, total: seen.append(step))
+    torch.cuda.synchronize()
+    got = F.unpack(gi.cpu().numpy(), 2 * hh, 2 * ww)
+    assert seen == [1, 2, 3, 4]
+    assert rel_l2(got, ref) < 2e-2
+    keep = mask == 0  # the last sigma is 0: preserved pixels hold the original exactly
+    assert np.allclose(got[keep], orig[keep], atol=1e-6)

@@ -75,3 +75,17 @@ def test_key_order_permutation():
     assert (pos[:7][~mask.bool()] >= nv).all()         # masked keys after the valid prefix
     pos, nv = key_order(torch.zeros(3, dtype=torch.uint8), 2)
     assert nv == 2 and pos.tolist() == [2, 3, 4, 0, 1]
+
+
+def test_inpaint_blend_known_answers():
+    """img2img.rs:346-362: mask 0 restores orig * (1 - sigma) + noise * sigma; mask 1 keeps the
+    current latent (flux/transformer.rs:79-87 is the same blend)."""
+    from oracle import flux_ref as F
+    cur = np.array([100.0, 200.0], np.float32)
+    orig = np.array([2.0, 4.0], np.float32)
+    noise = np.array([10.0, 20.0], np.float32)
+    assert F.inpaint_blend(cur, (np.zeros(2, np.float32), orig, noise), 0.25).tolist() == [4.0, 8.0]
+    assert F.inpaint_blend(cur, (np.ones(2, np.float32), orig, noise), 0.25).tolist() == [100.0, 200.0]
+    # flow_match_interpolate_blends_encoded_and_noise (img2img.rs:172-190): sigma 0 and 0.5
+    assert F.inpaint_blend(cur, (np.zeros(2, np.float32), orig, noise), 0.0).tolist() == [2.0, 4.0]
+    assert F.inpaint_blend(cur, (np.zeros(2, np.float32), orig, noise), 0.5).tolist() == [6.0, 12.0]
