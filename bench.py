@@ -53,8 +53,9 @@ def parse():
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline sample")
     ap.add_argument("--kernels-only", action="store_true", help="only the standalone kernel timings (profiling)")
     ap.add_argument("--kernel", default="gemm,attention",
-                    help="with --kernels-only: comma list of gemm, attention, gemv, ln_modulate, qk_norm_rope, "
-                         "dequant (the HBM-bound ones at the FLUX step's shapes, L2 flushed between launches)")
+                    help="with --kernels-only: comma list of gemm, attention, gemm_qwen_mlp0, gemv, ln_modulate, "
+                         "qk_norm_rope, dequant (the HBM-bound ones at the FLUX step's shapes, L2 flushed between "
+                         "launches)")
     ap.add_argument("--sweep", action="store_true",
                     help="BASELINE config 2: the Q4_K dequant-GEMM over the ten FLUX linear shapes, one JSON line each")
     return ap.parse_args()
@@ -436,13 +437,14 @@ def time_attention(L, H, device, reps=20):
 
 def _events_ms(fn, reps, flush, st):
     """Median CUDA-event time of fn() on stream st over `reps` launches, each preceded (outside the
-    timed pair of events) by a write of `flush` (256 MB, larger than L2)."""
+    timed pair of events) by a read of `flush` (256 MB, larger than L2): the launch finds none of
+    its inputs in L2, and no dirty lines of the flush are written back during it."""
     import torch
     for _ in range(3):
         fn()
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(reps)]
     for e0, e1 in ev:
-        flush.fill_(1.0)
+        flush.sum()
         e0.record(st)
         fn()
         e1.record(st)
@@ -570,7 +572,7 @@ SWEEP_KN = (("qkv", 3072, 9216), ("mlp_in", 3072, 12288), ("mlp_out", 12288, 307
 def sweep(args, local, peaks, reps=10):
     """Q4_K dequant-GEMM over M x (K->N) of BASELINE config 2 (weights quantized from N(0, 0.02),
     bf16 N(0, 1) activations, seed 0). Each launch is timed alone with CUDA events on the launching
-    stream after 3 warm-ups; a 256 MB buffer is written between launches so that every launch reads
+    stream after 3 warm-ups; a 256 MB buffer is read between launches so that every launch reads
     its weight and activations from HBM (L2 flushed), and the median of `reps` launches is kept."""
     import torch
     import mold_b200 as mb
@@ -590,7 +592,7 @@ def sweep(args, local, peaks, reps=10):
                 w.forward(x, out=y)
             ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(reps)]
             for e0, e1 in ev:
-                flush.fill_(1.0)
+                flush.sum()  # a 256 MB read: L2 holds none of the launch's inputs
                 e0.record(st)
                 w.forward(x, out=y)
                 e1.record(st)
@@ -602,7 +604,7 @@ def sweep(args, local, peaks, reps=10):
                               "N": N, "ms": ms, "tflops": flops / ms / 1e9,
                               "frac_of_burst": flops / ms / 1e9 / peaks["bf16_tflops"],
                               "peak": peaks["bf16_tflops"], "peak_source": peaks["source"],
-                              "algorithmic_bytes": alg, "gbs": alg / ms / 1e6, "l2": "flushed between launches"}),
+                              "algorithmic_bytes": alg, "gbs": alg / ms / 1e6, "l2": "flushed (256 MB read) between launches"}),
                   flush=True)
         del w
     if mb.device_status() != 0:
@@ -642,6 +644,9 @@ def main():
             k["gemm_linear1"] = time_gemm(raw, gtype, (3 * 3072 + 12288, 3072), L_TXT + L_IMG, local, 5)
         if "attention" in want:
             k["attention"] = time_attention(L_TXT + L_IMG, 24, local, 5)
+        if "gemm_qwen_mlp0" in want:  # Qwen-Image img_mlp.net.0.proj over the CFG batch's 2 x 4096 rows
+            wq = qfn(torch.randn((12288, 3072), generator=g, device=dev) * 0.02)
+            k["gemm_qwen_mlp0"] = time_gemm(wq, gtype, (12288, 3072), 2 * L_IMG, local, 5)
         k.update(time_hbm_kernels(want, raw, gtype, qfn, local, peaks))
         if rank == 0:
             print(json.dumps({"kernels": k}), flush=True)
@@ -675,8 +680,8 @@ def main():
     kern = None
     if rank == 0:
         kern = time_kernels(keep, local, peaks)
-        kern.update(time_hbm_kernels({"gemv", "ln_modulate", "qk_norm_rope"}, None, None, quantizer(args.quant)[1],
-                                     local, peaks))
+        gtype, qfn, _ = quantizer(args.quant)
+        kern.update(time_hbm_kernels({"gemv", "ln_modulate", "qk_norm_rope"}, None, gtype, qfn, local, peaks))
     img = img0.clone()
     st = torch.cuda.current_stream()
     # warm-up: first call captures the step graph, then W replays
@@ -868,7 +873,10 @@ def main_qwen(args, world, rank, local, dev, peaks):
             cpu = {"value": None, "unit": "steps/s", "cores": None, "kind": "port", "sample": f"failed: {ex}"}
     g = kern["gemm_mlp0"]
     roof = {"bound": "tensor", "achieved": g["tflops"], "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
-            "frac": g["tflops"] / peaks["bf16_tflops"], "traffic": None,
+            "frac": g["tflops"] / peaks["bf16_tflops"],
+            "traffic": profiled_traffic("k_qgemm_q4k_qwen_mlp0_8192x12288x3072.md") if args.quant == "q4_k" else None,
+            "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, one launch of the same shape "
+                              "(profiles/k_qgemm_q4k_qwen_mlp0_8192x12288x3072.md)",
             "algorithmic_bytes": g["weight_bytes"] + g["act_bytes"],
             "kernel": "k_qgemm<%s> img_mlp.net.0.proj M=8192 N=12288 K=3072" % args.quant.upper(),
             "peak_source": peaks["source"] + " bf16_tflops (burst; kernel timed alone)"}

@@ -41,8 +41,6 @@ constexpr float kRescaleThreshold = 8.f;
 constexpr int kPolyPerChunk = MB_ATTN_POLY;  // of every 32 exponentials, this many use the FMA-pipe polynomial
 
 struct Params {
-  unsigned long long* trace;  // builds with -DMB_TRACE only: summed wait cycles per role (see AW)
-  int ablate;                 // builds with -DMB_TRACE only: 1 no S loads, 2 no P stores, 4 no exp
   int H, Lq, Lk, n_valid, n_kv;
   __nv_bfloat16* out;   // rows [0, split)
   __nv_bfloat16* out2;  // rows [split, Lq), from its row 0
@@ -126,24 +124,6 @@ MB_DEV void umma_ts_elect(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint
 }
 
 
-#ifdef MB_TRACE
-#define AABL(bit) ((p.ablate & (bit)) != 0)
-#else
-#define AABL(bit) false
-#endif
-#ifdef MB_TRACE
-// Slots: 0 TMA kv_empty, 1 MMA v_full, 2 MMA p_full[0], 3 MMA k_full, 4 MMA p_full[1], 5 softmax(t0)
-// s_full, 6 softmax(t0) total, 7 MMA total, 8 softmax(t1) s_full.
-#define AW(slot, call)                                     \
-  ([&]() {                                                 \
-    const long long t0__ = clock64();                      \
-    const bool r__ = (call);                               \
-    tr_[slot] += (unsigned long long)(clock64() - t0__);   \
-    return r__;                                            \
-  }())
-#else
-#define AW(slot, call) (call)
-#endif
 
 __global__ void __launch_bounds__(kThreads, 1)
     k_attention(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
@@ -168,10 +148,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int h = blockIdx.y, q0 = blockIdx.x * (NT * BQ);
   const int n_kv = p.n_kv;
-#ifdef MB_TRACE
-  unsigned long long tr_[16] = {};
-  const long long t_start_ = clock64();
-#endif
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -211,7 +187,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int j = 0; j < n_kv; j++) {
         const int s = j & 1;
         const uint32_t ph = (j >> 1) & 1;
-        if (!AW(0, mbar_wait(&kv_empty[s], ph ^ 1, abort_flag, p.status, kDevTimeoutAttn))) break;
+        if (!(mbar_wait(&kv_empty[s], ph ^ 1, abort_flag, p.status, kDevTimeoutAttn))) break;
         mbar_expect_tx(&k_full[s], kTile);
         tma_load_3d(sK + s * kTile, &tk, &k_full[s], 0, j * BKV, h);
         tma_load_3d(sK + s * kTile + kHalf, &tk, &k_full[s], 64, j * BKV, h);
@@ -232,9 +208,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool ok = mbar_wait(q_full, 0, abort_flag, p.status, kDevTimeoutAttn);
     // S_t(g) = Q_t K_g^T (64 keys) into S half g & 1
     auto issue_s = [&](int g) {
-#ifdef MB_TRACE
-      const long long ti0 = clock64();
-#endif
       const int hh = g & 1;
       {
         const uint32_t ka = smem_u32(sK + ((g >> 1) & 1) * kTile) + hh * 8192;
@@ -247,15 +220,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) umma_commit(&s_full[t * 2 + hh]);
       }
       __syncwarp();
-#ifdef MB_TRACE
-      if (t == 0) tr_[9] += (unsigned long long)(clock64() - ti0);
-#endif
     };
     // O_t += P_t(g) V_g with P read from TMEM (bf16 pairs over the first 32 columns of S half g & 1)
     auto issue_pv = [&](int g) {
-#ifdef MB_TRACE
-      const long long ti0 = clock64();
-#endif
       const int hh = g & 1;
       {
         const uint32_t va = smem_u32(sV + ((g >> 1) & 1) * kTile);
@@ -272,9 +239,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       __syncwarp();
-#ifdef MB_TRACE
-      if (t == 0) tr_[10] += (unsigned long long)(clock64() - ti0);
-#endif
     };
     if (ok && n_kv > 0) {
       if ((ok = mbar_wait(&k_full[0], 0, abort_flag, p.status, kDevTimeoutAttn))) {
@@ -285,14 +249,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int g = 0; g < n_sub && ok; g++) {
       const int hh = g & 1, j = g >> 1;
-      if (hh == 0 && !(ok = AW(1, mbar_wait(&v_full[j & 1], (j >> 1) & 1, abort_flag, p.status, kDevTimeoutAttn))))
+      if (hh == 0 && !(ok = (mbar_wait(&v_full[j & 1], (j >> 1) & 1, abort_flag, p.status, kDevTimeoutAttn))))
         break;
-      if (!(ok = AW(2, mbar_wait(&p_full[t * 2 + hh], j & 1, abort_flag, p.status, kDevTimeoutAttn)))) break;
+      if (!(ok = (mbar_wait(&p_full[t * 2 + hh], j & 1, abort_flag, p.status, kDevTimeoutAttn)))) break;
       tc_fence_after();
       issue_pv(g);
       if (g + 2 < n_sub) {
         if (hh == 0 &&
-            !(ok = AW(3, mbar_wait(&k_full[(j + 1) & 1], ((j + 1) >> 1) & 1, abort_flag, p.status, kDevTimeoutAttn))))
+            !(ok = (mbar_wait(&k_full[(j + 1) & 1], ((j + 1) >> 1) & 1, abort_flag, p.status, kDevTimeoutAttn))))
           break;
         tc_fence_after();
         issue_s(g + 2);
@@ -300,9 +264,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     if (ok && lane == 0) umma_commit(&o_full[t]);
     __syncwarp();
-#ifdef MB_TRACE
-    tr_[7] = (unsigned long long)(clock64() - t_start_);
-#endif
   } else if (warp >= 4 && warp < 12) {
     // ---------------------------------------------------------------- softmax
     // 4 warps per tile; thread = query row = TMEM lane (warp w may only touch lanes 32 (w % 4) ..).
@@ -315,35 +276,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool ok = true;
     for (int g = 0; g < 2 * n_kv; g++) {
       const int hh = g & 1;
-      if (!(ok = AW(t ? 8 : 5, mbar_wait(&s_full[t * 2 + hh], (g >> 1) & 1, abort_flag, p.status, kDevTimeoutAttn))))
+      if (!(ok = (mbar_wait(&s_full[t * 2 + hh], (g >> 1) & 1, abort_flag, p.status, kDevTimeoutAttn))))
         break;
       tc_fence_after();
       const uint32_t tSh = tS + hh * 64;
       const int valid = p.n_valid - g * 64;  // keys >= valid are masked
-#ifdef MB_TRACE
-      long long tph = clock64();
-#define APH(slot)                                  \
-  do {                                             \
-    const long long n__ = clock64();               \
-    if (t == 0) tr_[slot] += (unsigned long long)(n__ - tph); \
-    tph = n__;                                     \
-  } while (0)
-#else
-#define APH(slot) \
-  do {            \
-  } while (0)
-#endif
       uint32_t v[2][32];
-      if (AABL(1)) {
-#pragma unroll
-        for (int c = 0; c < 2; c++)
-#pragma unroll
-          for (int i = 0; i < 32; i++) v[c][i] = __float_as_uint((float)(i + c));
-      } else {
-        tmem_ld32(tSh, v[0]);
-        tmem_ld32(tSh + 32, v[1]);
-        tmem_wait_ld();
-      }
+      tmem_ld32(tSh, v[0]);
+      tmem_ld32(tSh + 32, v[1]);
+      tmem_wait_ld();
       if (valid < 64) {
 #pragma unroll
         for (int c = 0; c < 2; c++)
@@ -351,7 +292,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int i = 0; i < 32; i++)
             if (c * 32 + i >= valid) v[c][i] = __float_as_uint(-INFINITY);
       }
-      APH(11);
       // row max of the 64 keys: two independent max3 chains
       float mc[2];
 #pragma unroll
@@ -361,7 +301,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int i = 2; i < 32; i += 2) mc[c] = max3(mc[c], __uint_as_float(v[c][i]), __uint_as_float(v[c][i + 1]));
       }
       const float mx = fmaxf(mc[0], mc[1]);
-      APH(12);
       const float m_new = fmaxf(m_run, mx * kScaleLog2);
       // lazy rescale: only rows whose max grew by more than 2^8 move their reference point
       const bool need = g == 0 || m_new > m_run + kRescaleThreshold;
@@ -378,9 +317,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int i = 0; i < 16; i++) {
           const uint64_t x2 = fma2(pk2(__uint_as_float(v[c][2 * i]), __uint_as_float(v[c][2 * i + 1])), sc2, nm2);
           float e0, e1;
-          if (AABL(4)) {
-            up2(x2, e0, e1);
-          } else if (2 * i < kPolyPerChunk) {
+          if (2 * i < kPolyPerChunk) {
             exp2_poly3(x2, e0, e1);
           } else {
             float x0, x1;
@@ -391,9 +328,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           sum2 = add2(sum2, pk2(e0, e1));
           pk[i] = pack_bf16x2(e0, e1);
         }
-        if (!AABL(2)) tmem_st16a(tSh + c * 16, pk);
+        tmem_st16a(tSh + c * 16, pk);
       }
-      APH(13);
       float sa, sb;
       up2(sum2, sa, sb);
       if (g > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
@@ -416,7 +352,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_full[t * 2 + hh]);
-      APH(14);
     }
     if (ok) ok = mbar_wait(&o_full[t], 0, abort_flag, p.status, kDevTimeoutAttn);
     if (ok) {
@@ -443,16 +378,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
-#ifdef MB_TRACE
-    if (t == 0) tr_[6] = (unsigned long long)(clock64() - t_start_);
-#endif
   }
 
-#ifdef MB_TRACE
-  if (p.trace && lane == 0 && (warp <= 1 || warp == 4 || warp == 8))
-    for (int i = 0; i < 16; i++)
-      if (tr_[i]) atomicAdd(p.trace + i, tr_[i]);
-#endif
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
@@ -463,14 +390,6 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 }  // namespace attn
 
-#ifdef MB_TRACE
-unsigned long long* g_attn_trace = nullptr;
-int g_attn_ablate = 0;
-extern "C" __attribute__((visibility("default"))) void mb_debug_set_attn_ablate(int f) { g_attn_ablate = f; }
-extern "C" __attribute__((visibility("default"))) void mb_debug_set_attn_trace(unsigned long long* buf) {
-  g_attn_trace = buf;
-}
-#endif
 
 cudaError_t launch_attention(const void* q, const void* k, const void* v, int H, int64_t Lq, int64_t Lk,
                              int64_t n_valid, void* out, int64_t ldo, cudaStream_t st, int64_t split_row,
@@ -496,13 +415,6 @@ cudaError_t launch_attention(const void* q, const void* k, const void* v, int H,
   p.split = (split_row < 0 || split_row > Lq) ? (int)Lq : (int)split_row;
   p.ldo = ldo;
   p.status = device_status_ptr();
-#ifdef MB_TRACE
-  p.trace = g_attn_trace;
-  p.ablate = g_attn_ablate;
-#else
-  p.trace = nullptr;
-  p.ablate = 0;
-#endif
   static int attr_done[64];
   int dev = 0;
   cudaGetDevice(&dev);

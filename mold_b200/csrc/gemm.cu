@@ -107,29 +107,7 @@ struct Params {
   int nprob;
   int n_tiles;
   int* status;
-  int ablate;  // builds with -DMB_TRACE only: 1 decode, 2 X loads, 4 raw loads, 8 TMEM stores, 16 epilogue,
-              // 32 drain staging stores, 64 drain arithmetic
-  unsigned long long* trace;  // builds with -DMB_TRACE only: summed wait cycles per role (see TW)
 };
-
-#ifdef MB_TRACE
-#define ABL(bit) ((p.ablate & (bit)) != 0)
-// Cycles lane 0 of a role spends in a wait, accumulated in tr_[slot] and summed over CTAs at
-// exit. Slots: 0 TMA empty, 1 TMA r_empty, 2 MMA acc_empty, 3 MMA full, 4 epilogue drain,
-// 5 decode r_full, 6 decode empty, 7 epilogue acc_full, 8 MMA role total, 9/10 drain phases,
-// 11 MMA issue, 12/13 MMA full waits in the first 4 / later stages of a tile, 14/15 decode
-// compute / TMEM store + arrive of one decoder warp.
-#define TW(slot, call)                          \
-  ([&]() {                                      \
-    const long long t0__ = clock64();           \
-    const bool r__ = (call);                    \
-    tr_[slot] += (unsigned long long)(clock64() - t0__); \
-    return r__;                                 \
-  }())
-#else
-#define ABL(bit) false
-#define TW(slot, call) (call)
-#endif
 
 // ---- packed f32x2 arithmetic (sm_100): two IEEE single-precision ops per instruction ----
 MB_DEV uint64_t f2(float a, float b) {
@@ -437,10 +415,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int tile_step = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
   constexpr int kTileN = PAIR ? 2 * TN : TN;  // weight rows per tile
   constexpr uint32_t kPairArrivals = PAIR ? 2 : 1;
-#ifdef MB_TRACE
-  unsigned long long tr_[16] = {};
-  const long long t_start_ = clock64();
-#endif
   // problem of a global tile index and the tile's origin within it
 #define TILE_SETUP(tile)                                                   \
   const int pi_ = (p.nprob > 1 && (tile) >= p.pr[1].tile0) ? 1 : 0;      \
@@ -498,13 +472,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int m0 = (lt_ % P.tiles_m) * TM + (int)rank * (TM / 2);
         for (int ks = 0; ks < nks && ok; ks++, it++) {
           const uint32_t sx = it % SX, px = (it / SX) & 1;
-          if (!(ok = TW(0, mbar_wait(&empty[sx], px ^ 1, abort_flag, p.status, kDevTimeoutGemm)))) break;
+          if (!(ok = (mbar_wait(&empty[sx], px ^ 1, abort_flag, p.status, kDevTimeoutGemm)))) break;
           if constexpr (PAIR) {
             // both halves complete on the leader's barrier, which expects the pair's bytes
             if (leader) mbar_expect_tx(&full[sx], 2 * kXS);
             tma_load_2d_pair(xs + sx * kXS, tm_x, smem_in_cta(&full[sx], 0), ks * BK, m0);
-          } else if (ABL(2)) {
-            mbar_arrive(&full[sx]);
           } else {
             mbar_expect_tx(&full[sx], kXS);
             tma_load_2d(xs + sx * kXS, tm_x, &full[sx], ks * BK, m0);
@@ -520,11 +492,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int ks = 0; ks < nks && ok; ks += kSPC) {  // one raw chunk (kSPC stages) per 128-row block
           const uint32_t sr = ic % kSR, pr = (ic / kSR) & 1;
           ic++;
-          if (!(ok = TW(1, mbar_wait(&r_empty[sr], pr ^ 1, abort_flag, p.status, kDevTimeoutGemm)))) break;
-          if (ABL(4)) {
-            mbar_arrive(&r_full[sr]);
-            continue;
-          }
+          if (!(ok = (mbar_wait(&r_empty[sr], pr ^ 1, abort_flag, p.status, kDevTimeoutGemm)))) break;
           mbar_expect_tx(&r_full[sr], kRawStage);
           uint8_t* rdst = rs + sr * kRawStage;
           if (WT == MB_GGML_Q8_0) {  // 16-bit elements
@@ -544,19 +512,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool ok = true;
     for (int tile = tile_first; tile < n_tiles && ok && leader; tile += tile_step, tcount++) {
       TILE_SETUP(tile);
-      if (!(ok = TW(2, PAIR ? mbar_wait_cl(acc_empty, (tcount & 1) ^ 1, abort_flag, p.status, kDevTimeoutGemm)
+      if (!(ok = (PAIR ? mbar_wait_cl(acc_empty, (tcount & 1) ^ 1, abort_flag, p.status, kDevTimeoutGemm)
                             : mbar_wait(acc_empty, (tcount & 1) ^ 1, abort_flag, p.status, kDevTimeoutGemm))))
         break;
       tc_fence_after();
       for (int ks = 0; ks < nks; ks++, it++) {
         const uint32_t sx = it % SX, px = (it / SX) & 1, sa = sx;
-        if (!(ok = TW(ks < 4 ? 12 : 13, PAIR ? mbar_wait_cl(&full[sx], px, abort_flag, p.status, kDevTimeoutGemm)
+        if (!(ok = (PAIR ? mbar_wait_cl(&full[sx], px, abort_flag, p.status, kDevTimeoutGemm)
                                              : mbar_wait(&full[sx], px, abort_flag, p.status, kDevTimeoutGemm))))
           break;
         tc_fence_after();
-#ifdef MB_TRACE
-        const long long ti0 = clock64();
-#endif
         {
           // The whole (converged) warp runs the issue sequence and lane 0 issues the stage's four
           // MMAs under one elect.sync (umma_ts_stage4): every instruction of the issuer costs
@@ -575,9 +540,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
         __syncwarp();
-#ifdef MB_TRACE
-        tr_[11] += (unsigned long long)(clock64() - ti0);
-#endif
       }
       if (!ok) break;
       if (lane == 0) {
@@ -588,9 +550,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       __syncwarp();
     }
-#ifdef MB_TRACE
-    tr_[8] = (unsigned long long)(clock64() - t_start_);
-#endif
   } else if (warp < 2 + kDW) {
     // ------------------------------------------------ dequant: raw GGML -> bf16 -> TMEM
     const int q = warp & 3;               // TMEM lane quarter
@@ -599,11 +558,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t lane_addr = (uint32_t)(q * 32) << 16;
     uint32_t it = 0, ic = 0;
     bool ok = true;
+#ifdef MB_DEC_PIPE
+    int pend_sa = -1;  // stage whose TMEM store is in flight (its full arrival deferred)
+#endif
     for (int tile = tile_first; tile < n_tiles && ok; tile += tile_step) {
       TILE_SETUP(tile);
       for (int kc = 0; kc < nks / kSPC && ok; kc++, ic++) {
         const uint32_t sr = ic % kSR, pr = (ic / kSR) & 1;
-        if (!(ok = TW(5, mbar_wait(&r_full[sr], pr, abort_flag, p.status, kDevTimeoutGemm)))) break;
+        if (!(ok = (mbar_wait(&r_full[sr], pr, abort_flag, p.status, kDevTimeoutGemm)))) break;
         const uint8_t* R = rs + sr * kRawStage;
         // Q4_K: this thread's four sub-blocks (2j + hh, j = 0..3) of the super-block, decoded once.
         // High nibbles (hh = 1) are used in place (16 q) with the scale divided by 16: still exact.
@@ -624,14 +586,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int j = 0; j < kSPC; j++, it++) {
           const int ks = kc * kSPC + j;
           const uint32_t sa = it % SX, pa = (it / SX) & 1;
-#ifdef MB_TRACE
-          const long long td0 = clock64();
-#endif
           uint32_t o[16];
-          if (ABL(1)) {
-#pragma unroll
-            for (int i = 0; i < 16; i++) o[i] = 0x3c003c00u ^ (uint32_t)(ks + i);
-          } else if constexpr (WT == MB_GGML_Q4_K) {
+          if constexpr (WT == MB_GGML_Q4_K) {
             const uint4* qp = (const uint4*)(R + r * 144 + 16 + 32 * j);
             const uint4 qa = qp[0], qb = qp[1];
             const float d1 = d1v[j], m1 = m1v[j];
@@ -674,18 +630,27 @@ __global__ void __launch_bounds__(kThreads, 1)
             __syncwarp();
             if (lane == 0) mbar_arrive(&r_empty[sr]);
           }
-#ifdef MB_TRACE
-          tr_[14] += (unsigned long long)(clock64() - td0);
-#endif
-          if (!(ok = TW(6, mbar_wait(&empty[sa], pa ^ 1, abort_flag, p.status, kDevTimeoutGemm)))) break;
-#ifdef MB_TRACE
-          const long long td1 = clock64();
-#endif
-          tc_fence_after();
-          if (!ABL(8)) {
-            tmem_st16(tmem + lane_addr + kTmemA + sa * 32 + hh * 16, o);
+#ifdef MB_DEC_PIPE
+          if (pend_sa >= 0) {
             tmem_wait_st();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) {
+              if constexpr (PAIR)
+                mbar_arrive_cluster(smem_in_cta(&full[pend_sa], 0));
+              else
+                mbar_arrive(&full[pend_sa]);
+            }
           }
+          if (!(ok = (mbar_wait(&empty[sa], pa ^ 1, abort_flag, p.status, kDevTimeoutGemm)))) break;
+          tc_fence_after();
+          tmem_st16(tmem + lane_addr + kTmemA + sa * 32 + hh * 16, o);
+          pend_sa = (int)sa;
+#else
+          if (!(ok = (mbar_wait(&empty[sa], pa ^ 1, abort_flag, p.status, kDevTimeoutGemm)))) break;
+          tc_fence_after();
+          tmem_st16(tmem + lane_addr + kTmemA + sa * 32 + hh * 16, o);
+          tmem_wait_st();
           tc_fence_before();
           __syncwarp();
           if (lane == 0) {
@@ -694,12 +659,23 @@ __global__ void __launch_bounds__(kThreads, 1)
             else
               mbar_arrive(&full[sa]);
           }
-#ifdef MB_TRACE
-          tr_[15] += (unsigned long long)(clock64() - td1);
 #endif
         }
       }
     }
+#ifdef MB_DEC_PIPE
+    if (ok && pend_sa >= 0) {
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        if constexpr (PAIR)
+          mbar_arrive_cluster(smem_in_cta(&full[pend_sa], 0));
+        else
+          mbar_arrive(&full[pend_sa]);
+      }
+    }
+#endif
   } else {
     // ------------------------------------------------ epilogue (thread = output feature n)
     // both CTAs of a pair release the accumulator on the leader's barrier
@@ -723,21 +699,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool nvalid = n < P.N;
       const float bias = (nvalid && e.bias) ? e.bias[n] : 0.f;
       const float gate = (nvalid && e.kind == MB_EPI_GATE_RESIDUAL) ? e.gate[n] : 0.f;
-      if (!(ok = TW(7, mbar_wait(acc_full, tcount & 1, abort_flag, p.status, kDevTimeoutGemm)))) break;
+      if (!(ok = (mbar_wait(acc_full, tcount & 1, abort_flag, p.status, kDevTimeoutGemm)))) break;
       tc_fence_after();
-#ifdef MB_TRACE
-      const long long t_drain_ = clock64();
-#define DRAIN_DONE() (tr_[4] += (unsigned long long)(clock64() - t_drain_))
-#else
-#define DRAIN_DONE() ((void)0)
-#endif
       const bool do_gelu = e.kind == MB_EPI_GELU_TANH && n >= e.gelu_from;
       const bool fast_bf16 = e.out_bf16 && e.kind != MB_EPI_GATE_RESIDUAL && (P.N & 1) == 0;
-      if (ABL(16)) {
-        __syncwarp();
-        if (lane == 0) release_acc(acc_empty);
-        DRAIN_DONE();
-      } else if (fast_bf16) {
+      if (fast_bf16) {
         // bf16 output: pack the warp's 128 accumulator columns to bf16 pairs (rows m, m+1 of
         // feature n), park them in the TMEM staging columns, free the accumulator, then read them
         // back 16 words at a time and store 32-bit words: lanes 2j / 2j+1 exchange halves so each
@@ -746,45 +712,24 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll 1
         for (int c = 0; c < 4; c++) {
           uint32_t v[32];
-#ifdef MB_TRACE
-          const long long tl0 = clock64();
-#endif
           tmem_ld32(tmem + lane_addr + ch * 128 + c * 32, v);
           tmem_wait_ld();
-#ifdef MB_TRACE
-          tr_[9] += (unsigned long long)(clock64() - tl0);
-#endif
           uint32_t o[16];
-          if (ABL(64)) {
 #pragma unroll
-            for (int j = 0; j < 16; j++) o[j] = v[2 * j] ^ v[2 * j + 1];
-          } else {
-#pragma unroll
-            for (int j = 0; j < 16; j++) {
-              float a0 = __uint_as_float(v[2 * j]) + bias, a1 = __uint_as_float(v[2 * j + 1]) + bias;
-              if (do_gelu) {
-                a0 = gelu_tanh(a0);
-                a1 = gelu_tanh(a1);
-              }
-              o[j] = pack_bf16x2(a0, a1);
+          for (int j = 0; j < 16; j++) {
+            float a0 = __uint_as_float(v[2 * j]) + bias, a1 = __uint_as_float(v[2 * j + 1]) + bias;
+            if (do_gelu) {
+              a0 = gelu_tanh(a0);
+              a1 = gelu_tanh(a1);
             }
+            o[j] = pack_bf16x2(a0, a1);
           }
-#ifdef MB_TRACE
-          const long long tc1 = clock64();
-#endif
-          if (!ABL(32)) tmem_st16(stage + c * 16, o);
-#ifdef MB_TRACE
-          tr_[3] += (unsigned long long)(clock64() - tc1);  // slot 3: drain staging-store issue
-#endif
+          tmem_st16(stage + c * 16, o);
         }
         tmem_wait_st();
-#ifdef MB_TRACE
-        tr_[10] += (unsigned long long)(clock64() - t_drain_);
-#endif
         tc_fence_before();
         __syncwarp();
         if (lane == 0) release_acc(acc_empty);
-        DRAIN_DONE();
         const bool odd = lane & 1;
         const int ncol = n - (odd ? 1 : 0);  // even feature of the pair this lane writes
 #pragma unroll 1
@@ -822,7 +767,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) release_acc(acc_empty);
-        DRAIN_DONE();
         // y usually aliases res: issue a batch of 16 residual loads before any store so their
         // latencies overlap (the compiler cannot reorder loads past aliasing stores). The TMEM
         // reads stay warp-uniform; only the global accesses depend on the lane's feature.
@@ -859,7 +803,6 @@ __global__ void __launch_bounds__(kThreads, 1)
             tc_fence_before();
             __syncwarp();
             if (lane == 0) release_acc(acc_empty);
-        DRAIN_DONE();
           }
           const int mb = m0 + c * 32;
           if (nvalid) {
@@ -886,11 +829,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
 
-#ifdef MB_TRACE
-  if (p.trace && (lane == 0 || (warp == 0 && lane == 1)) && (warp <= 2 || warp == 2 + kDW))
-    for (int i = 0; i < 16; i++)
-      if (tr_[i]) atomicAdd(p.trace + i, tr_[i]);
-#endif
   tc_fence_before();
   __syncthreads();
   // a pair's CTAs stay resident until neither can still be reached by the other's arrivals,
@@ -905,8 +843,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-int g_gemm_ablate = 0;
-unsigned long long* g_gemm_trace = nullptr;
 
 template <int WT, bool PAIR>
 bool make_maps(const mb_weight* w, const void* x, int64_t M, int64_t ldx, CUtensorMap* tx, CUtensorMap* tw) {
@@ -959,8 +895,6 @@ cudaError_t launch_t(int n, const GemmProblem* g, cudaStream_t st) {
   p.nprob = n;
   p.n_tiles = tiles;
   p.status = device_status_ptr();
-  p.ablate = g_gemm_ablate;
-  p.trace = g_gemm_trace;
   constexpr size_t smem = smem_bytes<WT, PAIR>();
   static int attr_done[64];  // per template instance and device: 1 + the co-resident cluster count
   int dev = 0;
@@ -1005,13 +939,6 @@ cudaError_t launch_w(int n, const GemmProblem* g, cudaStream_t st) {
 
 }  // namespace gemm
 
-#ifdef MB_TRACE
-extern "C" __attribute__((visibility("default"))) void mb_debug_set_gemm_ablate(int flags) { gemm::g_gemm_ablate = flags; }
-// Device buffer of 9 u64 counters (NULL = off) that k_qgemm adds its per-role wait cycles to.
-extern "C" __attribute__((visibility("default"))) void mb_debug_set_gemm_trace(unsigned long long* buf) {
-  gemm::g_gemm_trace = buf;
-}
-#endif
 
 cudaError_t launch_qgemm_group(int n, const GemmProblem* g, cudaStream_t st) {
   if (n < 1 || n > 2) return cudaErrorInvalidValue;

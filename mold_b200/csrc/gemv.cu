@@ -17,13 +17,70 @@ constexpr int kWarps = 4;                                 // warps per block
 constexpr int kRowsPerWarp = kGemvRowsPerBlock / kWarps;  // 8
 constexpr int kMaxLen = 4096;
 constexpr int kMaxInputs = 4;
-constexpr int kStageStride = kMaxLen + kMaxLen / 32;  // x, then its 32-value partial sums
+// Per staged input: x, its 32-value partial sums, then x scaled for the Q4_K path (kQ4Off).
+constexpr int kQ4Off = kMaxLen + kMaxLen / 32;
+constexpr int kQ8Off = kQ4Off + kMaxLen;  // x scaled for the Q8_0 path
+constexpr int kStageStride = kQ8Off + kMaxLen;
+
+// Q4_K nibbles become floats without a conversion instruction: OR-ing a nibble that sits at bit
+// position p (p + 4 <= 23) into the mantissa of 2^23 and subtracting 2^23 gives q * 2^p exactly.
+// A 32-bit word of a Q4_K quant run holds, in bytes b = 0..3, the low nibble of value 4I + b
+// (sub-block 2g) and the high nibble of value 32 + 4I + b (sub-block 2g + 1). Taken from the word
+// W at bits 0, 8, 16 (low nibbles of b0..b2) and 4, 12 (high of b0, b1), and from W >> 12 at bits
+// 8, 12, 16 (high of b2, low of b3, high of b3), each value arrives multiplied by a fixed power
+// of two; the staged copy of x carries the inverse power, so the products are exact as before.
+MB_DEV float q4_pos_scale(int j) {  // j = value index within a 64-value unit
+  const bool hi = j >= 32;
+  const int b = j & 3;
+  const int p = hi ? (b == 0 ? 4 : b == 1 ? 12 : b == 2 ? 8 : 16) : (b == 0 ? 0 : b == 1 ? 8 : b == 2 ? 16 : 12);
+  return __int_as_float((127 - p) << 23);  // 2^-p
+}
 
 struct Inputs {
   GemvInput in[kMaxInputs];
 };
 
 MB_DEV float h16(uint32_t v) { return __half2float(__ushort_as_half((unsigned short)(v & 0xFFFFu))); }
+
+// ---- packed f32x2 arithmetic (sm_100): two IEEE single-precision ops per instruction
+MB_DEV uint64_t pk(uint32_t a, uint32_t b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1,%2};" : "=l"(r) : "r"(a), "r"(b));
+  return r;
+}
+MB_DEV uint64_t pkf(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1,%2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+MB_DEV uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+MB_DEV uint64_t sub2(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+MB_DEV float sum2(uint64_t v) {
+  float a, b;
+  asm("mov.b64 {%0,%1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+  return a + b;
+}
+// mask ? (v ^ c) : c in one LOP3: a signed byte of v, offset by 128 (c's bit 7 of the byte
+// flips its sign bit), placed in the mantissa of 2^23 (c holds 0x4B000000 outside the byte).
+MB_DEV uint32_t magic_s8(uint32_t v, uint32_t mask, uint32_t c) {
+  uint32_t r;
+  asm("lop3.b32 %0, %1, %2, %3, 0x6A;" : "=r"(r) : "r"(v), "r"(mask), "r"(c));
+  return r;
+}
+// (v & mask) | 0x4B000000 in one LOP3: the nibble placed in the mantissa of 2^23.
+MB_DEV uint32_t magic(uint32_t v, uint32_t mask) {
+  uint32_t r;
+  asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(r) : "r"(v), "r"(mask), "r"(0x4B000000u));
+  return r;
+}
 
 MB_DEV uint32_t sb(uint32_t sy, uint32_t sz, uint32_t sw, int k) {
   const uint32_t w = k < 4 ? sy : (k < 8 ? sz : sw);
@@ -55,6 +112,11 @@ __global__ void k_gemv_stage(Inputs ins, float* __restrict__ stage) {
       v.x = silu(v.x); v.y = silu(v.y); v.z = silu(v.z); v.w = silu(v.w);
     }
     *(float4*)(xs + i) = v;
+    const int j = i & 63;
+    *(float4*)(xs + kQ4Off + i) = make_float4(v.x * q4_pos_scale(j), v.y * q4_pos_scale(j + 1),
+                                              v.z * q4_pos_scale(j + 2), v.w * q4_pos_scale(j + 3));
+    // Q8_0: bytes 1 and 3 of a word arrive multiplied by 2^8 (see rows_q8)
+    *(float4*)(xs + kQ8Off + i) = make_float4(v.x, v.y * 0.00390625f, v.z, v.w * 0.00390625f);
   }
   __syncthreads();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -99,7 +161,7 @@ MB_DEV void rows_q4k(const GemvJob& job, const float* __restrict__ xs, const flo
   for (int i = 0; i < RPL; i++) acc[i] = 0.f;
   for (int u = sl; u < U; u += LPR) {
     const int kb = u >> 2, g = u & 3;
-    const float4* x4 = (const float4*)(xs + u * 64);
+    const float4* xq4 = (const float4*)(xs + kQ4Off + u * 64);
     const float s_lo = __ldg(xsum + 2 * u), s_hi = __ldg(xsum + 2 * u + 1);
     // rows in batches of RB: all loads of a batch first (rows past the job's end re-read its
     // last row; finish_rows drops them); the unit's x values are read per word (L1) and shared
@@ -115,25 +177,37 @@ MB_DEV void rows_q4k(const GemvJob& job, const float* __restrict__ xs, const flo
         A[j] = __ldg((const uint4*)(b + 16 + 32 * g));
         B[j] = __ldg((const uint4*)(b + 32 + 32 * g));
       }
-      float dlo[RB], dhi[RB];
+      // dot products per row: (low sub-block, high sub-block), each as two packed partial sums
+      uint64_t alo[RB], blo[RB], ahi[RB], bhi[RB];
+      const uint64_t M2 = pkf(8388608.f, 8388608.f);
 #pragma unroll
-      for (int j = 0; j < RB; j++) dlo[j] = dhi[j] = 0.f;
+      for (int j = 0; j < RB; j++) alo[j] = blo[j] = ahi[j] = bhi[j] = 0ull;
 #pragma unroll
       for (int I = 0; I < 8; I++) {
-        const float4 xl = __ldg(x4 + I), xh = __ldg(x4 + 8 + I);
+        const float4 xl = __ldg(xq4 + I), xh = __ldg(xq4 + 8 + I);
+        const uint64_t xl01 = pkf(xl.x, xl.y), xl23 = pkf(xl.z, xl.w);
+        const uint64_t xh01 = pkf(xh.x, xh.y), xh23 = pkf(xh.z, xh.w);
 #pragma unroll
         for (int j = 0; j < RB; j++) {
           const uint32_t W = I < 4 ? (I == 0 ? A[j].x : I == 1 ? A[j].y : I == 2 ? A[j].z : A[j].w)
                                    : (I == 4 ? B[j].x : I == 5 ? B[j].y : I == 6 ? B[j].z : B[j].w);
-          dlo[j] = fmaf((float)(W & 0xFu), xl.x, dlo[j]);
-          dhi[j] = fmaf((float)((W >> 4) & 0xFu), xh.x, dhi[j]);
-          dlo[j] = fmaf((float)((W >> 8) & 0xFu), xl.y, dlo[j]);
-          dhi[j] = fmaf((float)((W >> 12) & 0xFu), xh.y, dhi[j]);
-          dlo[j] = fmaf((float)((W >> 16) & 0xFu), xl.z, dlo[j]);
-          dhi[j] = fmaf((float)((W >> 20) & 0xFu), xh.z, dhi[j]);
-          dlo[j] = fmaf((float)((W >> 24) & 0xFu), xl.w, dlo[j]);
-          dhi[j] = fmaf((float)(W >> 28), xh.w, dhi[j]);
+          const uint32_t W2 = W >> 12;
+          // low nibbles of bytes 0,1 | 2,3 and high nibbles of bytes 0,1 | 2,3 (see q4_pos_scale)
+          const uint64_t l01 = sub2(pk(magic(W, 0xFu), magic(W, 0xF00u)), M2);
+          const uint64_t l23 = sub2(pk(magic(W, 0xF0000u), magic(W2, 0xF000u)), M2);
+          const uint64_t h01 = sub2(pk(magic(W, 0xF0u), magic(W, 0xF000u)), M2);
+          const uint64_t h23 = sub2(pk(magic(W2, 0xF00u), magic(W2, 0xF0000u)), M2);
+          alo[j] = fma2(l01, xl01, alo[j]);
+          blo[j] = fma2(l23, xl23, blo[j]);
+          ahi[j] = fma2(h01, xh01, ahi[j]);
+          bhi[j] = fma2(h23, xh23, bhi[j]);
         }
+      }
+      float dlo[RB], dhi[RB];
+#pragma unroll
+      for (int j = 0; j < RB; j++) {
+        dlo[j] = sum2(alo[j]) + sum2(blo[j]);
+        dhi[j] = sum2(ahi[j]) + sum2(bhi[j]);
       }
 #pragma unroll
       for (int j = 0; j < RB; j++) {
@@ -148,22 +222,28 @@ MB_DEV void rows_q4k(const GemvJob& job, const float* __restrict__ xs, const flo
   finish_rows<LPR>(acc, r0, sub, sl, nr, job);
 }
 
-// Q8_0 rows: unit = one 34-byte block (fp16 d + 32 int8) of 32 values.
+// Q8_0 rows: unit = one 34-byte block (fp16 d + 32 int8) of 32 values. A signed byte at bit
+// position p (0 or 8) of a word becomes a float without a conversion instruction: the byte plus
+// 128 is placed in the mantissa of 2^23 (magic_s8) and 2^23 + 128 * 2^p subtracted, giving
+// q * 2^p exactly; bytes 2 and 3 are taken from the word shifted right by 16, and the staged
+// x (kQ8Off) carries 2^-8 for bytes 1 and 3.
 template <int LPR>
 MB_DEV void rows_q8(const GemvJob& job, const float* __restrict__ xs, int r0, int nr, int lane) {
   constexpr int NSUB = 32 / LPR, RPL = kRowsPerWarp / NSUB, RB = RPL < 4 ? RPL : 4;
   const int sub = lane / LPR, sl = lane % LPR;
   const int U = job.n_cols / 32;
   const uint8_t* wbase = (const uint8_t*)job.w + (int64_t)r0 * job.row_bytes;
+  const uint64_t M8 = pkf(8388608.f + 128.f, 8388608.f + 32768.f);
   float acc[RPL];
 #pragma unroll
   for (int i = 0; i < RPL; i++) acc[i] = 0.f;
   for (int u = sl; u < U; u += LPR) {
-    float x[32];
+    uint64_t x2[16];
 #pragma unroll
     for (int i = 0; i < 8; i++) {
-      const float4 t = __ldg((const float4*)(xs + u * 32) + i);
-      x[4 * i] = t.x; x[4 * i + 1] = t.y; x[4 * i + 2] = t.z; x[4 * i + 3] = t.w;
+      const float4 t = __ldg((const float4*)(xs + kQ8Off + u * 32) + i);
+      x2[2 * i] = pkf(t.x, t.y);
+      x2[2 * i + 1] = pkf(t.z, t.w);
     }
 #pragma unroll
     for (int i0 = 0; i0 < RPL; i0 += RB) {
@@ -181,14 +261,17 @@ MB_DEV void rows_q8(const GemvJob& job, const float* __restrict__ xs, int r0, in
 #pragma unroll
     for (int j = 0; j < RB; j++) {
       const float d = sh[j] ? h16(wv[j][0] >> 16) : h16(wv[j][0]);
-      float sum = 0.f;
+      uint64_t s01 = 0ull, s23 = 0ull;
 #pragma unroll
       for (int k = 0; k < 8; k++) {
         const uint32_t q = sh[j] ? wv[j][k + 1] : __byte_perm(wv[j][k], wv[j][k + 1], 0x5432);
-#pragma unroll
-        for (int t = 0; t < 4; t++) sum = fmaf((float)(int8_t)((q >> (8 * t)) & 0xFF), x[4 * k + t], sum);
+        const uint32_t q2 = q >> 16;
+        const uint64_t v01 = sub2(pk(magic_s8(q, 0xFFu, 0x4B000080u), magic_s8(q, 0xFF00u, 0x4B008000u)), M8);
+        const uint64_t v23 = sub2(pk(magic_s8(q2, 0xFFu, 0x4B000080u), magic_s8(q2, 0xFF00u, 0x4B008000u)), M8);
+        s01 = fma2(v01, x2[2 * k], s01);
+        s23 = fma2(v23, x2[2 * k + 1], s23);
       }
-      acc[i0 + j] += d * sum;
+      acc[i0 + j] += d * (sum2(s01) + sum2(s23));
     }
     }
   }

@@ -9,9 +9,9 @@ oracle needs ~30 s per full-width FLUX forward on a CPU).
     rel-L2 <= 1e-2 of the prediction.
   * The 28-step denoise through mb_flux_denoise with the product's own schedule
     (flux/transformer.rs:50-95): cosine >= 0.999 of the final latent.
-  * Qwen-Image one block at 4096 + 256 tokens with a partial text mask through mb_qwen_forward,
-    and one CFG Euler step through mb_qwen_denoise (cond + uncond prompts with different masks,
-    qwen_image/pipeline.rs:2655-2716): rel-L2 <= 1e-2.
+  * Qwen-Image one block at 4096 + 256 tokens with a partial text mask through mb_qwen_forward
+    (rel-L2 <= 1e-2), and one CFG Euler step through mb_qwen_denoise (cond + uncond prompts with
+    different masks, qwen_image/pipeline.rs:2655-2716): the step's update at cosine >= 0.999.
 
 Both GGUF types of the path (Q4_K and Q8_0) are covered for FLUX; Qwen uses Q4_K."""
 import dataclasses
@@ -185,5 +185,10 @@ def test_qwen_cfg_step_full_width(qwen_case):
     got = F.unpack(gi.cpu().numpy(), 2 * G.HT, 2 * G.WT)
     d_ref = gold["d_cfg_step"].astype(np.float32)
     assert mb.device_status() == 0
-    assert rel_l2(got - latent, d_ref) < 1e-2   # the step's update
+    # The guidance combination u + g (c - u) with g = 4 weighs the two forwards' errors by -3 and 4,
+    # so the step's update carries ~5x the per-forward rel-L2 (which the test above bounds by 1e-2):
+    # the update is held to cosine >= 0.999 and 2.5e-2, the latent after the step to 1e-2.
+    du = (got - latent).ravel()
+    assert float(np.dot(du, d_ref.ravel()) / np.linalg.norm(du) / np.linalg.norm(d_ref)) >= 0.999
+    assert rel_l2(got - latent, d_ref) < 2.5e-2
     assert rel_l2(got, latent + d_ref) < 1e-2

@@ -145,10 +145,11 @@ def test_qlinear_f32_unaligned_rejected(cuda):
 
 # ------------------------------------------------------------------ K3 GEMV
 @pytest.mark.parametrize("t", [oracle.GGML_Q4_K, oracle.GGML_Q8_0])
-def test_qgemv_silu(cuda, t):
-    N, K = 1000, 3072
+@pytest.mark.parametrize("K,xs", [(3072, 1.0), (256, 1.0), (768, 1.0), (4096, 1.0), (3072, 1e3), (3072, 1e-3)])
+def test_qgemv_silu(cuda, t, K, xs):
+    N = 1000
     w, raw = qmat(oracle.randn(19, (N, K), 0.02), t)
-    x = oracle.randn(20, (K,))
+    x = oracle.randn(20, (K,)) * np.float32(xs)
     b = oracle.randn(21, (N,), 0.02)
     ref = F.silu(x.astype(np.float64)) @ oracle.dequantize(raw, t, (N, K)).astype(np.float64).T + b
     y = mb.qgemv(w, torch.from_numpy(x).to(cuda), apply_silu=True, bias=torch.from_numpy(b).to(cuda))
