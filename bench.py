@@ -58,6 +58,8 @@ def parse():
                          "launches)")
     ap.add_argument("--sweep", action="store_true",
                     help="BASELINE config 2: the Q4_K dequant-GEMM over the ten FLUX linear shapes, one JSON line each")
+    ap.add_argument("--sweep-only", default=None, metavar="LINEAR:M",
+                    help="with --sweep: only this shape (e.g. attn_out:1536), for a profiler capture")
     return ap.parse_args()
 
 
@@ -581,11 +583,16 @@ def sweep(args, local, peaks, reps=10):
     flush = torch.empty(64 << 20, dtype=torch.float32, device=dev)
     gtype, qfn, _ = quantizer(args.quant)
     g = torch.Generator(device=dev)
+    only = tuple(args.sweep_only.split(":")) if args.sweep_only else None
     for name, K, N in SWEEP_KN:
+        if only and only[0] != name:
+            continue
         g.manual_seed(WEIGHT_SALT + K * 7 + N)
         raw = qfn(torch.randn((N, K), generator=g, device=dev) * 0.02)
         w = mb.QMatMul.from_device_bytes(raw, gtype, N, K, local)
         for M in SWEEP_M:
+            if only and int(only[1]) != M:
+                continue
             x = torch.randn((M, K), generator=g, device=dev).bfloat16()
             y = torch.empty((M, N), device=dev, dtype=torch.bfloat16)
             for _ in range(3):

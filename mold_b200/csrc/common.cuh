@@ -20,6 +20,7 @@ enum DeviceStatus : int {
   kDevOk = 0,
   kDevTimeoutGemm = 0x100,
   kDevTimeoutAttn = 0x200,
+  kDevTimeoutGemv = 0x300,
 };
 
 // ~2 s at 1.9 GHz: far above any legitimate wait of these kernels.
@@ -72,6 +73,15 @@ MB_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, 
       return false;
     }
   }
+}
+
+// Contiguous global -> shared copy by the bulk-copy engine (no tensor map), completing `bytes`
+// of transactions on `bar`. dst, src and bytes must be multiples of 16.
+MB_DEV void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(dst)),
+               "l"(src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
 }
 
 // ---------------------------------------------------------------- CTA pairs (clusters of 2)

@@ -19,6 +19,7 @@
 //                           input of single-block linear2 (and [3h, 3h+m) of double-block mlp.2)
 //   q,k,v bf16 [H, L, 128]  attention layout written by the fused QK-norm/RoPE kernel
 //   pe  f32  [L, 64, 2, 2]  RoPE table (computed once per denoise call)
+#include <algorithm>
 #include <cstdio>
 #include <cstdlib>
 #include <map>
@@ -67,6 +68,7 @@ struct mb_flux {
   int64_t mod_off_final = 0, mod_total = 0;
   GemvJob* jobs_dev = nullptr;
   int gemv_kinds = 0;  // bit gemv_kind(type) of every GEMV job's weight type
+  int64_t gemv_smem_rb = 0;  // largest row_bytes a GEMV block stages in shared memory
   int* blocks_dev = nullptr;
   int n_jobs[3] = {0, 0, 0}, n_blocks[3] = {0, 0, 0}, job0[3] = {0, 0, 0}, block0[3] = {0, 0, 0};
 
@@ -193,6 +195,7 @@ mb_status finalize(mb_flux* m) {
     j.w = w->dev;
     j.type = w->type;
     m->gemv_kinds |= 1 << gemv_kind(w->type);
+    m->gemv_smem_rb = std::max(m->gemv_smem_rb, gemv_smem_row_bytes(w->type, w->row_bytes));
     j.n_rows = (int)w->n_rows;
     j.n_cols = (int)w->n_cols;
     j.row_bytes = w->row_bytes;
@@ -256,7 +259,7 @@ mb_status finalize(mb_flux* m) {
 
 mb_status gemv_table(const mb_flux* m, int table, const GemvInput* ins, int n_in, cudaStream_t st) {
   return check_launch(launch_gemv_batch(m->jobs_dev, m->gemv_kinds, m->blocks_dev + 2 * m->block0[table], m->n_blocks[table], ins,
-                                        n_in, m->gemv_stage, st),
+                                        n_in, m->gemv_stage, m->gemv_smem_rb, st),
                       "gemv batch");
 }
 

@@ -558,9 +558,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t lane_addr = (uint32_t)(q * 32) << 16;
     uint32_t it = 0, ic = 0;
     bool ok = true;
-#ifdef MB_DEC_PIPE
-    int pend_sa = -1;  // stage whose TMEM store is in flight (its full arrival deferred)
-#endif
     for (int tile = tile_first; tile < n_tiles && ok; tile += tile_step) {
       TILE_SETUP(tile);
       for (int kc = 0; kc < nks / kSPC && ok; kc++, ic++) {
@@ -630,23 +627,6 @@ __global__ void __launch_bounds__(kThreads, 1)
             __syncwarp();
             if (lane == 0) mbar_arrive(&r_empty[sr]);
           }
-#ifdef MB_DEC_PIPE
-          if (pend_sa >= 0) {
-            tmem_wait_st();
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) {
-              if constexpr (PAIR)
-                mbar_arrive_cluster(smem_in_cta(&full[pend_sa], 0));
-              else
-                mbar_arrive(&full[pend_sa]);
-            }
-          }
-          if (!(ok = (mbar_wait(&empty[sa], pa ^ 1, abort_flag, p.status, kDevTimeoutGemm)))) break;
-          tc_fence_after();
-          tmem_st16(tmem + lane_addr + kTmemA + sa * 32 + hh * 16, o);
-          pend_sa = (int)sa;
-#else
           if (!(ok = (mbar_wait(&empty[sa], pa ^ 1, abort_flag, p.status, kDevTimeoutGemm)))) break;
           tc_fence_after();
           tmem_st16(tmem + lane_addr + kTmemA + sa * 32 + hh * 16, o);
@@ -659,23 +639,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             else
               mbar_arrive(&full[sa]);
           }
-#endif
         }
       }
     }
-#ifdef MB_DEC_PIPE
-    if (ok && pend_sa >= 0) {
-      tmem_wait_st();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) {
-        if constexpr (PAIR)
-          mbar_arrive_cluster(smem_in_cta(&full[pend_sa], 0));
-        else
-          mbar_arrive(&full[pend_sa]);
-      }
-    }
-#endif
   } else {
     // ------------------------------------------------ epilogue (thread = output feature n)
     // both CTAs of a pair release the accumulator on the leader's barrier

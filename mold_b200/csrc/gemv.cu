@@ -13,13 +13,20 @@
 namespace mb {
 namespace gemv {
 
-constexpr int kWarps = 4;                                 // warps per block
+#ifndef MB_GEMV_WARPS
+#define MB_GEMV_WARPS 4
+#endif
+constexpr int kWarps = MB_GEMV_WARPS;                     // warps per block
 constexpr int kRowsPerWarp = kGemvRowsPerBlock / kWarps;  // 8
 constexpr int kMaxLen = 4096;
 constexpr int kMaxInputs = 4;
-// Per staged input: x, its 32-value partial sums, then x scaled for the Q4_K path (kQ4Off).
+// Per staged input: x, its 32-value partial sums, then x scaled for the Q4_K path (kQ4Off) and
+// for the Q8_0 path (kQ8Off). The scaled copies are stored slot-major: float4 number s of every
+// unit (64 values for Q4_K, 32 for Q8_0) first, then float4 s + 1, ..., so that the lanes of a
+// row group, which take consecutive units, read consecutive 16-byte pieces (coalesced) instead
+// of pieces one unit (256 or 128 bytes) apart.
 constexpr int kQ4Off = kMaxLen + kMaxLen / 32;
-constexpr int kQ8Off = kQ4Off + kMaxLen;  // x scaled for the Q8_0 path
+constexpr int kQ8Off = kQ4Off + kMaxLen;
 constexpr int kStageStride = kQ8Off + kMaxLen;
 
 // Q4_K nibbles become floats without a conversion instruction: OR-ing a nibble that sits at bit
@@ -113,10 +120,13 @@ __global__ void k_gemv_stage(Inputs ins, float* __restrict__ stage) {
     }
     *(float4*)(xs + i) = v;
     const int j = i & 63;
-    *(float4*)(xs + kQ4Off + i) = make_float4(v.x * q4_pos_scale(j), v.y * q4_pos_scale(j + 1),
-                                              v.z * q4_pos_scale(j + 2), v.w * q4_pos_scale(j + 3));
+    const int u64 = i >> 6, u32 = i >> 5;
+    ((float4*)(xs + kQ4Off))[(j >> 2) * (in.len >> 6) + u64] =
+        make_float4(v.x * q4_pos_scale(j), v.y * q4_pos_scale(j + 1), v.z * q4_pos_scale(j + 2),
+                    v.w * q4_pos_scale(j + 3));
     // Q8_0: bytes 1 and 3 of a word arrive multiplied by 2^8 (see rows_q8)
-    *(float4*)(xs + kQ8Off + i) = make_float4(v.x, v.y * 0.00390625f, v.z, v.w * 0.00390625f);
+    ((float4*)(xs + kQ8Off))[((i & 31) >> 2) * (in.len >> 5) + u32] =
+        make_float4(v.x, v.y * 0.00390625f, v.z, v.w * 0.00390625f);
   }
   __syncthreads();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -147,21 +157,20 @@ MB_DEV void finish_rows(const float (&acc)[kRowsPerWarp * LPR / 32], int r0, int
 // sl, sl + LPR, ... (unit = the low and high nibbles of one 32-byte quant run = sub-blocks
 // 2g and 2g+1) of its RPL rows.
 template <int LPR>
-MB_DEV void rows_q4k(const GemvJob& job, const float* __restrict__ xs, const float* __restrict__ xsum, int r0, int nr,
-                     int lane) {
+MB_DEV void rows_q4k(const GemvJob& job, const uint8_t* wbase, const float* __restrict__ xs,
+                     const float* __restrict__ xsum, int r0, int nr, int lane) {
 #ifndef MB_GEMV_Q4K_RB
 #define MB_GEMV_Q4K_RB 4
 #endif
   constexpr int NSUB = 32 / LPR, RPL = kRowsPerWarp / NSUB, RB = RPL < MB_GEMV_Q4K_RB ? RPL : MB_GEMV_Q4K_RB;
   const int sub = lane / LPR, sl = lane % LPR;
   const int U = job.n_cols / 64;
-  const uint8_t* wbase = (const uint8_t*)job.w + (int64_t)r0 * job.row_bytes;
   float acc[RPL];
 #pragma unroll
   for (int i = 0; i < RPL; i++) acc[i] = 0.f;
   for (int u = sl; u < U; u += LPR) {
     const int kb = u >> 2, g = u & 3;
-    const float4* xq4 = (const float4*)(xs + kQ4Off + u * 64);
+    const float4* xq4 = (const float4*)(xs + kQ4Off) + u;  // slot s of unit u at xq4[s * U]
     const float s_lo = __ldg(xsum + 2 * u), s_hi = __ldg(xsum + 2 * u + 1);
     // rows in batches of RB: all loads of a batch first (rows past the job's end re-read its
     // last row; finish_rows drops them); the unit's x values are read per word (L1) and shared
@@ -173,9 +182,9 @@ MB_DEV void rows_q4k(const GemvJob& job, const float* __restrict__ xs, const flo
       for (int j = 0; j < RB; j++) {
         const int rr = min(sub + (i0 + j) * NSUB, nr - 1);
         const uint8_t* b = wbase + (int64_t)rr * job.row_bytes + kb * 144;
-        H[j] = __ldg((const uint4*)b);
-        A[j] = __ldg((const uint4*)(b + 16 + 32 * g));
-        B[j] = __ldg((const uint4*)(b + 32 + 32 * g));
+        H[j] = *(const uint4*)b;
+        A[j] = *(const uint4*)(b + 16 + 32 * g);
+        B[j] = *(const uint4*)(b + 32 + 32 * g);
       }
       // dot products per row: (low sub-block, high sub-block), each as two packed partial sums
       uint64_t alo[RB], blo[RB], ahi[RB], bhi[RB];
@@ -184,7 +193,7 @@ MB_DEV void rows_q4k(const GemvJob& job, const float* __restrict__ xs, const flo
       for (int j = 0; j < RB; j++) alo[j] = blo[j] = ahi[j] = bhi[j] = 0ull;
 #pragma unroll
       for (int I = 0; I < 8; I++) {
-        const float4 xl = __ldg(xq4 + I), xh = __ldg(xq4 + 8 + I);
+        const float4 xl = __ldg(xq4 + I * U), xh = __ldg(xq4 + (8 + I) * U);
         const uint64_t xl01 = pkf(xl.x, xl.y), xl23 = pkf(xl.z, xl.w);
         const uint64_t xh01 = pkf(xh.x, xh.y), xh23 = pkf(xh.z, xh.w);
 #pragma unroll
@@ -228,11 +237,11 @@ MB_DEV void rows_q4k(const GemvJob& job, const float* __restrict__ xs, const flo
 // q * 2^p exactly; bytes 2 and 3 are taken from the word shifted right by 16, and the staged
 // x (kQ8Off) carries 2^-8 for bytes 1 and 3.
 template <int LPR>
-MB_DEV void rows_q8(const GemvJob& job, const float* __restrict__ xs, int r0, int nr, int lane) {
+MB_DEV void rows_q8(const GemvJob& job, const uint8_t* wbase, const float* __restrict__ xs, int r0, int nr,
+                    int lane) {
   constexpr int NSUB = 32 / LPR, RPL = kRowsPerWarp / NSUB, RB = RPL < 4 ? RPL : 4;
   const int sub = lane / LPR, sl = lane % LPR;
   const int U = job.n_cols / 32;
-  const uint8_t* wbase = (const uint8_t*)job.w + (int64_t)r0 * job.row_bytes;
   const uint64_t M8 = pkf(8388608.f + 128.f, 8388608.f + 32768.f);
   float acc[RPL];
 #pragma unroll
@@ -241,7 +250,7 @@ MB_DEV void rows_q8(const GemvJob& job, const float* __restrict__ xs, int r0, in
     uint64_t x2[16];
 #pragma unroll
     for (int i = 0; i < 8; i++) {
-      const float4 t = __ldg((const float4*)(xs + kQ8Off + u * 32) + i);
+      const float4 t = __ldg((const float4*)(xs + kQ8Off) + i * U + u);
       x2[2 * i] = pkf(t.x, t.y);
       x2[2 * i + 1] = pkf(t.z, t.w);
     }
@@ -256,7 +265,7 @@ MB_DEV void rows_q8(const GemvJob& job, const float* __restrict__ xs, int r0, in
       const uint32_t* a4 = (const uint32_t*)((uintptr_t)b & ~(uintptr_t)3);
       sh[j] = ((uintptr_t)b & 3) != 0;
 #pragma unroll
-      for (int k = 0; k < 10; k++) wv[j][k] = __ldg(a4 + k);
+      for (int k = 0; k < 10; k++) wv[j][k] = a4[k];
     }
 #pragma unroll
     for (int j = 0; j < RB; j++) {
@@ -462,35 +471,65 @@ MB_DEV bool fast_kind(int t) {
 // One block = kWarps warps x kRowsPerWarp rows of one job (blocks[] = (job, first row)). Two
 // kernels (KIND 0: Q4_K, Q8_0, plain; KIND 1: the decode_unit types) so that each is compiled
 // for its own paths' registers; a block whose job is of the other kind returns at once.
+// Q4_K and Q8_0 blocks first copy their 32 contiguous rows into shared memory with one bulk copy
+// (smem_rb bytes per row reserved): the copy engine streams them at full rate, and the lanes then
+// read their scattered 16-byte pieces from shared memory (conflict-free) instead of as many
+// partially used global sectors.
 #ifndef MB_GEMV_MINB
 #define MB_GEMV_MINB 3
 #endif
 template <int KIND>
 __global__ void __launch_bounds__(kWarps * 32, MB_GEMV_MINB)
     k_gemv(const GemvJob* __restrict__ jobs, const int2* __restrict__ blocks, GemvJob inline_job,
-           const float* __restrict__ stage) {
+           const float* __restrict__ stage, int smem_rb, int* status) {
+  extern __shared__ __align__(128) uint8_t sw[];
+  __shared__ uint64_t wbar;
+  __shared__ int abort_flag;
   const int2 bj = jobs ? blocks[blockIdx.x] : make_int2(0, blockIdx.x * kGemvRowsPerBlock);
   const GemvJob job = jobs ? jobs[bj.x] : inline_job;
   if (fast_kind(job.type) != (KIND == 0)) return;
   const float* xs = stage + (int64_t)job.x_slot * kStageStride;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if constexpr (KIND == 0) {
+    if (job.type == MB_GGML_Q4_K || job.type == MB_GGML_Q8_0) {
+      const int nrb = min(kGemvRowsPerBlock, job.n_rows - bj.y);
+      if (job.row_bytes > smem_rb || nrb <= 0) return;  // the launch reserved too little: skip, never overrun
+      const uint32_t bytes = (uint32_t)(nrb * job.row_bytes);
+      if (threadIdx.x == 0) {
+        abort_flag = 0;
+        mbar_init(&wbar, 1);
+        fence_mbar_init();
+      }
+      __syncthreads();
+      if (threadIdx.x == 0) {
+        mbar_expect_tx(&wbar, bytes);
+        bulk_load(sw, (const uint8_t*)job.w + (int64_t)bj.y * job.row_bytes, bytes, &wbar);
+      }
+      if (!mbar_wait(&wbar, 0, &abort_flag, status, kDevTimeoutGemv)) return;
+      const int rl = warp * kRowsPerWarp;  // first row of this warp within the block
+      if (rl >= nrb) return;
+      const int nr = min(kRowsPerWarp, nrb - rl);
+      const uint8_t* wb = sw + (int64_t)rl * job.row_bytes;
+      const int r0 = bj.y + rl;
+      if (job.type == MB_GGML_Q4_K) {
+        if ((job.n_cols / 64) % 16 == 0)
+          rows_q4k<16>(job, wb, xs, xs + kMaxLen, r0, nr, lane);
+        else
+          rows_q4k<32>(job, wb, xs, xs + kMaxLen, r0, nr, lane);
+      } else {
+        if ((job.n_cols / 32) % 32 == 0)
+          rows_q8<32>(job, wb, xs, r0, nr, lane);
+        else
+          rows_q8<16>(job, wb, xs, r0, nr, lane);
+      }
+      return;
+    }
+  }
   const int r0 = bj.y + warp * kRowsPerWarp;
   if (r0 >= job.n_rows) return;
   const int nr = min(kRowsPerWarp, job.n_rows - r0);
   if constexpr (KIND == 0) {
-    if (job.type == MB_GGML_Q4_K) {
-      if ((job.n_cols / 64) % 16 == 0)
-        rows_q4k<16>(job, xs, xs + kMaxLen, r0, nr, lane);
-      else
-        rows_q4k<32>(job, xs, xs + kMaxLen, r0, nr, lane);
-    } else if (job.type == MB_GGML_Q8_0) {
-      if ((job.n_cols / 32) % 32 == 0)
-        rows_q8<32>(job, xs, r0, nr, lane);
-      else
-        rows_q8<16>(job, xs, r0, nr, lane);
-    } else {
-      rows_plain(job, xs, r0, nr, lane);
-    }
+    rows_plain(job, xs, r0, nr, lane);
   } else {
     if (job.type == MB_GGML_Q4_0) {
       rows_units_any<MB_GGML_Q4_0>(job, xs, r0, nr, lane);
@@ -523,8 +562,29 @@ int gemv_kind(int ggml_type) {
              : 1;
 }
 
+int64_t gemv_smem_row_bytes(int ggml_type, int64_t row_bytes) {
+  return (ggml_type == MB_GGML_Q4_K || ggml_type == MB_GGML_Q8_0) ? row_bytes : 0;
+}
+
+// Dynamic shared memory of the KIND 0 kernel for `smem_rb` bytes per row (its attribute is raised
+// once per device to the largest size requested so far).
+static cudaError_t gemv0_smem(int64_t smem_rb, size_t* bytes) {
+  *bytes = (size_t)smem_rb * kGemvRowsPerBlock;
+  if (*bytes > 200 * 1024) return cudaErrorInvalidValue;
+  static size_t done[64];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (*bytes > done[dev & 63]) {
+    cudaError_t e = cudaFuncSetAttribute(gemv::k_gemv<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)*bytes);
+    if (e != cudaSuccess) return e;
+    done[dev & 63] = *bytes;
+  }
+  return cudaSuccess;
+}
+
 cudaError_t launch_gemv_batch(const GemvJob* jobs_dev, int kinds, const int* block_job_dev, int n_blocks,
-                              const GemvInput* inputs, int n_inputs, float* stage, cudaStream_t st) {
+                              const GemvInput* inputs, int n_inputs, float* stage, int64_t smem_row_bytes,
+                              cudaStream_t st) {
   if (kinds & ~3) return cudaErrorInvalidValue;
   if (n_inputs < 1 || n_inputs > gemv::kMaxInputs || !stage) return cudaErrorInvalidValue;
   gemv::Inputs ins = {};
@@ -534,8 +594,17 @@ cudaError_t launch_gemv_batch(const GemvJob* jobs_dev, int kinds, const int* blo
   }
   gemv::k_gemv_stage<<<n_inputs, 256, 0, st>>>(ins, stage);
   GemvJob dummy = {};
-  if (kinds & 1) gemv::k_gemv<0><<<n_blocks, gemv::kWarps * 32, 0, st>>>(jobs_dev, (const int2*)block_job_dev, dummy, stage);
-  if (kinds & 2) gemv::k_gemv<1><<<n_blocks, gemv::kWarps * 32, 0, st>>>(jobs_dev, (const int2*)block_job_dev, dummy, stage);
+  int* status = device_status_ptr();
+  if (kinds & 1) {
+    size_t sm = 0;
+    cudaError_t e = gemv0_smem(smem_row_bytes, &sm);
+    if (e != cudaSuccess) return e;
+    gemv::k_gemv<0><<<n_blocks, gemv::kWarps * 32, sm, st>>>(jobs_dev, (const int2*)block_job_dev, dummy, stage,
+                                                            (int)smem_row_bytes, status);
+  }
+  if (kinds & 2)
+    gemv::k_gemv<1><<<n_blocks, gemv::kWarps * 32, 0, st>>>(jobs_dev, (const int2*)block_job_dev, dummy, stage, 0,
+                                                           status);
   return cudaGetLastError();
 }
 
@@ -563,10 +632,16 @@ cudaError_t launch_gemv_single(const mb_weight* w, const float* x, int apply_sil
   ins.in[0].len = (int)w->n_cols;
   gemv::k_gemv_stage<<<1, 256, 0, st>>>(ins, stage);
   const int blocks = (int)((w->n_rows + kGemvRowsPerBlock - 1) / kGemvRowsPerBlock);
-  if (gemv_kind(w->type) == 0)
-    gemv::k_gemv<0><<<blocks, gemv::kWarps * 32, 0, st>>>(nullptr, nullptr, j, stage);
-  else
-    gemv::k_gemv<1><<<blocks, gemv::kWarps * 32, 0, st>>>(nullptr, nullptr, j, stage);
+  int* status = device_status_ptr();
+  if (gemv_kind(w->type) == 0) {
+    const int64_t rb = gemv_smem_row_bytes(w->type, w->row_bytes);
+    size_t sm = 0;
+    cudaError_t e = gemv0_smem(rb, &sm);
+    if (e != cudaSuccess) return e;
+    gemv::k_gemv<0><<<blocks, gemv::kWarps * 32, sm, st>>>(nullptr, nullptr, j, stage, (int)rb, status);
+  } else {
+    gemv::k_gemv<1><<<blocks, gemv::kWarps * 32, 0, st>>>(nullptr, nullptr, j, stage, 0, status);
+  }
   return cudaGetLastError();
 }
 

@@ -106,8 +106,13 @@ constexpr int kGemvRowsPerBlock = 32;  // rows of one job handled by one GEMV bl
 // jobs_dev / block_job_dev live in device memory.
 // `kinds`: bit gemv_kind(type) set for every weight type among the jobs (one kernel per kind
 // runs; blocks of a job of the other kind exit at once).
+// `smem_row_bytes`: the largest row_bytes among the batch's Q4_K / Q8_0 jobs (their blocks copy
+// their rows to shared memory in one bulk copy; 0 if there are none).
 cudaError_t launch_gemv_batch(const GemvJob* jobs_dev, int kinds, const int* block_job_dev, int n_blocks,
-                              const GemvInput* inputs, int n_inputs, float* stage, cudaStream_t st);
+                              const GemvInput* inputs, int n_inputs, float* stage, int64_t smem_row_bytes,
+                              cudaStream_t st);
+// Row bytes a Q4_K / Q8_0 GEMV block stages in shared memory for this weight type (0 = none).
+int64_t gemv_smem_row_bytes(int ggml_type, int64_t row_bytes);
 // 0: Q4_K, Q8_0 and plain types (their own row kernels); 1: the other block types (decode_unit)
 int gemv_kind(int ggml_type);
 size_t gemv_stage_floats();

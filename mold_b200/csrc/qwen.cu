@@ -32,6 +32,7 @@
 //   q,k,v bf16 [B][H][L][128]  per sequence: text positions 0..Lt, image Lt..L (k / v
 //                              permuted by kv_pos)
 //   pe  f32  [L, 64, 2, 2]     RoPE table shared by the batch
+#include <algorithm>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
@@ -83,6 +84,7 @@ struct mb_qwen {
   int64_t mod_off_final = 0;
   GemvJob* jobs_dev = nullptr;
   int gemv_kinds = 0;  // bit gemv_kind(type) of every GEMV job's weight type
+  int64_t gemv_smem_rb = 0;  // largest row_bytes a GEMV block stages in shared memory
   int* blocks_dev = nullptr;
   int n_blocks[3] = {0, 0, 0}, block0[3] = {0, 0, 0};
 
@@ -221,6 +223,7 @@ mb_status finalize(mb_qwen* m) {
     j.w = w->dev;
     j.type = w->type;
     m->gemv_kinds |= 1 << gemv_kind(w->type);
+    m->gemv_smem_rb = std::max(m->gemv_smem_rb, gemv_smem_row_bytes(w->type, w->row_bytes));
     j.n_rows = (int)w->n_rows;
     j.n_cols = (int)w->n_cols;
     j.row_bytes = w->row_bytes;
@@ -265,7 +268,7 @@ mb_status finalize(mb_qwen* m) {
 
 mb_status gemv_table(const mb_qwen* m, int table, const GemvInput* in, cudaStream_t st) {
   return check_launch(launch_gemv_batch(m->jobs_dev, m->gemv_kinds, m->blocks_dev + 2 * m->block0[table], m->n_blocks[table], in,
-                                        1, m->gemv_stage, st),
+                                        1, m->gemv_stage, m->gemv_smem_rb, st),
                       "gemv batch");
 }
 
