@@ -365,13 +365,21 @@ WORKLOAD = {"flux": "FLUX.1-dev {q} 1024x1024 (4096 img + 512 txt tokens), 28-st
                     "30-step schedule, guidance 4.0"}
 
 
+def all_host_threads():
+    """Let the CPU sample use every host core: torchrun sets OMP_NUM_THREADS=1 in each rank's
+    environment when it starts more than one process, which would leave BLAS single-threaded."""
+    from threadpoolctl import threadpool_limits
+    return threadpool_limits(limits=CpuSample.cores())
+
+
 def reference_arm(args, rank):
     if rank != 0:
         return
-    s = cpu_sample(args)
-    for _ in range(max(args.warmup, 1)):
-        s.run()
-    times = [s.run() for _ in range(args.steps)]
+    with all_host_threads():
+        s = cpu_sample(args)
+        for _ in range(max(args.warmup, 1)):
+            s.run()
+        times = [s.run() for _ in range(args.steps)]
     t_step = statistics.mean(times) * s.ratio
     v = 1.0 / t_step
     line = {"impl": "reference", "metric": METRIC[args.model], "value": v, "unit": "steps/s",
@@ -748,9 +756,10 @@ def main():
     cpu = None  # the CPU sample is taken at N=1 only (rank 0 is the only rank there)
     if not args.no_cpu and world == 1:
         try:
-            s = CpuSample(args.quant)
-            s.run()
-            tt = [s.run() for _ in range(2)]
+            with all_host_threads():
+                s = CpuSample(args.quant)
+                s.run()
+                tt = [s.run() for _ in range(2)]
             cpu = {"value": 1.0 / (statistics.mean(tt) * s.ratio), "unit": "steps/s", "cores": s.cores(),
                    "kind": "port",
                    "sample": "numpy/OpenBLAS oracle: %s (%s), mean of 2 timed runs, extrapolated x%.1f "
@@ -869,9 +878,10 @@ def main_qwen(args, world, rank, local, dev, peaks):
     cpu = None
     if not args.no_cpu and world == 1:
         try:
-            s = QwenCpuSample(args.quant)
-            s.run()
-            tt = [s.run() for _ in range(2)]
+            with all_host_threads():
+                s = QwenCpuSample(args.quant)
+                s.run()
+                tt = [s.run() for _ in range(2)]
             cpu = {"value": 1.0 / (statistics.mean(tt) * s.ratio), "unit": "steps/s", "cores": s.cores(),
                    "kind": "port",
                    "sample": "numpy/OpenBLAS oracle: %s (%s), mean of 2 timed runs, extrapolated x%.1f "
