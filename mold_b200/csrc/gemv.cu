@@ -160,7 +160,7 @@ template <int LPR>
 MB_DEV void rows_q4k(const GemvJob& job, const uint8_t* wbase, const float* __restrict__ xs,
                      const float* __restrict__ xsum, int r0, int nr, int lane) {
 #ifndef MB_GEMV_Q4K_RB
-#define MB_GEMV_Q4K_RB 4
+#define MB_GEMV_Q4K_RB 2
 #endif
   constexpr int NSUB = 32 / LPR, RPL = kRowsPerWarp / NSUB, RB = RPL < MB_GEMV_Q4K_RB ? RPL : MB_GEMV_Q4K_RB;
   const int sub = lane / LPR, sl = lane % LPR;
@@ -464,13 +464,16 @@ MB_DEV void rows_plain(const GemvJob& job, const float* __restrict__ xs, int r0,
   finish_rows<32>(acc, r0, 0, lane, nr, job);
 }
 
-MB_DEV bool fast_kind(int t) {
-  return t == MB_GGML_Q4_K || t == MB_GGML_Q8_0 || t == MB_GGML_F32 || t == MB_GGML_F16 || t == MB_GGML_BF16;
+// Kernel instance of a weight type: 2 Q4_K, 0 Q8_0 and the plain types, 1 the decode_unit types.
+__host__ __device__ inline int kind_of(int t) {
+  return t == MB_GGML_Q4_K ? 2
+                           : ((t == MB_GGML_Q8_0 || t == MB_GGML_F32 || t == MB_GGML_F16 || t == MB_GGML_BF16) ? 0 : 1);
 }
 
-// One block = kWarps warps x kRowsPerWarp rows of one job (blocks[] = (job, first row)). Two
-// kernels (KIND 0: Q4_K, Q8_0, plain; KIND 1: the decode_unit types) so that each is compiled
-// for its own paths' registers; a block whose job is of the other kind returns at once.
+// One block = kWarps warps x kRowsPerWarp rows of one job (blocks[] = (job, first row)). Three
+// kernels (KIND 2: Q4_K; KIND 0: Q8_0 and the plain types; KIND 1: the decode_unit types) so that
+// each is compiled for its own paths' registers (the Q4_K kernel, alone, fits more blocks per SM);
+// a block whose job is of another kind returns at once.
 // Q4_K and Q8_0 blocks first copy their 32 contiguous rows into shared memory with one bulk copy
 // (smem_rb bytes per row reserved): the copy engine streams them at full rate, and the lanes then
 // read their scattered 16-byte pieces from shared memory (conflict-free) instead of as many
@@ -478,8 +481,11 @@ MB_DEV bool fast_kind(int t) {
 #ifndef MB_GEMV_MINB
 #define MB_GEMV_MINB 3
 #endif
+#ifndef MB_GEMV_MINB_Q4K
+#define MB_GEMV_MINB_Q4K 4
+#endif
 template <int KIND>
-__global__ void __launch_bounds__(kWarps * 32, MB_GEMV_MINB)
+__global__ void __launch_bounds__(kWarps * 32, KIND == 2 ? MB_GEMV_MINB_Q4K : MB_GEMV_MINB)
     k_gemv(const GemvJob* __restrict__ jobs, const int2* __restrict__ blocks, GemvJob inline_job,
            const float* __restrict__ stage, int smem_rb, int* status) {
   extern __shared__ __align__(128) uint8_t sw[];
@@ -487,10 +493,10 @@ __global__ void __launch_bounds__(kWarps * 32, MB_GEMV_MINB)
   __shared__ int abort_flag;
   const int2 bj = jobs ? blocks[blockIdx.x] : make_int2(0, blockIdx.x * kGemvRowsPerBlock);
   const GemvJob job = jobs ? jobs[bj.x] : inline_job;
-  if (fast_kind(job.type) != (KIND == 0)) return;
+  if (kind_of(job.type) != KIND) return;
   const float* xs = stage + (int64_t)job.x_slot * kStageStride;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  if constexpr (KIND == 0) {
+  if constexpr (KIND == 0 || KIND == 2) {
     if (job.type == MB_GGML_Q4_K || job.type == MB_GGML_Q8_0) {
       const int nrb = min(kGemvRowsPerBlock, job.n_rows - bj.y);
       if (job.row_bytes > smem_rb || nrb <= 0) return;  // the launch reserved too little: skip, never overrun
@@ -511,7 +517,7 @@ __global__ void __launch_bounds__(kWarps * 32, MB_GEMV_MINB)
       const int nr = min(kRowsPerWarp, nrb - rl);
       const uint8_t* wb = sw + (int64_t)rl * job.row_bytes;
       const int r0 = bj.y + rl;
-      if (job.type == MB_GGML_Q4_K) {
+      if constexpr (KIND == 2) {
         if ((job.n_cols / 64) % 16 == 0)
           rows_q4k<16>(job, wb, xs, xs + kMaxLen, r0, nr, lane);
         else
@@ -530,7 +536,7 @@ __global__ void __launch_bounds__(kWarps * 32, MB_GEMV_MINB)
   const int nr = min(kRowsPerWarp, job.n_rows - r0);
   if constexpr (KIND == 0) {
     rows_plain(job, xs, r0, nr, lane);
-  } else {
+  } else if constexpr (KIND == 1) {
     if (job.type == MB_GGML_Q4_0) {
       rows_units_any<MB_GGML_Q4_0>(job, xs, r0, nr, lane);
     } else if (job.type == MB_GGML_Q4_1) {
@@ -555,27 +561,24 @@ __global__ void __launch_bounds__(kWarps * 32, MB_GEMV_MINB)
 
 }  // namespace gemv
 
-int gemv_kind(int ggml_type) {
-  return (ggml_type == MB_GGML_Q4_K || ggml_type == MB_GGML_Q8_0 || ggml_type == MB_GGML_F32 ||
-          ggml_type == MB_GGML_F16 || ggml_type == MB_GGML_BF16)
-             ? 0
-             : 1;
-}
+int gemv_kind(int ggml_type) { return gemv::kind_of(ggml_type); }
 
 int64_t gemv_smem_row_bytes(int ggml_type, int64_t row_bytes) {
   return (ggml_type == MB_GGML_Q4_K || ggml_type == MB_GGML_Q8_0) ? row_bytes : 0;
 }
 
-// Dynamic shared memory of the KIND 0 kernel for `smem_rb` bytes per row (its attribute is raised
-// once per device to the largest size requested so far).
-static cudaError_t gemv0_smem(int64_t smem_rb, size_t* bytes) {
+// Dynamic shared memory of the KIND 0 / 2 kernels for `smem_rb` bytes per row (their attribute is
+// raised once per device to the largest size requested so far).
+template <int KIND>
+static cudaError_t gemv_smem(int64_t smem_rb, size_t* bytes) {
   *bytes = (size_t)smem_rb * kGemvRowsPerBlock;
   if (*bytes > 200 * 1024) return cudaErrorInvalidValue;
   static size_t done[64];
   int dev = 0;
   cudaGetDevice(&dev);
   if (*bytes > done[dev & 63]) {
-    cudaError_t e = cudaFuncSetAttribute(gemv::k_gemv<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)*bytes);
+    cudaError_t e =
+        cudaFuncSetAttribute(gemv::k_gemv<KIND>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)*bytes);
     if (e != cudaSuccess) return e;
     done[dev & 63] = *bytes;
   }
@@ -585,7 +588,7 @@ static cudaError_t gemv0_smem(int64_t smem_rb, size_t* bytes) {
 cudaError_t launch_gemv_batch(const GemvJob* jobs_dev, int kinds, const int* block_job_dev, int n_blocks,
                               const GemvInput* inputs, int n_inputs, float* stage, int64_t smem_row_bytes,
                               cudaStream_t st) {
-  if (kinds & ~3) return cudaErrorInvalidValue;
+  if (kinds & ~7) return cudaErrorInvalidValue;
   if (n_inputs < 1 || n_inputs > gemv::kMaxInputs || !stage) return cudaErrorInvalidValue;
   gemv::Inputs ins = {};
   for (int i = 0; i < n_inputs; i++) {
@@ -597,9 +600,16 @@ cudaError_t launch_gemv_batch(const GemvJob* jobs_dev, int kinds, const int* blo
   int* status = device_status_ptr();
   if (kinds & 1) {
     size_t sm = 0;
-    cudaError_t e = gemv0_smem(smem_row_bytes, &sm);
+    cudaError_t e = gemv_smem<0>(smem_row_bytes, &sm);
     if (e != cudaSuccess) return e;
     gemv::k_gemv<0><<<n_blocks, gemv::kWarps * 32, sm, st>>>(jobs_dev, (const int2*)block_job_dev, dummy, stage,
+                                                            (int)smem_row_bytes, status);
+  }
+  if (kinds & 4) {
+    size_t sm = 0;
+    cudaError_t e = gemv_smem<2>(smem_row_bytes, &sm);
+    if (e != cudaSuccess) return e;
+    gemv::k_gemv<2><<<n_blocks, gemv::kWarps * 32, sm, st>>>(jobs_dev, (const int2*)block_job_dev, dummy, stage,
                                                             (int)smem_row_bytes, status);
   }
   if (kinds & 2)
@@ -633,12 +643,16 @@ cudaError_t launch_gemv_single(const mb_weight* w, const float* x, int apply_sil
   gemv::k_gemv_stage<<<1, 256, 0, st>>>(ins, stage);
   const int blocks = (int)((w->n_rows + kGemvRowsPerBlock - 1) / kGemvRowsPerBlock);
   int* status = device_status_ptr();
-  if (gemv_kind(w->type) == 0) {
+  const int kind = gemv_kind(w->type);
+  if (kind == 0 || kind == 2) {
     const int64_t rb = gemv_smem_row_bytes(w->type, w->row_bytes);
     size_t sm = 0;
-    cudaError_t e = gemv0_smem(rb, &sm);
+    cudaError_t e = kind == 0 ? gemv_smem<0>(rb, &sm) : gemv_smem<2>(rb, &sm);
     if (e != cudaSuccess) return e;
-    gemv::k_gemv<0><<<blocks, gemv::kWarps * 32, sm, st>>>(nullptr, nullptr, j, stage, (int)rb, status);
+    if (kind == 0)
+      gemv::k_gemv<0><<<blocks, gemv::kWarps * 32, sm, st>>>(nullptr, nullptr, j, stage, (int)rb, status);
+    else
+      gemv::k_gemv<2><<<blocks, gemv::kWarps * 32, sm, st>>>(nullptr, nullptr, j, stage, (int)rb, status);
   } else {
     gemv::k_gemv<1><<<blocks, gemv::kWarps * 32, 0, st>>>(nullptr, nullptr, j, stage, 0, status);
   }
