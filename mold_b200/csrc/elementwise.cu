@@ -92,9 +92,40 @@ MB_DEV float block_sum(float v, float* red) {
   return t;
 }
 
+// Mean and sum of squared deviations of two equal-count groups merged (Chan et al.):
+// mean = (ma + mb) / 2, M2 = M2a + M2b + (mb - ma)^2 n / 2 for groups of n values each.
+MB_DEV void chan_merge(float& m, float& q, float mo, float qo, float n) {
+  const float d = mo - m;
+  q = q + qo + d * d * (0.5f * n);
+  m = 0.5f * (m + mo);
+}
+// Block-wide mean and M2 from per-thread ones over n values each (blockDim a power-of-two number
+// of warps): one pass over the data and one shared-memory exchange, with the two-pass form's
+// numerical stability.
+MB_DEV void block_mean_m2(float& m, float& q, float n, float2* red) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const float mo = __shfl_xor_sync(0xffffffffu, m, o), qo = __shfl_xor_sync(0xffffffffu, q, o);
+    chan_merge(m, q, mo, qo, n);
+    n *= 2.f;
+  }
+  if (lane == 0) red[warp] = make_float2(m, q);
+  __syncthreads();
+  float2 a = red[lane < nw ? lane : 0];
+  for (int o = 1; o < nw; o <<= 1) {
+    const float mo = __shfl_xor_sync(0xffffffffu, a.x, o), qo = __shfl_xor_sync(0xffffffffu, a.y, o);
+    chan_merge(a.x, a.y, mo, qo, n);
+    n *= 2.f;
+  }
+  m = __shfl_sync(0xffffffffu, a.x, 0);
+  q = __shfl_sync(0xffffffffu, a.y, 0);
+}
+
 template <int NV>
 __global__ void __launch_bounds__(1024) k_ln_modulate_blk(const float* __restrict__ x, int C, int64_t ldx, LnSegs segs,
                                                           __nv_bfloat16* __restrict__ y, int64_t ldy) {
+  __shared__ float2 red2[32];
   __shared__ float red[32];
   int si = 0;
   int64_t r = blockIdx.x;
@@ -109,14 +140,33 @@ __global__ void __launch_bounds__(1024) k_ln_modulate_blk(const float* __restric
   float s = 0.f;
 #pragma unroll
   for (int i = 0; i < NV; i++) s += (v[i].x + v[i].y) + (v[i].z + v[i].w);
-  const float mean = block_sum(s, red) / (float)C;
-  float q = 0.f;
+  float mean, rstd;
+  if (((blockDim.x >> 5) & ((blockDim.x >> 5) - 1)) == 0) {
+    // one pass: per-thread mean and M2, merged across the block in one exchange
+    mean = s * (1.f / (4 * NV));
+    float q = 0.f;
 #pragma unroll
-  for (int i = 0; i < NV; i++) {
-    v[i].x -= mean; v[i].y -= mean; v[i].z -= mean; v[i].w -= mean;
-    q += (v[i].x * v[i].x + v[i].y * v[i].y) + (v[i].z * v[i].z + v[i].w * v[i].w);
+    for (int i = 0; i < NV; i++) {
+      const float a = v[i].x - mean, b = v[i].y - mean, c = v[i].z - mean, d = v[i].w - mean;
+      q += (a * a + b * b) + (c * c + d * d);
+    }
+    block_mean_m2(mean, q, (float)(4 * NV), red2);
+#pragma unroll
+    for (int i = 0; i < NV; i++) {
+      v[i].x -= mean; v[i].y -= mean; v[i].z -= mean; v[i].w -= mean;
+    }
+    rstd = 1.f / sqrtf(q / (float)C + 1e-6f);
+  } else {
+    // a number of warps that is not a power of two: two passes through block_sum
+    mean = block_sum(s, red) / (float)C;
+    float q = 0.f;
+#pragma unroll
+    for (int i = 0; i < NV; i++) {
+      v[i].x -= mean; v[i].y -= mean; v[i].z -= mean; v[i].w -= mean;
+      q += (v[i].x * v[i].x + v[i].y * v[i].y) + (v[i].z * v[i].z + v[i].w * v[i].w);
+    }
+    rstd = 1.f / sqrtf(block_sum(q, red) / (float)C + 1e-6f);
   }
-  const float rstd = 1.f / sqrtf(block_sum(q, red) / (float)C + 1e-6f);
   __nv_bfloat16* yr = y + row * ldy;
 #pragma unroll
   for (int i = 0; i < NV; i++) {

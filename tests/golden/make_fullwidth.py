@@ -3,7 +3,7 @@
 oracle/qwen_ref.py). Everything is seeded through the oracle's C generator and quantizers, so
 the GPU tests rebuild the same GGUF bytes and inputs bit for bit on any host.
 
-    python tests/golden/make_fullwidth.py [flux_q4_k] [flux_q8_0] [qwen_q4_k]   # default: all
+    python tests/golden/make_fullwidth.py [flux_q4_k] [flux_q8_0] [qwen_q4_k] [flux_full_q4_k]
 
 It takes about half an hour of CPU per FLUX case (the 28-step denoise dominates).
 
@@ -19,6 +19,9 @@ flux_q4_k / flux_q8_0: FLUX.1-dev widths (hidden 3072, 24 heads x 128, MLP 12288
   d_single        single block 0 update on the seeded input X_SINGLE [4608, 3072] ~ N(0, 1)
   pred            float16 [4096, 64]: the whole model's prediction at t = T_BLOCK
   denoise         float32 [4096, 64]: the latent after the 28-step schedule (get_schedule(28, 4096))
+flux_full_q4_k: the full FLUX.1-dev architecture (19 double + 38 single blocks) in Q4_K, seed 14,
+  the same token counts and guidance; one forward (about 25 min of CPU).
+  pred            float16 [4096, 64]: the model's prediction at t = T_BLOCK
 qwen_q4_k: Qwen-Image widths (hidden 3072, 24 heads, MLP 12288, text width 3584) with 1 block,
   4096 image + 256 text tokens, conditional mask keeping the first 200 text tokens,
   unconditional mask a seeded 60 % pattern.
@@ -118,6 +121,20 @@ def make_flux(name):
                         denoise=den.astype(np.float32))
 
 
+FULL_SEED = 14
+
+
+def make_flux_full(name):
+    """The full-depth model: one forward (decodes are not cached, so memory stays at the raw bytes)."""
+    cfg = F.FluxConfig()
+    W = F.synth_weights(cfg, seed=FULL_SEED, qtype=oracle.GGML_Q4_K)
+    img, ids, txt, tids, y, _ = flux_inputs(FULL_SEED)
+    t0 = time.time()
+    pred = F.forward(W, cfg, img, ids, txt, tids, T_BLOCK, y, GUIDANCE)
+    print(f"{name}: forward {time.time() - t0:.0f} s", flush=True)
+    np.savez_compressed(os.path.join(HERE, f"fullwidth_{name}.npz"), pred=pred.astype(np.float16))
+
+
 def make_qwen(name):
     cfg = qwen_config()
     W = cached(Q.synth_weights(cfg, seed=13, qtype=oracle.GGML_Q4_K))
@@ -132,9 +149,12 @@ def make_qwen(name):
 
 
 def main(argv):
-    todo = argv or list(FLUX_CASES) + ["qwen_q4_k"]
+    todo = argv or list(FLUX_CASES) + ["qwen_q4_k", "flux_full_q4_k"]
     for name in todo:
-        (make_qwen if name.startswith("qwen") else make_flux)(name)
+        if name == "flux_full_q4_k":
+            make_flux_full(name)
+        else:
+            (make_qwen if name.startswith("qwen") else make_flux)(name)
 
 
 if __name__ == "__main__":

@@ -192,3 +192,20 @@ def test_qwen_cfg_step_full_width(qwen_case):
     assert float(np.dot(du, d_ref.ravel()) / np.linalg.norm(du) / np.linalg.norm(d_ref)) >= 0.999
     assert rel_l2(got - latent, d_ref) < 2.5e-2
     assert rel_l2(got, latent + d_ref) < 1e-2
+
+
+def test_flux_full_depth_forward(cuda):
+    """The whole FLUX.1-dev architecture (19 double + 38 single blocks, Q4_K, 512 + 4096 tokens)
+    through mb_flux_forward against the oracle's forward of the same seeded GGUF bytes: the
+    prediction within rel-L2 2e-2 (the per-block errors of 57 blocks compound) and cosine >= 0.999."""
+    cfg = F.FluxConfig()
+    W = F.synth_weights(cfg, seed=G.FULL_SEED, qtype=oracle.GGML_Q4_K)
+    m = flux_model(cfg, W)
+    del W
+    img, ids, txt, tids, y, _ = G.flux_inputs(G.FULL_SEED)
+    pred = m.forward(t(img), t(ids), t(txt), t(tids), G.T_BLOCK, t(y), G.GUIDANCE).cpu().numpy()
+    ref = fixture("flux_full_q4_k")["pred"].astype(np.float32)
+    assert mb.device_status() == 0
+    err = rel_l2(pred, ref)
+    cos = float(np.dot(pred.ravel(), ref.ravel()) / np.linalg.norm(pred) / np.linalg.norm(ref))
+    assert err < 2e-2 and cos >= 0.999, (err, cos)

@@ -157,9 +157,13 @@ def test_qgemv_silu(cuda, t, K, xs):
 
 
 # ------------------------------------------------------------------ K5 / K6 / rope / euler
-def test_ln_modulate(cuda):
-    M, C = 300, 3072
-    x = oracle.randn(22, (M, C)) * 3 + 1
+@pytest.mark.parametrize("C,offset", [(3072, 1.0), (3072, 1000.0), (2304, 1.0), (1536, 50.0), (6144, 1.0)])
+def test_ln_modulate(cuda, C, offset):
+    """Widths whose blocks have a power-of-two number of warps (one-pass merged statistics) and
+    not (2304: three warps, two passes); a row mean far above the spread checks the stability of
+    the variance."""
+    M = 300
+    x = (oracle.randn(22, (M, C)) * 3 + offset).astype(np.float32)
     sh, sc = oracle.randn(23, (C,)), oracle.randn(24, (C,))
     ref = F.modulate(x, sh, sc)
     y = mb.ln_modulate(torch.from_numpy(x).to(cuda), torch.from_numpy(sh).to(cuda), torch.from_numpy(sc).to(cuda))
