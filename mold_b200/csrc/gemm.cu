@@ -581,7 +581,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
 #pragma unroll
         for (int j = 0; j < kSPC; j++, it++) {
-          const int ks = kc * kSPC + j;
           const uint32_t sa = it % SX, pa = (it / SX) & 1;
           uint32_t o[16];
           if constexpr (WT == MB_GGML_Q4_K) {
