@@ -20,74 +20,24 @@ constexpr int kWarps = MB_GEMV_WARPS;                     // warps per block
 constexpr int kRowsPerWarp = kGemvRowsPerBlock / kWarps;  // 8
 constexpr int kMaxLen = 4096;
 constexpr int kMaxInputs = 4;
-// Per staged input: x, its 32-value partial sums, then x scaled for the Q4_K path (kQ4Off) and
-// for the Q8_0 path (kQ8Off). The scaled copies are stored slot-major: float4 number s of every
-// unit (64 values for Q4_K, 32 for Q8_0) first, then float4 s + 1, ..., so that the lanes of a
-// row group, which take consecutive units, read consecutive 16-byte pieces (coalesced) instead
-// of pieces one unit (256 or 128 bytes) apart.
-constexpr int kQ4Off = kMaxLen + kMaxLen / 32;
-constexpr int kQ8Off = kQ4Off + kMaxLen;
-constexpr int kStageStride = kQ8Off + kMaxLen;
+// Per staged input: x, its 32-value partial sums, then x as fixed-point digits for the Q4_K and
+// Q8_0 paths (kQ4IOff in Q4_K unit order, kQ8IOff in Q8_0 unit order), stored slot-major: piece s of every unit (64 values for Q4_K, 32
+// for Q8_0) first, then piece s + 1, ..., so that the lanes of a row group, which take
+// consecutive units, read consecutive 16-byte pieces (coalesced) instead of pieces one unit apart.
+// The digits: x = S * xi with xi a 24-bit integer (S = max|x| / (2^23 - 1)), xi = d0 2^16 +
+// d1 2^8 + d2 (d0 signed, d1 and d2 unsigned bytes); four values' digits are packed per 32-bit
+// word, as uint4 (d0 word, d1 word, d2 word, unused) per 4 values. S is stored at kScaleOff.
+constexpr int kQ4IOff = kMaxLen + kMaxLen / 32;
+constexpr int kQ8IOff = kQ4IOff + kMaxLen;
+constexpr int kScaleOff = kQ8IOff + kMaxLen;
+constexpr int kStageStride = kScaleOff + 4;
 
-// Q4_K nibbles become floats without a conversion instruction: OR-ing a nibble that sits at bit
-// position p (p + 4 <= 23) into the mantissa of 2^23 and subtracting 2^23 gives q * 2^p exactly.
-// A 32-bit word of a Q4_K quant run holds, in bytes b = 0..3, the low nibble of value 4I + b
-// (sub-block 2g) and the high nibble of value 32 + 4I + b (sub-block 2g + 1). Taken from the word
-// W at bits 0, 8, 16 (low nibbles of b0..b2) and 4, 12 (high of b0, b1), and from W >> 12 at bits
-// 8, 12, 16 (high of b2, low of b3, high of b3), each value arrives multiplied by a fixed power
-// of two; the staged copy of x carries the inverse power, so the products are exact as before.
-MB_DEV float q4_pos_scale(int j) {  // j = value index within a 64-value unit
-  const bool hi = j >= 32;
-  const int b = j & 3;
-  const int p = hi ? (b == 0 ? 4 : b == 1 ? 12 : b == 2 ? 8 : 16) : (b == 0 ? 0 : b == 1 ? 8 : b == 2 ? 16 : 12);
-  return __int_as_float((127 - p) << 23);  // 2^-p
-}
 
 struct Inputs {
   GemvInput in[kMaxInputs];
 };
 
 MB_DEV float h16(uint32_t v) { return __half2float(__ushort_as_half((unsigned short)(v & 0xFFFFu))); }
-
-// ---- packed f32x2 arithmetic (sm_100): two IEEE single-precision ops per instruction
-MB_DEV uint64_t pk(uint32_t a, uint32_t b) {
-  uint64_t r;
-  asm("mov.b64 %0, {%1,%2};" : "=l"(r) : "r"(a), "r"(b));
-  return r;
-}
-MB_DEV uint64_t pkf(float a, float b) {
-  uint64_t r;
-  asm("mov.b64 %0, {%1,%2};" : "=l"(r) : "f"(a), "f"(b));
-  return r;
-}
-MB_DEV uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
-  uint64_t r;
-  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
-  return r;
-}
-MB_DEV uint64_t sub2(uint64_t a, uint64_t b) {
-  uint64_t r;
-  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
-  return r;
-}
-MB_DEV float sum2(uint64_t v) {
-  float a, b;
-  asm("mov.b64 {%0,%1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
-  return a + b;
-}
-// mask ? (v ^ c) : c in one LOP3: a signed byte of v, offset by 128 (c's bit 7 of the byte
-// flips its sign bit), placed in the mantissa of 2^23 (c holds 0x4B000000 outside the byte).
-MB_DEV uint32_t magic_s8(uint32_t v, uint32_t mask, uint32_t c) {
-  uint32_t r;
-  asm("lop3.b32 %0, %1, %2, %3, 0x6A;" : "=r"(r) : "r"(v), "r"(mask), "r"(c));
-  return r;
-}
-// (v & mask) | 0x4B000000 in one LOP3: the nibble placed in the mantissa of 2^23.
-MB_DEV uint32_t magic(uint32_t v, uint32_t mask) {
-  uint32_t r;
-  asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(r) : "r"(v), "r"(mask), "r"(0x4B000000u));
-  return r;
-}
 
 MB_DEV uint32_t sb(uint32_t sy, uint32_t sz, uint32_t sw, int k) {
   const uint32_t w = k < 4 ? sy : (k < 8 ? sz : sw);
@@ -119,18 +69,39 @@ __global__ void k_gemv_stage(Inputs ins, float* __restrict__ stage) {
       v.x = silu(v.x); v.y = silu(v.y); v.z = silu(v.z); v.w = silu(v.w);
     }
     *(float4*)(xs + i) = v;
-    const int j = i & 63;
-    const int u64 = i >> 6, u32 = i >> 5;
-    ((float4*)(xs + kQ4Off))[(j >> 2) * (in.len >> 6) + u64] =
-        make_float4(v.x * q4_pos_scale(j), v.y * q4_pos_scale(j + 1), v.z * q4_pos_scale(j + 2),
-                    v.w * q4_pos_scale(j + 3));
-    // Q8_0: bytes 1 and 3 of a word arrive multiplied by 2^8 (see rows_q8)
-    ((float4*)(xs + kQ8Off))[((i & 31) >> 2) * (in.len >> 5) + u32] =
-        make_float4(v.x, v.y * 0.00390625f, v.z, v.w * 0.00390625f);
   }
   __syncthreads();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  {
+    // the integer copies: S from the vector's max |x|, then the three digits of round(x / S)
+    __shared__ float red[32];
+    float mx = 0.f;
+    for (int i = threadIdx.x; i < in.len; i += blockDim.x) mx = fmaxf(mx, fabsf(xs[i]));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if (lane == 0) red[warp] = mx;
+    __syncthreads();
+    mx = 0.f;
+    for (int w = 0; w < (int)(blockDim.x >> 5); w++) mx = fmaxf(mx, red[w]);
+    const float S = mx > 0.f ? mx / 8388607.f : 1.f;
+    const float invS = 1.f / S;
+    if (threadIdx.x == 0) xs[kScaleOff] = S;
+    for (int i = threadIdx.x * 4; i < in.len; i += blockDim.x * 4) {
+      uint32_t w0 = 0, w1 = 0, w2 = 0;
+#pragma unroll
+      for (int t = 0; t < 4; t++) {
+        int xi = __float2int_rn(xs[i + t] * invS);
+        xi = max(-8388607, min(8388607, xi));
+        w0 |= ((uint32_t)(xi >> 16) & 0xFFu) << (8 * t);
+        w1 |= ((uint32_t)(xi >> 8) & 0xFFu) << (8 * t);
+        w2 |= ((uint32_t)xi & 0xFFu) << (8 * t);
+      }
+      ((uint4*)(xs + kQ4IOff))[((i & 63) >> 2) * (in.len >> 6) + (i >> 6)] = make_uint4(w0, w1, w2, 0u);
+      ((uint4*)(xs + kQ8IOff))[((i & 31) >> 2) * (in.len >> 5) + (i >> 5)] = make_uint4(w0, w1, w2, 0u);
+    }
+  }
   for (int c = warp; c < in.len / 32; c += blockDim.x >> 5) {
+
     float v = xs[c * 32 + lane];
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
@@ -153,28 +124,52 @@ MB_DEV void finish_rows(const float (&acc)[kRowsPerWarp * LPR / 32], int r0, int
   }
 }
 
-// Q4_K rows: a group of LPR lanes serves one row; lane sl takes the 64-value units
-// sl, sl + LPR, ... (unit = the low and high nibbles of one 32-byte quant run = sub-blocks
-// 2g and 2g+1) of its RPL rows.
-template <int LPR>
-MB_DEV void rows_q4k(const GemvJob& job, const uint8_t* wbase, const float* __restrict__ xs,
-                     const float* __restrict__ xsum, int r0, int nr, int lane) {
+MB_DEV int dp4a_us(uint32_t a, uint32_t b, int c) {  // unsigned bytes of a . signed bytes of b + c
+  int d;
+  asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+MB_DEV uint32_t dp4a_uu(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t d;
+  asm("dp4a.u32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+MB_DEV int dp4a_ss(uint32_t a, uint32_t b, int c) {  // signed bytes . signed bytes + c
+  int d;
+  asm("dp4a.s32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+MB_DEV int dp4a_su(uint32_t a, uint32_t b, int c) {  // signed bytes of a . unsigned bytes of b + c
+  int d;
+  asm("dp4a.s32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+
+// Q4_K rows on the integer pipe: a group of LPR lanes serves one row; lane sl takes the 64-value
+// units sl, sl + LPR, ... (unit = the low and high nibbles of one 32-byte quant run = sub-blocks
+// 2g and 2g+1) of its RPL rows. The nibbles (low ones as bytes 0..15, high ones in place as
+// 16 q) multiply the three byte digits of the fixed-point x with dp4a, 4 products per
+// instruction with exact integer sums; a unit's digit sums are combined in f32 once.
 #ifndef MB_GEMV_Q4K_RB
-#define MB_GEMV_Q4K_RB 2
+#define MB_GEMV_Q4K_RB 2  // rows per load batch
 #endif
+template <int LPR>
+MB_DEV void rows_q4k_int(const GemvJob& job, const uint8_t* wbase, const float* __restrict__ xs,
+                         const float* __restrict__ xsum, int r0, int nr, int lane) {
   constexpr int NSUB = 32 / LPR, RPL = kRowsPerWarp / NSUB, RB = RPL < MB_GEMV_Q4K_RB ? RPL : MB_GEMV_Q4K_RB;
   const int sub = lane / LPR, sl = lane % LPR;
   const int U = job.n_cols / 64;
+  const float S = xs[kScaleOff];
   float acc[RPL];
 #pragma unroll
   for (int i = 0; i < RPL; i++) acc[i] = 0.f;
   for (int u = sl; u < U; u += LPR) {
     const int kb = u >> 2, g = u & 3;
-    const float4* xq4 = (const float4*)(xs + kQ4Off) + u;  // slot s of unit u at xq4[s * U]
+    const uint4* xi = (const uint4*)(xs + kQ4IOff) + u;  // slot s of unit u at xi[s * U]
     const float s_lo = __ldg(xsum + 2 * u), s_hi = __ldg(xsum + 2 * u + 1);
     // rows in batches of RB: all loads of a batch first (rows past the job's end re-read its
-    // last row; finish_rows drops them); the unit's x values are read per word (L1) and shared
-    // by the batch's rows, so no 64-value x array is held in registers
+    // last row; finish_rows drops them); the unit's digits are read per word and shared by the
+    // batch's rows
 #pragma unroll
     for (int i0 = 0; i0 < RPL; i0 += RB) {
       uint4 H[RB], A[RB], B[RB];
@@ -186,102 +181,83 @@ MB_DEV void rows_q4k(const GemvJob& job, const uint8_t* wbase, const float* __re
         A[j] = *(const uint4*)(b + 16 + 32 * g);
         B[j] = *(const uint4*)(b + 32 + 32 * g);
       }
-      // dot products per row: (low sub-block, high sub-block), each as two packed partial sums
-      uint64_t alo[RB], blo[RB], ahi[RB], bhi[RB];
-      const uint64_t M2 = pkf(8388608.f, 8388608.f);
+      int l0[RB], h0[RB];
+      uint32_t l1[RB], l2[RB], h1[RB], h2[RB];
 #pragma unroll
-      for (int j = 0; j < RB; j++) alo[j] = blo[j] = ahi[j] = bhi[j] = 0ull;
+      for (int j = 0; j < RB; j++) l0[j] = h0[j] = 0, l1[j] = l2[j] = h1[j] = h2[j] = 0u;
 #pragma unroll
       for (int I = 0; I < 8; I++) {
-        const float4 xl = __ldg(xq4 + I * U), xh = __ldg(xq4 + (8 + I) * U);
-        const uint64_t xl01 = pkf(xl.x, xl.y), xl23 = pkf(xl.z, xl.w);
-        const uint64_t xh01 = pkf(xh.x, xh.y), xh23 = pkf(xh.z, xh.w);
+        const uint4 xl = __ldg(xi + I * U), xh = __ldg(xi + (8 + I) * U);
 #pragma unroll
         for (int j = 0; j < RB; j++) {
           const uint32_t W = I < 4 ? (I == 0 ? A[j].x : I == 1 ? A[j].y : I == 2 ? A[j].z : A[j].w)
                                    : (I == 4 ? B[j].x : I == 5 ? B[j].y : I == 6 ? B[j].z : B[j].w);
-          const uint32_t W2 = W >> 12;
-          // low nibbles of bytes 0,1 | 2,3 and high nibbles of bytes 0,1 | 2,3 (see q4_pos_scale)
-          const uint64_t l01 = sub2(pk(magic(W, 0xFu), magic(W, 0xF00u)), M2);
-          const uint64_t l23 = sub2(pk(magic(W, 0xF0000u), magic(W2, 0xF000u)), M2);
-          const uint64_t h01 = sub2(pk(magic(W, 0xF0u), magic(W, 0xF000u)), M2);
-          const uint64_t h23 = sub2(pk(magic(W2, 0xF00u), magic(W2, 0xF0000u)), M2);
-          alo[j] = fma2(l01, xl01, alo[j]);
-          blo[j] = fma2(l23, xl23, blo[j]);
-          ahi[j] = fma2(h01, xh01, ahi[j]);
-          bhi[j] = fma2(h23, xh23, bhi[j]);
+          const uint32_t lo = W & 0x0F0F0F0Fu, hi = W & 0xF0F0F0F0u;  // hi bytes hold 16 q
+          l0[j] = dp4a_us(lo, xl.x, l0[j]);
+          l1[j] = dp4a_uu(lo, xl.y, l1[j]);
+          l2[j] = dp4a_uu(lo, xl.z, l2[j]);
+          h0[j] = dp4a_us(hi, xh.x, h0[j]);
+          h1[j] = dp4a_uu(hi, xh.y, h1[j]);
+          h2[j] = dp4a_uu(hi, xh.z, h2[j]);
         }
       }
-      float dlo[RB], dhi[RB];
 #pragma unroll
       for (int j = 0; j < RB; j++) {
-        dlo[j] = sum2(alo[j]) + sum2(blo[j]);
-        dhi[j] = sum2(ahi[j]) + sum2(bhi[j]);
-      }
-#pragma unroll
-      for (int j = 0; j < RB; j++) {
+        const float dlo = S * ((float)l0[j] * 65536.f + (float)l1[j] * 256.f + (float)l2[j]);
+        const float dhi = S * 0.0625f * ((float)h0[j] * 65536.f + (float)h1[j] * 256.f + (float)h2[j]);
         const float d = h16(H[j].x), dmin = h16(H[j].x >> 16);
         int sc0, m0, sc1, m1;
         q4k_sm(2 * g, H[j].y, H[j].z, H[j].w, sc0, m0);
         q4k_sm(2 * g + 1, H[j].y, H[j].z, H[j].w, sc1, m1);
-        acc[i0 + j] += d * (float)sc0 * dlo[j] - dmin * (float)m0 * s_lo + d * (float)sc1 * dhi[j] - dmin * (float)m1 * s_hi;
+        acc[i0 + j] += d * (float)sc0 * dlo - dmin * (float)m0 * s_lo + d * (float)sc1 * dhi - dmin * (float)m1 * s_hi;
       }
     }
   }
   finish_rows<LPR>(acc, r0, sub, sl, nr, job);
 }
 
-// Q8_0 rows: unit = one 34-byte block (fp16 d + 32 int8) of 32 values. A signed byte at bit
-// position p (0 or 8) of a word becomes a float without a conversion instruction: the byte plus
-// 128 is placed in the mantissa of 2^23 (magic_s8) and 2^23 + 128 * 2^p subtracted, giving
-// q * 2^p exactly; bytes 2 and 3 are taken from the word shifted right by 16, and the staged
-// x (kQ8Off) carries 2^-8 for bytes 1 and 3.
+// Q8_0 rows on the integer pipe: each block's 32 int8 weights times the three byte digits of the
+// fixed-point x (dp4a, exact integer sums), combined in f32 once per block and scaled by d.
 template <int LPR>
-MB_DEV void rows_q8(const GemvJob& job, const uint8_t* wbase, const float* __restrict__ xs, int r0, int nr,
-                    int lane) {
+MB_DEV void rows_q8_int(const GemvJob& job, const uint8_t* wbase, const float* __restrict__ xs, int r0, int nr,
+                        int lane) {
   constexpr int NSUB = 32 / LPR, RPL = kRowsPerWarp / NSUB, RB = RPL < 4 ? RPL : 4;
   const int sub = lane / LPR, sl = lane % LPR;
   const int U = job.n_cols / 32;
-  const uint64_t M8 = pkf(8388608.f + 128.f, 8388608.f + 32768.f);
+  const float S = xs[kScaleOff];
   float acc[RPL];
 #pragma unroll
   for (int i = 0; i < RPL; i++) acc[i] = 0.f;
   for (int u = sl; u < U; u += LPR) {
-    uint64_t x2[16];
+    uint4 xd[8];
 #pragma unroll
-    for (int i = 0; i < 8; i++) {
-      const float4 t = __ldg((const float4*)(xs + kQ8Off) + i * U + u);
-      x2[2 * i] = pkf(t.x, t.y);
-      x2[2 * i + 1] = pkf(t.z, t.w);
-    }
+    for (int i = 0; i < 8; i++) xd[i] = __ldg((const uint4*)(xs + kQ8IOff) + i * U + u);
 #pragma unroll
     for (int i0 = 0; i0 < RPL; i0 += RB) {
-    uint32_t wv[RB][10];
-    bool sh[RB];  // the 34-byte block starts 2 bytes into a word
+      uint32_t wv[RB][10];
+      bool sh[RB];  // the 34-byte block starts 2 bytes into a word
 #pragma unroll
-    for (int j = 0; j < RB; j++) {
-      const int rr = min(sub + (i0 + j) * NSUB, nr - 1);
-      const uint8_t* b = wbase + (int64_t)rr * job.row_bytes + u * 34;
-      const uint32_t* a4 = (const uint32_t*)((uintptr_t)b & ~(uintptr_t)3);
-      sh[j] = ((uintptr_t)b & 3) != 0;
+      for (int j = 0; j < RB; j++) {
+        const int rr = min(sub + (i0 + j) * NSUB, nr - 1);
+        const uint8_t* b = wbase + (int64_t)rr * job.row_bytes + u * 34;
+        const uint32_t* a4 = (const uint32_t*)((uintptr_t)b & ~(uintptr_t)3);
+        sh[j] = ((uintptr_t)b & 3) != 0;
 #pragma unroll
-      for (int k = 0; k < 10; k++) wv[j][k] = a4[k];
-    }
-#pragma unroll
-    for (int j = 0; j < RB; j++) {
-      const float d = sh[j] ? h16(wv[j][0] >> 16) : h16(wv[j][0]);
-      uint64_t s01 = 0ull, s23 = 0ull;
-#pragma unroll
-      for (int k = 0; k < 8; k++) {
-        const uint32_t q = sh[j] ? wv[j][k + 1] : __byte_perm(wv[j][k], wv[j][k + 1], 0x5432);
-        const uint32_t q2 = q >> 16;
-        const uint64_t v01 = sub2(pk(magic_s8(q, 0xFFu, 0x4B000080u), magic_s8(q, 0xFF00u, 0x4B008000u)), M8);
-        const uint64_t v23 = sub2(pk(magic_s8(q2, 0xFFu, 0x4B000080u), magic_s8(q2, 0xFF00u, 0x4B008000u)), M8);
-        s01 = fma2(v01, x2[2 * k], s01);
-        s23 = fma2(v23, x2[2 * k + 1], s23);
+        for (int k = 0; k < 10; k++) wv[j][k] = a4[k];
       }
-      acc[i0 + j] += d * (sum2(s01) + sum2(s23));
-    }
+#pragma unroll
+      for (int j = 0; j < RB; j++) {
+        const float d = sh[j] ? h16(wv[j][0] >> 16) : h16(wv[j][0]);
+        int a0 = 0, a1 = 0, a2 = 0;
+#pragma unroll
+        for (int k = 0; k < 8; k++) {
+          const uint32_t q = sh[j] ? wv[j][k + 1] : __byte_perm(wv[j][k], wv[j][k + 1], 0x5432);
+          a0 = dp4a_ss(q, xd[k].x, a0);
+          a1 = dp4a_su(q, xd[k].y, a1);
+          a2 = dp4a_su(q, xd[k].z, a2);
+        }
+        acc[i0 + j] += d * (S * ((float)a0 * 65536.f + (float)a1 * 256.f + (float)a2));
+      }
     }
   }
   finish_rows<LPR>(acc, r0, sub, sl, nr, job);
@@ -519,14 +495,14 @@ __global__ void __launch_bounds__(kWarps * 32, KIND == 2 ? MB_GEMV_MINB_Q4K : MB
       const int r0 = bj.y + rl;
       if constexpr (KIND == 2) {
         if ((job.n_cols / 64) % 16 == 0)
-          rows_q4k<16>(job, wb, xs, xs + kMaxLen, r0, nr, lane);
+          rows_q4k_int<16>(job, wb, xs, xs + kMaxLen, r0, nr, lane);
         else
-          rows_q4k<32>(job, wb, xs, xs + kMaxLen, r0, nr, lane);
+          rows_q4k_int<32>(job, wb, xs, xs + kMaxLen, r0, nr, lane);
       } else {
         if ((job.n_cols / 32) % 32 == 0)
-          rows_q8<32>(job, wb, xs, r0, nr, lane);
+          rows_q8_int<32>(job, wb, xs, r0, nr, lane);
         else
-          rows_q8<16>(job, wb, xs, r0, nr, lane);
+          rows_q8_int<16>(job, wb, xs, r0, nr, lane);
       }
       return;
     }
