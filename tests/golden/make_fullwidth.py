@@ -3,7 +3,7 @@
 oracle/qwen_ref.py). Everything is seeded through the oracle's C generator and quantizers, so
 the GPU tests rebuild the same GGUF bytes and inputs bit for bit on any host.
 
-    python tests/golden/make_fullwidth.py [flux_q4_k] [flux_q8_0] [qwen_q4_k] [flux_full_q4_k]
+    python tests/golden/make_fullwidth.py [flux_q4_k] [flux_q8_0] [qwen_q4_k] [flux_full_q4_k] [qwen_full_q4_k]
 
 It takes about half an hour of CPU per FLUX case (the 28-step denoise dominates).
 
@@ -22,6 +22,9 @@ flux_q4_k / flux_q8_0: FLUX.1-dev widths (hidden 3072, 24 heads x 128, MLP 12288
 flux_full_q4_k: the full FLUX.1-dev architecture (19 double + 38 single blocks) in Q4_K, seed 14,
   the same token counts and guidance; one forward (about 25 min of CPU).
   pred            float16 [4096, 64]: the model's prediction at t = T_BLOCK
+qwen_full_q4_k: the full Qwen-Image architecture (60 blocks) in Q4_K, seed 15, with the qwen_q4_k
+  inputs; one forward with the conditional prompt (about 15 min of CPU).
+  pred            float16 [4096, 64]: the prediction at t = 700
 qwen_q4_k: Qwen-Image widths (hidden 3072, 24 heads, MLP 12288, text width 3584) with 1 block,
   4096 image + 256 text tokens, conditional mask keeping the first 200 text tokens,
   unconditional mask a seeded 60 % pattern.
@@ -135,6 +138,20 @@ def make_flux_full(name):
     np.savez_compressed(os.path.join(HERE, f"fullwidth_{name}.npz"), pred=pred.astype(np.float16))
 
 
+QWEN_FULL_SEED = 15
+
+
+def make_qwen_full(name):
+    """The full-depth Qwen-Image model: one forward (decodes not cached)."""
+    cfg = Q.QwenConfig()
+    W = Q.synth_weights(cfg, seed=QWEN_FULL_SEED, qtype=oracle.GGML_Q4_K)
+    x, txt, mk, _ = qwen_inputs()
+    t0 = time.time()
+    pred = Q.forward(W, cfg, x, Q_T, txt[0], mk[0].astype(bool), HT, WT)
+    print(f"{name}: forward {time.time() - t0:.0f} s", flush=True)
+    np.savez_compressed(os.path.join(HERE, f"fullwidth_{name}.npz"), pred=pred.astype(np.float16))
+
+
 def make_qwen(name):
     cfg = qwen_config()
     W = cached(Q.synth_weights(cfg, seed=13, qtype=oracle.GGML_Q4_K))
@@ -149,10 +166,12 @@ def make_qwen(name):
 
 
 def main(argv):
-    todo = argv or list(FLUX_CASES) + ["qwen_q4_k", "flux_full_q4_k"]
+    todo = argv or list(FLUX_CASES) + ["qwen_q4_k", "flux_full_q4_k", "qwen_full_q4_k"]
     for name in todo:
         if name == "flux_full_q4_k":
             make_flux_full(name)
+        elif name == "qwen_full_q4_k":
+            make_qwen_full(name)
         else:
             (make_qwen if name.startswith("qwen") else make_flux)(name)
 

@@ -13,6 +13,9 @@ oracle needs ~30 s per full-width FLUX forward on a CPU).
     (rel-L2 <= 1e-2), and one CFG Euler step through mb_qwen_denoise (cond + uncond prompts with
     different masks, qwen_image/pipeline.rs:2655-2716): the step's update at cosine >= 0.999.
 
+  * The full-depth models (FLUX.1-dev 19 + 38 blocks, Qwen-Image 60 blocks, Q4_K) for one
+    forward each: rel-L2 < 2e-2 and cosine >= 0.999 of the prediction.
+
 Both GGUF types of the path (Q4_K and Q8_0) are covered for FLUX; Qwen uses Q4_K."""
 import dataclasses
 import os
@@ -205,6 +208,27 @@ def test_flux_full_depth_forward(cuda):
     img, ids, txt, tids, y, _ = G.flux_inputs(G.FULL_SEED)
     pred = m.forward(t(img), t(ids), t(txt), t(tids), G.T_BLOCK, t(y), G.GUIDANCE).cpu().numpy()
     ref = fixture("flux_full_q4_k")["pred"].astype(np.float32)
+    assert mb.device_status() == 0
+    err = rel_l2(pred, ref)
+    cos = float(np.dot(pred.ravel(), ref.ravel()) / np.linalg.norm(pred) / np.linalg.norm(ref))
+    assert err < 2e-2 and cos >= 0.999, (err, cos)
+
+
+def test_qwen_full_depth_forward(cuda):
+    """The whole Qwen-Image architecture (60 dual-stream blocks, Q4_K, 256 + 4096 tokens with the
+    partial text mask) through mb_qwen_forward against the oracle's forward of the same seeded
+    GGUF bytes: the prediction within rel-L2 2e-2 and cosine >= 0.999."""
+    cfg = Q.QwenConfig()
+    W = Q.synth_weights(cfg, seed=G.QWEN_FULL_SEED, qtype=oracle.GGML_Q4_K)
+    m = mb.QwenTransformer(mb.QwenConfig(**dataclasses.asdict(cfg)), max_txt=G.Q_LT, max_img=G.HT * G.WT,
+                           max_batch=1)
+    for n, qt in W.items():
+        m.set_tensor(n, mb.QTensor(qt.ggml_type, qt.shape, qt.raw))
+    del W
+    assert m.missing() == []
+    x, txt, mk, _ = G.qwen_inputs()
+    pred = m.forward(t(x[None]), G.Q_T, t(txt[:1]), t(mk[:1]), G.HT, G.WT).cpu().numpy()[0]
+    ref = fixture("qwen_full_q4_k")["pred"].astype(np.float32)
     assert mb.device_status() == 0
     err = rel_l2(pred, ref)
     cos = float(np.dot(pred.ravel(), ref.ravel()) / np.linalg.norm(pred) / np.linalg.norm(ref))
