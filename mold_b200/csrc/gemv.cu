@@ -76,15 +76,19 @@ __global__ void k_gemv_stage(Inputs ins, float* __restrict__ stage) {
     // the integer copies: S from the vector's max |x|, then the three digits of round(x / S)
     __shared__ float red[32];
     float mx = 0.f;
-    for (int i = threadIdx.x; i < in.len; i += blockDim.x) mx = fmaxf(mx, fabsf(xs[i]));
+    for (int i = threadIdx.x; i < in.len; i += blockDim.x) {
+      const float a = fabsf(xs[i]);
+      mx = a <= 3.402823466e38f ? fmaxf(mx, a) : __int_as_float(0x7f800000);  // NaN and inf count as inf
+    }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
     if (lane == 0) red[warp] = mx;
     __syncthreads();
     mx = 0.f;
     for (int w = 0; w < (int)(blockDim.x >> 5); w++) mx = fmaxf(mx, red[w]);
-    const float S = mx > 0.f ? mx / 8388607.f : 1.f;
-    const float invS = 1.f / S;
+    // a non-finite x makes S NaN, so the rows' results are NaN as a float product's would be
+    const float S = !(mx <= 3.402823466e38f) ? __int_as_float(0x7fc00000) : (mx > 0.f ? mx / 8388607.f : 1.f);
+    const float invS = S == S ? 1.f / S : 0.f;
     if (threadIdx.x == 0) xs[kScaleOff] = S;
     for (int i = threadIdx.x * 4; i < in.len; i += blockDim.x * 4) {
       uint32_t w0 = 0, w1 = 0, w2 = 0;

@@ -86,3 +86,15 @@ def test_size_limits_rejected(cuda):
                              None, 0, 0, None, None, 0, None)
     assert rc == _lib.MB_ERR_INVALID
     assert mb.device_status() == 0
+
+
+@pytest.mark.parametrize("t", [oracle.GGML_Q4_K, oracle.GGML_Q8_0])
+def test_gemv_nonfinite_input_propagates(cuda, t):
+    """The GEMV stages x as fixed point; a non-finite input must still give non-finite outputs."""
+    w, _ = qmat(oracle.randn(10, (64, 512), 0.02), t)
+    x = torch.from_numpy(oracle.randn(11, (512,))).to(cuda)
+    x[7] = float("inf")
+    y = mb.qgemv(w, x)
+    assert not torch.isfinite(y).any()
+    x[7] = float("nan")
+    assert not torch.isfinite(mb.qgemv(w, x)).any()
